@@ -848,6 +848,15 @@ B3X_API int b3x_batch_restore_gpu(B3Batch batch, const void* initial, const unsi
 B3X_API int b3x_batch_apply_gpu(B3Batch batch, int kind, int index, const float* values, int values_per_world,
     const unsigned char* active, void* stream, unsigned long long config_signature);
 
+/* Device generators of the benchmark inputs (seeded scenes of
+ * puffysics_b200/scenes/b3_scenes.h): per-step action values of world
+ * first+i (returns values per world, 0 when the scene has none, -1 on error)
+ * and the 1%-per-step reset mask of the scale-out configuration. */
+B3X_API int b3x_scene_actions_gpu(float* out, int n, int scene, unsigned long long seed, unsigned long long first,
+    unsigned long long step, void* stream);
+B3X_API int b3x_scene_reset_gpu(unsigned char* out, int n, unsigned long long seed, unsigned long long first,
+    unsigned long long step, void* stream);
+
 /* Capacity configuration helpers (host). */
 B3X_API size_t b3x_world_bytes(unsigned long long config_signature);
 B3X_API const char* b3x_version(void);

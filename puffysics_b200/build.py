@@ -1,0 +1,95 @@
+"""Build libpuffysics_b200.so (sm_100a) in-tree with nvcc.
+
+    python -m puffysics_b200.build [-v]
+
+Flags that matter for parity: -fmad=false (no fused multiply-add
+contraction), -prec-div=true / -prec-sqrt=true / -ftz=false (IEEE division,
+square root and denormals).  With them every float expression of the step
+rounds exactly like the reference's CPU build with -ffp-contract=off.
+"""
+import os
+import subprocess
+import sys
+
+PKG = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(PKG)
+LIB_DIR = os.path.join(PKG, "_lib")
+LIB = os.path.join(LIB_DIR, "libpuffysics_b200.so")
+SOURCES = [os.path.join(PKG, "csrc", "b3x_step.cu"), os.path.join(PKG, "csrc", "b3x_scenes.cu")]
+HEADERS = [os.path.join(ROOT, "include", "puffysics_b200.h"),
+           os.path.join(PKG, "csrc", "b3x_math.cuh"),
+           os.path.join(PKG, "csrc", "b3x_narrow.cuh"),
+           os.path.join(PKG, "csrc", "b3x_world.cuh"),
+           os.path.join(PKG, "scenes", "b3_scenes.h")]
+SCENES_SRC = os.path.join(PKG, "scenes", "b3_scenes_host.c")
+# capacity configurations the host scene builders are compiled for:
+# name -> (bodies, shapes, contacts, joints)
+SCENE_CONFIGS = {"hover": (2, 2, 4, 1), "stack": (9, 9, 32, 1), "chain": (12, 12, 32, 10),
+                 "pile": (37, 37, 128, 1), "hovertask": (2, 2, 4, 2), "default": (80, 128, 128, 32)}
+CC = os.environ.get("CC", "gcc")
+
+NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc" if os.path.exists("/usr/local/cuda/bin/nvcc") else "nvcc")
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+PARITY = ["-fmad=false", "-prec-div=true", "-prec-sqrt=true", "-ftz=false"]
+
+
+def nvcc_cmd(out=LIB, extra=()):
+    return ([NVCC] + ARCH + ["-lineinfo", "-O3", "-std=c++17"] + PARITY
+            + ["-Xcompiler", "-fPIC,-fvisibility=hidden", "-shared", "-cudart", "static",
+               "-I" + os.path.join(ROOT, "include"), "-I" + os.path.join(PKG, "csrc"),
+               "-I" + os.path.join(PKG, "scenes")]
+            + list(extra) + SOURCES + ["-o", out])
+
+
+def scenes_lib(name):
+    return os.path.join(LIB_DIR, "libb3scenes_%s.so" % name)
+
+
+def _newer(out, deps):
+    if not os.path.exists(out):
+        return True
+    t = os.path.getmtime(out)
+    return any(os.path.getmtime(d) > t for d in deps)
+
+
+def up_to_date():
+    deps = SOURCES + HEADERS + [__file__]
+    return not _newer(LIB, deps) and not any(_newer(scenes_lib(n), [SCENES_SRC] + HEADERS) for n in SCENE_CONFIGS)
+
+
+def build_scenes(force=False):
+    """Host scene builders, one per capacity configuration (gcc, exact float
+    expressions: -ffp-contract=off)."""
+    for name, (b, s, c, j) in SCENE_CONFIGS.items():
+        out = scenes_lib(name)
+        if not force and not _newer(out, [SCENES_SRC] + HEADERS):
+            continue
+        cmd = [CC, "-O2", "-ffp-contract=off", "-fno-fast-math", "-fPIC", "-shared", "-std=gnu11",
+               "-fvisibility=hidden", "-DB3_MAX_BODIES=%d" % b, "-DB3_MAX_SHAPES=%d" % s,
+               "-DB3_MAX_CONTACTS=%d" % c, "-DB3_MAX_JOINTS=%d" % j,
+               "-I" + os.path.join(ROOT, "include"), "-I" + os.path.join(PKG, "scenes"), SCENES_SRC, "-o", out,
+               "-lm"]
+        res = subprocess.run(cmd, capture_output=True, text=True)
+        if res.returncode != 0:
+            raise RuntimeError("scene builder build failed:\n" + " ".join(cmd) + "\n" + res.stdout + res.stderr)
+
+
+def build(force=False, verbose=False):
+    """Compile the library if any source is newer than it; returns its path."""
+    if not force and up_to_date():
+        return LIB
+    os.makedirs(LIB_DIR, exist_ok=True)
+    build_scenes(force)
+    if not force and not _newer(LIB, SOURCES + HEADERS + [__file__]):
+        return LIB
+    cmd = nvcc_cmd(extra=["-Xptxas", "-v"] if verbose else [])
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError("nvcc failed:\n" + " ".join(cmd) + "\n" + res.stdout + res.stderr)
+    if verbose:
+        sys.stdout.write(res.stdout + res.stderr)
+    return LIB
+
+
+if __name__ == "__main__":
+    print(build(force=True, verbose="-v" in sys.argv))

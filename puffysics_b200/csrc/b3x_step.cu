@@ -1,0 +1,301 @@
+// b3x_step.cu -- batched rigid-body step on B200 (sm_100a) and the exported
+// C-ABI of libpuffysics_b200.so.
+//
+// Mapping.  One thread owns one world; a 32-thread CTA owns a tile of 32
+// consecutive worlds and the grid is persistent (at most SMs x resident CTAs),
+// each CTA walking tiles with a grid stride.  The caller's worlds stay in
+// their AoS B3World layout (the drop-in contract); a step reads each world's
+// header, bodies, shapes, old contacts and joints once, keeps its working
+// state in lane-interleaved structure-of-arrays columns, and writes every
+// field the reference step writes once at the end:
+//   - body state (velocities, pose deltas, inverse mass / inertia, flags) in
+//     shared memory, [body][field][lane], so the per-world dynamic body
+//     indices of the Gauss-Seidel sweeps hit distinct banks;
+//   - shape world poses / AABBs, contacts and joints in a per-CTA workspace
+//     slot in global memory, [item][field][lane]: a warp touching item k of
+//     its 32 worlds reads one contiguous 128-byte line per field, and a slot
+//     is reused tile after tile so it stays resident in L2.
+// No thread communicates with another: there are no barriers, no waits and
+// no atomics, and every loop is bounded by the world's capacities.
+//
+// Arithmetic.  The per-world work follows the reference's default
+// b3_step (src/puffysics/09_step.inl:183-258) operation by operation; the
+// library is compiled with -fmad=false and IEEE division / square root so
+// the results equal the reference CPU build (-ffp-contract=off) bit for bit,
+// atan2f (revolute twist) excepted.  Reordering is limited to hoisting pure
+// values (shape world poses, gated inverse masses) and to evaluating the
+// side-effect-free broadphase filters in a cheaper order.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <tuple>
+
+#include "puffysics_b200.h"
+#include "b3x_world.cuh"
+
+namespace b3x {
+
+template <bool kBodySmem>
+__global__ void __launch_bounds__(kLanes) step_kernel(StepArgs a) {
+    extern __shared__ float smem[];
+    const int lane = threadIdx.x;
+    float* slot = a.scratch + (size_t)blockIdx.x * a.slot_words;
+    float* bc = (kBodySmem ? smem : slot + a.off_bodies) + lane;
+    float* sc = slot + a.off_shapes + lane;
+    float* cc = slot + a.off_contacts + lane;
+    float* jc = slot + a.off_joints + lane;
+    const int ntiles = (a.count + kLanes - 1) / kLanes;
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+        int wi = tile * kLanes + lane;
+        if (wi >= a.count) continue;
+        if (a.active && !a.active[wi]) continue;
+        unsigned char* wp = a.data + (size_t)wi * a.stride + a.offset;
+        world_step(wp, a, bc, sc, cc, jc);
+    }
+}
+
+// ---- restore, actions --------------------------------------------------------
+// One warp per world, 8-byte words, coalesced on both sides.
+__global__ void restore_kernel(unsigned char* data, unsigned long long stride, unsigned long long offset, int count,
+        const unsigned long long* initial, const unsigned char* reset, unsigned words) {
+    const int lane = threadIdx.x & 31;
+    const int warps = (int)(gridDim.x * (blockDim.x >> 5));
+    for (int wi = (int)(blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)); wi < count; wi += warps) {
+        if (reset && !reset[wi]) continue;
+        unsigned long long* dst = reinterpret_cast<unsigned long long*>(data + (size_t)wi * stride + offset);
+        const unsigned long long* src = initial + (size_t)wi * words;
+        for (unsigned w = lane; w < words; w += 32) dst[w] = src[w];
+    }
+}
+
+__global__ void apply_kernel(unsigned char* data, unsigned long long stride, unsigned long long offset, int count,
+        Layout L, int kind, int index, const float* values, int vpw, const unsigned char* active) {
+    int wi = blockIdx.x * blockDim.x + threadIdx.x;
+    if (wi >= count || (active && !active[wi])) return;
+    unsigned char* wp = data + (size_t)wi * stride + offset;
+    const Header* hd = reinterpret_cast<const Header*>(wp);
+    const float* v = values + (size_t)wi * vpw;
+    if (kind == B3X_ACTION_JOINT_TARGET) {
+        B3Joint* joints = reinterpret_cast<B3Joint*>(wp + L.joint_off);
+        int nj = clampi(hd->joint_count, 0, L.J);
+        for (int k = 0; k < vpw; k++)
+            if (index + k >= 0 && index + k < nj) joints[index + k].target_angle = b3_clamp(v[k], -B3_PI, B3_PI);
+        return;
+    }
+    B3Body* bodies = reinterpret_cast<B3Body*>(wp + B3X_WORLD_HEADER_BYTES);
+    int nb = clampi(hd->body_count, 0, L.B);
+    for (int k = 0; 3 * k + 2 < vpw; k++) {
+        int bi = index + k;
+        if (bi < 0 || bi >= nb) continue;
+        B3Body* b = &bodies[bi];
+        B3Vec3 x = b3_v(v[3 * k], v[3 * k + 1], v[3 * k + 2]);
+        if (kind == B3X_ACTION_FORCE) b->force = b3_add(b->force, x);
+        else if (kind == B3X_ACTION_TORQUE) b->torque = b3_add(b->torque, x);
+        else if (b->type == B3_DYNAMIC) b->lin_vel = b3_madd(b->lin_vel, b->inv_mass, x);
+    }
+}
+
+// ---- host side --------------------------------------------------------------
+struct Plan {
+    bool body_smem;
+    int grid_max;             // co-resident CTAs on the device
+    size_t smem_bytes;
+    unsigned long long slot_words;
+    unsigned off_bodies, off_shapes, off_contacts, off_joints;
+    size_t ws_bytes;
+};
+
+static std::mutex g_mutex;
+static std::map<std::pair<int, unsigned long long>, Plan> g_plans;
+static std::map<std::tuple<int, void*, unsigned long long>, std::pair<void*, size_t>> g_workspaces;
+
+// Body columns live in shared memory while they fit comfortably.
+static constexpr size_t kBodySmemLimit = 64 * 1024;
+
+static cudaError_t make_plan(int dev, unsigned long long sig, const Layout& L, Plan* out) {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    auto it = g_plans.find({dev, sig});
+    if (it != g_plans.end()) {
+        *out = it->second;
+        return cudaSuccess;
+    }
+    Plan p;
+    size_t body_words = (size_t)L.B * NBF * kLanes;
+    p.body_smem = body_words * 4 <= kBodySmemLimit;
+    p.smem_bytes = p.body_smem ? body_words * 4 : 0;
+    unsigned w = 0;
+    p.off_bodies = w;
+    if (!p.body_smem) w += (unsigned)body_words;
+    p.off_shapes = w;
+    w += (unsigned)((size_t)L.S * NSF * kLanes);
+    p.off_contacts = w;
+    w += (unsigned)((size_t)L.C * NCF * kLanes);
+    p.off_joints = w;
+    w += (unsigned)((size_t)L.J * NJF * kLanes);
+    w = (w + 63u) & ~63u;    // 256-byte aligned slots
+    p.slot_words = w;
+    int sms = 0;
+    cudaError_t e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
+    int occ = 0;
+    if (p.body_smem) {
+        if (p.smem_bytes > 48 * 1024) {
+            e = cudaFuncSetAttribute(step_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem_bytes);
+            if (e != cudaSuccess) return e;
+        }
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, step_kernel<true>, kLanes, p.smem_bytes);
+    } else {
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, step_kernel<false>, kLanes, 0);
+    }
+    if (e != cudaSuccess) return e;
+    if (occ < 1) occ = 1;
+    p.grid_max = sms * occ;
+    p.ws_bytes = (size_t)p.grid_max * p.slot_words * 4;
+    g_plans[{dev, sig}] = p;
+    *out = p;
+    return cudaSuccess;
+}
+
+static bool batch_ok(const B3Batch& b, size_t world_bytes) {
+    if (b.count < 0) return false;
+    if (b.count == 0) return true;
+    return b.data != nullptr && b.stride >= world_bytes && b.world_offset <= b.stride - world_bytes
+        && (size_t)b.count <= SIZE_MAX / b.stride;
+}
+
+static bool aligned8(const B3Batch& b) {
+    return (((uintptr_t)b.data + b.world_offset) % 8 == 0) && (b.stride % 8 == 0);
+}
+
+static cudaError_t launch_step(const B3Batch& batch, float dt, int substeps, const unsigned char* active,
+        cudaStream_t stream, const Layout& L, int ji, int ri, const Plan& p, void* ws, int grid_limit) {
+    StepArgs a;
+    a.data = (unsigned char*)batch.data;
+    a.stride = batch.stride;
+    a.offset = batch.world_offset;
+    a.count = batch.count;
+    a.active = active;
+    a.dt = dt;
+    a.substeps = substeps;
+    a.joint_iters = ji;
+    a.relax_iters = ri;
+    a.L = L;
+    a.scratch = (float*)ws;
+    a.slot_words = p.slot_words;
+    a.off_bodies = p.off_bodies;
+    a.off_shapes = p.off_shapes;
+    a.off_contacts = p.off_contacts;
+    a.off_joints = p.off_joints;
+    int ntiles = (batch.count + kLanes - 1) / kLanes;
+    int grid = ntiles < grid_limit ? ntiles : grid_limit;
+    if (p.body_smem) step_kernel<true><<<grid, kLanes, p.smem_bytes, stream>>>(a);
+    else step_kernel<false><<<grid, kLanes, 0, stream>>>(a);
+    return cudaGetLastError();
+}
+
+}  // namespace b3x
+
+using namespace b3x;
+
+extern "C" {
+
+B3X_API const char* b3x_version(void) { return "puffysics_b200 0.1 (sm_100a)"; }
+
+B3X_API size_t b3x_world_bytes(unsigned long long sig) {
+    Layout L;
+    return layout_from_signature(sig, &L) ? L.size : 0;
+}
+
+B3X_API size_t b3x_workspace_bytes(unsigned long long sig, int device) {
+    Layout L;
+    if (!layout_from_signature(sig, &L)) return 0;
+    Plan p;
+    if (make_plan(device, sig, L, &p) != cudaSuccess) return 0;
+    return p.ws_bytes;
+}
+
+static int step_common(B3Batch batch, float dt, int substeps, const unsigned char* active, void* stream,
+        unsigned long long sig, int ji, int ri, void* ws, size_t ws_bytes, bool own_ws) {
+    Layout L;
+    if (!layout_from_signature(sig, &L)) return cudaErrorInvalidValue;
+    if (!batch_ok(batch, L.size) || !std::isfinite(dt) || dt < 0 || substeps < 1 || ji < 1 || ri < 1)
+        return cudaErrorInvalidValue;
+    if (batch.count == 0 || dt == 0) return cudaSuccess;
+    if (!aligned8(batch)) return cudaErrorInvalidValue;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    Plan p;
+    e = make_plan(dev, sig, L, &p);
+    if (e != cudaSuccess) return e;
+    if (own_ws) {
+        std::lock_guard<std::mutex> lock(g_mutex);
+        auto key = std::make_tuple(dev, stream, sig);
+        auto it = g_workspaces.find(key);
+        if (it == g_workspaces.end()) {
+            void* mem = nullptr;
+            e = cudaMalloc(&mem, p.ws_bytes);
+            if (e != cudaSuccess) return e;
+            g_workspaces[key] = {mem, p.ws_bytes};
+            ws = mem;
+        } else {
+            ws = it->second.first;
+        }
+        ws_bytes = p.ws_bytes;
+    }
+    if (ws == nullptr || ((uintptr_t)ws % 256) != 0) return cudaErrorInvalidValue;
+    // A smaller caller workspace simply runs fewer persistent CTAs.
+    long long slots = (long long)(ws_bytes / (p.slot_words * 4));
+    if (slots < 1) return cudaErrorInvalidValue;
+    int grid_limit = (int)(slots < p.grid_max ? slots : p.grid_max);
+    return launch_step(batch, dt, substeps, active, (cudaStream_t)stream, L, ji, ri, p, ws, grid_limit);
+}
+
+B3X_API int b3x_batch_step_gpu(B3Batch batch, float dt, int substeps, const unsigned char* active, void* stream,
+        unsigned long long sig, int ji, int ri) {
+    return step_common(batch, dt, substeps, active, stream, sig, ji, ri, nullptr, 0, true);
+}
+
+B3X_API int b3x_batch_step_gpu_ws(B3Batch batch, float dt, int substeps, const unsigned char* active, void* stream,
+        unsigned long long sig, int ji, int ri, void* ws, size_t ws_bytes) {
+    return step_common(batch, dt, substeps, active, stream, sig, ji, ri, ws, ws_bytes, false);
+}
+
+B3X_API int b3x_batch_restore_gpu(B3Batch batch, const void* initial, const unsigned char* reset, void* stream,
+        unsigned long long sig) {
+    Layout L;
+    if (!layout_from_signature(sig, &L)) return cudaErrorInvalidValue;
+    if (!batch_ok(batch, L.size) || (batch.count && !initial)) return cudaErrorInvalidValue;
+    if (!batch.count) return cudaSuccess;
+    if (!aligned8(batch) || ((uintptr_t)initial % 8) != 0) return cudaErrorInvalidValue;
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    int warps_needed = batch.count;
+    int blocks = (warps_needed + 7) / 8;
+    int cap = sms * 16;
+    if (blocks > cap) blocks = cap;
+    restore_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>((unsigned char*)batch.data, batch.stride,
+        batch.world_offset, batch.count, (const unsigned long long*)initial, reset, L.size / 8);
+    return cudaGetLastError();
+}
+
+B3X_API int b3x_batch_apply_gpu(B3Batch batch, int kind, int index, const float* values, int vpw,
+        const unsigned char* active, void* stream, unsigned long long sig) {
+    Layout L;
+    if (!layout_from_signature(sig, &L)) return cudaErrorInvalidValue;
+    if (!batch_ok(batch, L.size) || kind < 0 || kind > 3 || vpw < 1 || (batch.count && !values))
+        return cudaErrorInvalidValue;
+    if (kind != B3X_ACTION_JOINT_TARGET && vpw % 3 != 0) return cudaErrorInvalidValue;
+    if (!batch.count) return cudaSuccess;
+    if (!aligned8(batch)) return cudaErrorInvalidValue;
+    int blocks = (batch.count + 127) / 128;
+    apply_kernel<<<blocks, 128, 0, (cudaStream_t)stream>>>((unsigned char*)batch.data, batch.stride,
+        batch.world_offset, batch.count, L, kind, index, values, vpw, active);
+    return cudaGetLastError();
+}
+
+}  // extern "C"

@@ -1,0 +1,113 @@
+"""Host-side mirror of the C-ABI (include/puffysics_b200.h) over ctypes.
+
+Names, argument meaning and return codes follow the reference batch API
+(reference b3_batch.cuh:12-99): functions return cudaError_t codes
+(0 = success, 1 = cudaErrorInvalidValue) and never raise for invalid
+arguments; nothing is launched or written when they return 1.
+
+Worlds are torch uint8 tensors on a CUDA device of shape (count, stride);
+torch is used only for device memory and streams.  There is no CPU path:
+loading fails loudly if libpuffysics_b200.so is missing.
+"""
+import ctypes
+import os
+
+from . import layout
+
+_PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_PKG, "_lib", "libpuffysics_b200.so")
+
+CUDA_SUCCESS = 0
+CUDA_ERROR_INVALID_VALUE = 1
+
+ACTION_FORCE, ACTION_TORQUE, ACTION_LINEAR_IMPULSE, ACTION_JOINT_TARGET = 0, 1, 2, 3
+
+
+class B3Batch(ctypes.Structure):
+    _fields_ = [("data", ctypes.c_void_p), ("stride", ctypes.c_size_t), ("world_offset", ctypes.c_size_t),
+                ("count", ctypes.c_int)]
+
+
+_lib = None
+
+
+def lib():
+    """The loaded C-ABI library (raises if it has not been built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError("libpuffysics_b200.so is not built (%s); run python -m puffysics_b200.build"
+                               % LIB_PATH)
+        L = ctypes.CDLL(LIB_PATH)
+        vp, u8p = ctypes.c_void_p, ctypes.c_void_p
+        L.b3x_batch_step_gpu.argtypes = [B3Batch, ctypes.c_float, ctypes.c_int, u8p, vp, ctypes.c_ulonglong,
+                                         ctypes.c_int, ctypes.c_int]
+        L.b3x_batch_step_gpu.restype = ctypes.c_int
+        L.b3x_batch_step_gpu_ws.argtypes = [B3Batch, ctypes.c_float, ctypes.c_int, u8p, vp, ctypes.c_ulonglong,
+                                            ctypes.c_int, ctypes.c_int, vp, ctypes.c_size_t]
+        L.b3x_batch_step_gpu_ws.restype = ctypes.c_int
+        L.b3x_workspace_bytes.argtypes = [ctypes.c_ulonglong, ctypes.c_int]
+        L.b3x_workspace_bytes.restype = ctypes.c_size_t
+        L.b3x_batch_restore_gpu.argtypes = [B3Batch, vp, u8p, vp, ctypes.c_ulonglong]
+        L.b3x_batch_restore_gpu.restype = ctypes.c_int
+        L.b3x_batch_apply_gpu.argtypes = [B3Batch, ctypes.c_int, ctypes.c_int, vp, ctypes.c_int, u8p, vp,
+                                          ctypes.c_ulonglong]
+        L.b3x_batch_apply_gpu.restype = ctypes.c_int
+        L.b3x_world_bytes.argtypes = [ctypes.c_ulonglong]
+        L.b3x_world_bytes.restype = ctypes.c_size_t
+        L.b3x_version.restype = ctypes.c_char_p
+        _lib = L
+    return _lib
+
+
+def _ptr(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(stream):
+    if stream is None:
+        import torch
+        stream = torch.cuda.current_stream()
+    return ctypes.c_void_p(stream.cuda_stream if hasattr(stream, "cuda_stream") else int(stream))
+
+
+def make_batch(worlds, stride=None, offset=0, count=None):
+    """B3Batch over a (count, stride) uint8 tensor (or raw pointer ints)."""
+    if isinstance(worlds, int) or worlds is None:
+        return B3Batch(worlds, stride or 0, offset, count or 0)
+    return B3Batch(worlds.data_ptr() if worlds.numel() else None,
+                   worlds.shape[1] if stride is None else stride, offset,
+                   worlds.shape[0] if count is None else count)
+
+
+def batch_step_gpu(worlds, dt, substeps, active=None, stream=None, caps=None, joint_iters=2, relax_iters=None,
+                   stride=None, offset=0, count=None, workspace=None):
+    """Step the selected worlds once (b3_batch_step_gpu).  Returns a cudaError_t code."""
+    sig = layout.signature(*caps)
+    relax_iters = joint_iters if relax_iters is None else relax_iters
+    b = make_batch(worlds, stride, offset, count)
+    if workspace is not None:
+        return lib().b3x_batch_step_gpu_ws(b, dt, substeps, _ptr(active), _stream(stream), sig, joint_iters,
+                                           relax_iters, _ptr(workspace), workspace.numel() * workspace.element_size())
+    return lib().b3x_batch_step_gpu(b, dt, substeps, _ptr(active), _stream(stream), sig, joint_iters, relax_iters)
+
+
+def batch_restore_gpu(worlds, initial, reset=None, stream=None, caps=None, stride=None, offset=0, count=None):
+    """Copy snapshots over the selected worlds (b3_batch_restore_gpu)."""
+    b = make_batch(worlds, stride, offset, count)
+    return lib().b3x_batch_restore_gpu(b, _ptr(initial), _ptr(reset), _stream(stream), layout.signature(*caps))
+
+
+def batch_apply_gpu(worlds, kind, index, values, active=None, stream=None, caps=None, stride=None, offset=0):
+    """Apply per-world forces / torques / impulses / joint targets (values: float32 (count, k))."""
+    b = make_batch(worlds, stride, offset)
+    return lib().b3x_batch_apply_gpu(b, kind, index, _ptr(values), values.shape[1], _ptr(active), _stream(stream),
+                                     layout.signature(*caps))
+
+
+def workspace_bytes(caps, device=0):
+    return lib().b3x_workspace_bytes(layout.signature(*caps), device)
+
+
+def world_bytes(caps):
+    return lib().b3x_world_bytes(layout.signature(*caps))
