@@ -1,0 +1,390 @@
+"""Benchmark: physics-only env-steps/s of the batched rigid-body step on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config stack]
+    python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N
+    python bench.py --impl reference        # the reference's CPU b3_batch_step
+
+A step = the scene's per-step actions applied to every world, then one
+b3_batch_step_gpu of every world (worlds x steps / s, substeps not counted,
+reference README.md:149-152).  One process per GPU; each rank owns a
+contiguous shard of independent worlds (weak scaling: the configuration's
+world count per GPU; `scaleout` keeps 1,048,576 worlds in total).  No
+collective runs inside the timed region.  Rank 0 prints one JSON line.
+
+value    device-resident: actions generated on the device, worlds resident in
+         HBM; per-step CUDA events on the launching stream, L2 flushed between
+         timed steps (outside the events), max over ranks.
+e2e      through the C-ABI with host buffers: each step copies that step's
+         actions from pinned host memory, applies them, steps, gathers one
+         observation per world and copies it back, then synchronises.
+roofline the step kernel alone, its CUDA-event duration against the
+         algorithmic bytes of a world-step (byte model in DESIGN.md).
+"""
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+from puffysics_b200.configs import CONFIGS  # noqa: E402
+
+METRIC = "physics-only env-steps/sec (worlds×steps/s) at 1/2/4/8 B200; % HBM roofline"
+UNIT = "env-steps/s"
+SEED = 1
+
+# Algorithmic bytes of one world-step, read + write, minimal SoA model:
+# dynamic body 196 B (pose+velocity 52 r / 52 w, force+torque 24 r / 24 w,
+# constants 44 r), other body 44 B, shape 84 B, contact 136 B (warm cache
+# 68 r / 68 w), joint 208 B (constants 112 r, impulses 48 r / 48 w).
+BYTES_DYN_BODY, BYTES_BODY, BYTES_SHAPE, BYTES_CONTACT, BYTES_JOINT = 196, 44, 84, 136, 208
+
+# Counted fp32 operations of one world-step of the reference's default path
+# (add/sub/mul/div/sqrt = 1 each, comparisons excluded) on these scenes,
+# measured by oracle/flops; None until counted.
+FLOPS_FILE = os.path.join(ROOT, "profiles", "flops_per_world_step.md")
+TRAFFIC_FILE_FMT = os.path.join(ROOT, "profiles", "step_kernel_%s.md")
+
+WORKLOAD = {"hover": "C1 hover (4,096 worlds/GPU)", "stack": "C2 box stack (16,384 worlds/GPU)",
+            "chain": "C3 capsule chain (16,384 worlds/GPU)", "pile": "C4 pile (65,536 worlds/GPU)",
+            "scaleout": "C5 scale-out (1,048,576 C2 worlds in total, 1% reset per step)"}
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--config", default="stack", choices=sorted(WORKLOAD))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--worlds", type=int, default=0, help="override worlds per GPU")
+    ap.add_argument("--e2e-steps", type=int, default=200)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def read_number(path, key):
+    """`key = number` from a committed profile summary, else None."""
+    try:
+        for line in open(path):
+            if line.strip().startswith(key):
+                return float(line.split("=", 1)[1].split()[0].replace(",", ""))
+    except (OSError, ValueError, IndexError):
+        pass
+    return None
+
+
+def host_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def cpu_model():
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def cpu_reference_run(cfg, steps, warmup, budget_s):
+    """Time the reference's CPU b3_batch_step (oracle/_ref) or, where it was
+    not built, its restatement (oracle/port) over all host threads.  With
+    steps=None the step count is chosen to fill about budget_s seconds on the
+    configuration's full world count; otherwise the world sample is sized."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as orc
+    kind = "reference" if orc.available(cfg.name, "ref") else "port"
+    o = orc.Oracle(cfg.name, "ref" if kind == "reference" else "port")
+    threads = host_threads()
+    # calibrate: a few steps over a small sample
+    probe = o.build(threads * 8, cfg.scene, SEED)
+    t = o.run_mt(probe, cfg.scene, SEED, 0, 1, 3, cfg.dt, cfg.substeps, threads)
+    per_world_step = max(t, 1e-6) / (3 * len(probe))
+    if steps is None:
+        worlds = min(cfg.worlds, 262144)
+        steps = int(min(2000, max(3, budget_s / (per_world_step * worlds))))
+    else:
+        worlds = int(budget_s / max(per_world_step * max(steps, 1), 1e-12))
+        worlds = max(threads, min(cfg.worlds, worlds))
+    w = o.build(worlds, cfg.scene, SEED)
+    if warmup:
+        o.run_mt(w, cfg.scene, SEED, 0, 1, warmup, cfg.dt, cfg.substeps, threads)
+    secs = o.run_mt(w, cfg.scene, SEED, 0, 1 + warmup, steps, cfg.dt, cfg.substeps, threads)
+    value = worlds * steps / secs
+    return {"value": value, "unit": UNIT, "cores": threads, "kind": kind,
+            "sample": "%d of the configuration's worlds x %d steps (after %d warm-up steps), %s, contiguous "
+                      "partitions, one pthread per host thread, %.2f s" % (worlds, steps, warmup, cpu_model(), secs)}
+
+
+class ClockSampler:
+    """NVML clocks and throttle reasons sampled every 20 ms (read only)."""
+
+    REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+               0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
+
+    def __init__(self, device):
+        self.samples, self.reasons, self.ok = [], set(), False
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(device)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:
+            self.max_mhz = None
+        self._stop = threading.Event()
+
+    def _run(self):
+        nv = self.nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                get = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                    nv.nvmlDeviceGetCurrentClocksThrottleReasons
+                r = get(self.h)
+                for bit, name in self.REASONS.items():
+                    if r & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(0.02)
+
+    def __enter__(self):
+        if self.ok:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self.ok:
+            self._stop.set()
+            self.t.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons), "samples": 0}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons - {"gpu_idle"}), "samples": len(self.samples)}
+
+
+def main():
+    args = parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    cfg = CONFIGS[args.config]
+    if args.impl == "reference":
+        if rank == 0:
+            ref = cpu_reference_run(cfg, args.steps, args.warmup, budget_s=max(30.0, args.cpu_seconds))
+            print(json.dumps({"impl": "reference", "metric": METRIC, "value": ref["value"], "unit": UNIT,
+                              "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+                              "ms_per_step": None, "higher_is_better": True, "scaling": "weak",
+                              "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                              "config": {"workload": WORKLOAD[args.config], "scene": cfg.name,
+                                         "dt": cfg.dt, "substeps": cfg.substeps,
+                                         "solver_iters": cfg.joint_iters},
+                              "cpu_baseline": ref,
+                              "e2e": {"value": ref["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
+                                      "d2h_bytes_per_step": 0}}), flush=True)
+        return
+
+    import torch
+    import torch.distributed as dist
+    from puffysics_b200 import build, engine, layout, shard, synth
+
+    build.build()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    per_gpu = args.worlds or (cfg.worlds // world if args.config == "scaleout" else cfg.worlds)
+    total = per_gpu * world
+    first = rank * per_gpu
+    caps, sig = cfg.caps, cfg.signature
+    kind, aidx, nv = cfg.action
+
+    scenes = synth.SceneLib(cfg)
+    host0 = scenes.build(per_gpu, SEED, first=first)
+    worlds = torch.from_numpy(host0).to(dev)
+    snapshots = worlds.clone() if cfg.reset_fraction else None
+    del host0
+    stream = torch.cuda.current_stream(dev)
+    vals = torch.zeros((per_gpu, max(nv, 1)), dtype=torch.float32, device=dev)
+    reset = torch.zeros(per_gpu, dtype=torch.uint8, device=dev)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)   # > 126 MB L2
+    step_no = [0]
+
+    def one_step(ev=None):
+        """Actions (+ reset) then the step, all on `stream`; returns kernels launched."""
+        step_no[0] += 1
+        s = step_no[0]
+        launches = 0
+        if cfg.reset_fraction:
+            assert synth.reset_gpu(reset, per_gpu, SEED, first, s, stream) == 0
+            assert engine.batch_restore_gpu(worlds, snapshots, reset, stream, caps) == 0
+            launches += 2
+        if nv:
+            assert synth.actions_gpu(vals, per_gpu, cfg.scene, SEED, first, s, stream) == nv
+            assert engine.batch_apply_gpu(worlds, kind, aidx, vals, None, stream, caps) == 0
+            launches += 2
+        if ev is not None:
+            ev.record(stream)
+        rc = engine.batch_step_gpu(worlds, cfg.dt, cfg.substeps, None, stream, caps, cfg.joint_iters,
+                                   cfg.relax_iters)
+        assert rc == 0, rc
+        return launches + 1
+
+    for _ in range(max(args.warmup, 3)):
+        one_step()
+    torch.cuda.synchronize(dev)
+
+    K = args.steps
+    ev0 = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    evk = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    ev1 = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    launches = 0
+    barrier()
+    torch.cuda.synchronize(dev)
+    sampler = ClockSampler(local)
+    with sampler:
+        for i in range(K):
+            flush.zero_()                      # evict L2 between timed steps (outside the events)
+            ev0[i].record(stream)
+            launches += one_step(evk[i])
+            ev1[i].record(stream)
+        torch.cuda.synchronize(dev)
+    barrier()
+    step_ms = [ev0[i].elapsed_time(ev1[i]) for i in range(K)]
+    kern_ms = [evk[i].elapsed_time(ev1[i]) for i in range(K)]
+    t_local = sum(step_ms)
+    k_local = sum(kern_ms)
+
+    # diagnostics of the final state (outside the timed region)
+    final = worlds.cpu().numpy()
+    stats = shard.world_stats(final, caps)
+    v = layout.view(final, caps)
+    nb_dyn = float((v["bodies"]["type"][:, :] == 2).sum(1).mean())
+    nbody = float(v["body_count"].mean())
+    nshape = float(v["shape_count"].mean())
+    ncont = float(v["contact_count"].mean())
+    njoint = float(v["joint_count"].mean())
+    del final, v
+
+    # e2e through the C-ABI with host buffers (pinned), synchronising per step
+    E = min(args.e2e_steps, K)
+    h_act = torch.zeros((per_gpu, max(nv, 1)), dtype=torch.float32).pin_memory()
+    h_obs = torch.zeros((per_gpu, 13), dtype=torch.float32).pin_memory()
+    d_obs = torch.zeros((per_gpu, 13), dtype=torch.float32, device=dev)
+    obs_body = aidx if kind in (0, 1, 2) else caps[0] - 1
+    obs_body = min(obs_body, int(layout.view(worlds[:1].cpu().numpy(), caps)["body_count"][0]) - 1)
+    act_src = [torch.from_numpy(scenes.actions(per_gpu, SEED, first, step_no[0] + 1 + i)).contiguous()
+               for i in range(min(E, 4))] if nv else []
+    barrier()
+    torch.cuda.synchronize(dev)
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_start.record(stream)
+    for i in range(E):
+        if nv:
+            h_act[:, :nv].copy_(act_src[i % len(act_src)])
+            vals.copy_(h_act[:, :nv], non_blocking=True)
+            assert engine.batch_apply_gpu(worlds, kind, aidx, vals, None, stream, caps) == 0
+        assert engine.batch_step_gpu(worlds, cfg.dt, cfg.substeps, None, stream, caps, cfg.joint_iters,
+                                     cfg.relax_iters) == 0
+        assert engine.batch_observe_gpu(worlds, obs_body, d_obs, stream, caps) == 0
+        h_obs.copy_(d_obs, non_blocking=True)
+        stream.synchronize()
+    e_end.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_local = e_start.elapsed_time(e_end)
+    bi = per_gpu * nv * 4
+    bo = per_gpu * 13 * 4
+
+    # reductions (after timing): max time over ranks, summed diagnostics
+    t_max, k_max, e_max = t_local, k_local, e2e_local
+    if world > 1:
+        tt = torch.tensor([t_local, k_local, e2e_local], dtype=torch.float64, device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t_max, k_max, e_max = tt.tolist()
+    tot = shard.reduce_stats(stats, device=dev)
+
+    if rank == 0:
+        value = total * K / (t_max / 1e3)
+        ms_per_step = t_max / K
+        kern_s = k_max / K / 1e3
+        bytes_world = (nb_dyn * BYTES_DYN_BODY + (nbody - nb_dyn) * BYTES_BODY + nshape * BYTES_SHAPE
+                       + ncont * BYTES_CONTACT + njoint * BYTES_JOINT)
+        alg_bytes = bytes_world * per_gpu
+        peaks = {}
+        try:
+            peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+        except (OSError, ValueError):
+            pass
+        hbm_peak = peaks.get("hbm_gbs") or 6650.0
+        achieved = alg_bytes / kern_s / 1e9
+        traffic_scene = cfg.name
+        traffic = read_number(TRAFFIC_FILE_FMT % traffic_scene, "dram_bytes_per_world_step")
+        flops_ws = read_number(FLOPS_FILE, "%s_flops_per_world_step" % cfg.name)
+        sm_max = (peaks.get("sm_max_mhz") or 1965.0)
+        fp32_peak = 148 * 128 * sm_max * 1e6 / 1e12      # one fp32 add or mul per lane per clock
+        roof = {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                "frac": achieved / hbm_peak,
+                "traffic": traffic * per_gpu if traffic else None,
+                "peak_source": "MEASURED_PEAKS.json hbm_gbs" if peaks.get("hbm_gbs") else "fallback 6650 GB/s",
+                "kernel": "b3x::step_kernel", "kernel_ms": kern_s * 1e3,
+                "algorithmic_bytes_per_launch": alg_bytes,
+                "algorithmic_bytes_per_world_step": bytes_world}
+        if flops_ws:
+            tf = flops_ws * per_gpu / kern_s / 1e12
+            roof["fp32"] = {"achieved": tf, "peak": fp32_peak, "unit": "TFLOP/s", "frac": tf / fp32_peak,
+                            "flops_per_world_step": flops_ws,
+                            "peak_note": "148 SMs x 128 fp32 lanes x 1 add-or-mul per clock at max SM clock "
+                                         "(the parity build contracts no multiply-add)"}
+        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K, "warmup": args.warmup,
+                "ms_per_step": ms_per_step, "higher_is_better": True,
+                "scaling": "strong" if args.config == "scaleout" else "weak", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic: seeded scenes (puffysics_b200/scenes/b3_scenes.h), on-device actions",
+                "config": {"workload": WORKLOAD[args.config], "scene": cfg.name, "worlds_per_gpu": per_gpu,
+                           "worlds": total, "dt": cfg.dt, "substeps": cfg.substeps,
+                           "solver_iters": cfg.joint_iters, "caps": list(caps),
+                           "l2": "flushed between timed steps (256 MiB write outside the events); world "
+                                 "array %.0f MB" % (per_gpu * layout.world_bytes(*caps) / 1e6),
+                           "parallelism": "dp%d (contiguous world shards, no per-step collective)" % world,
+                           "mean_contacts": ncont, "mean_bodies": nbody},
+                "roofline": roof,
+                "e2e": {"value": total * E / (e_max / 1e3), "unit": UNIT, "h2d_bytes_per_step": bi,
+                        "d2h_bytes_per_step": bo, "steps": E,
+                        "path": "pinned H2D actions -> b3x_batch_apply_gpu -> b3x_batch_step_gpu -> "
+                                "b3x_batch_observe_gpu -> D2H, stream synchronised every step"},
+                "gpu_launches": launches,
+                "clocks": sampler.summary(),
+                "diagnostics": {"worlds": int(tot[0]), "contacts": int(tot[1]), "overflowed_worlds": int(tot[2]),
+                                "dropped_contacts": int(tot[3])}}
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_reference_run(cfg, steps=None, warmup=2, budget_s=args.cpu_seconds)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

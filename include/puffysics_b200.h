@@ -848,6 +848,13 @@ B3X_API int b3x_batch_restore_gpu(B3Batch batch, const void* initial, const unsi
 B3X_API int b3x_batch_apply_gpu(B3Batch batch, int kind, int index, const float* values, int values_per_world,
     const unsigned char* active, void* stream, unsigned long long config_signature);
 
+/* Observation gather: out[13*i ..] = position(3), rotation(4: x y z s),
+ * lin_vel(3), ang_vel(3) of body `body` of world i (NaN when the world has
+ * fewer bodies).  What an adapter reads after b3_step (reference
+ * examples/pufferlib/puffysics_hover/hover_task.h:79-84), batched. */
+B3X_API int b3x_batch_observe_gpu(B3Batch batch, int body, float* out, void* stream,
+    unsigned long long config_signature);
+
 /* Device generators of the benchmark inputs (seeded scenes of
  * puffysics_b200/scenes/b3_scenes.h): per-step action values of world
  * first+i (returns values per world, 0 when the scene has none, -1 on error)
@@ -856,6 +863,12 @@ B3X_API int b3x_scene_actions_gpu(float* out, int n, int scene, unsigned long lo
     unsigned long long step, void* stream);
 B3X_API int b3x_scene_reset_gpu(unsigned char* out, int n, unsigned long long seed, unsigned long long first,
     unsigned long long step, void* stream);
+
+/* Nonzero if a step on the current device was abandoned because one of its
+ * bounded waits for a bulk copy into shared memory gave up (not expected;
+ * the worlds of that launch are then unspecified).  clear != 0 resets it.
+ * Synchronises the device; -1 on error. */
+B3X_API int b3x_fault_flags(int clear);
 
 /* Capacity configuration helpers (host). */
 B3X_API size_t b3x_world_bytes(unsigned long long config_signature);

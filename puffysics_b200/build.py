@@ -25,7 +25,8 @@ SCENES_SRC = os.path.join(PKG, "scenes", "b3_scenes_host.c")
 # capacity configurations the host scene builders are compiled for:
 # name -> (bodies, shapes, contacts, joints)
 SCENE_CONFIGS = {"hover": (2, 2, 4, 1), "stack": (9, 9, 32, 1), "chain": (12, 12, 32, 10),
-                 "pile": (37, 37, 128, 1), "hovertask": (2, 2, 4, 2), "default": (80, 128, 128, 32)}
+                 "pile": (37, 37, 128, 1), "hovertask": (2, 2, 4, 2), "default": (80, 128, 128, 32),
+                 "stacksmall": (9, 9, 4, 1)}
 CC = os.environ.get("CC", "gcc")
 
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc" if os.path.exists("/usr/local/cuda/bin/nvcc") else "nvcc")

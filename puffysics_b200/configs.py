@@ -46,6 +46,12 @@ CONFIGS = {
                     description="C3 chain: 10 capsules, weld + 9 revolutes (limits, springs, motors)"),
     "pile": Config("pile", SCENE_PILE, (37, 37, 128, 1), 8, 8, 1.0 / 60.0, 4, 65536, steps=240,
                    description="C4 pile: 16 boxes + 16 spheres between 4 walls"),
+    # capacity-edge variants used by the tests: default capacities (body state
+    # outside shared memory) and a contact capacity the stack overflows
+    "default": Config("default", SCENE_PILE, (80, 128, 128, 32), 2, 2, 1.0 / 60.0, 4, 1024,
+                      description="pile scene at the reference's default capacities"),
+    "stacksmall": Config("stacksmall", SCENE_STACK, (9, 9, 4, 1), 2, 2, 1.0 / 60.0, 4, 1024,
+                         description="stack scene with 4 contact slots (overflow path)"),
     "scaleout": Config("stack", SCENE_STACK, (9, 9, 32, 1), 8, 8, 1.0 / 60.0, 4, 1048576,
                        reset_fraction=0.01,
                        description="C5 scale-out: C2 worlds, 1% reset per step from snapshots"),

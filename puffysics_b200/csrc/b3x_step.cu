@@ -39,22 +39,40 @@
 
 namespace b3x {
 
+// Set (never cleared by the kernels) when a pipeline wait gave up; read with
+// b3x_fault_flags().  Not expected to happen: it would mean a bulk copy never
+// completed.
+__device__ int g_fault;
+
+// Shared memory of a CTA: the streaming stages, their mbarriers, then the
+// body columns when they live on chip.
+constexpr size_t kStageBytes = (size_t)kStages * kBufWords * kLanes * sizeof(float);
+constexpr size_t kBarBytes = 64;
+
 template <bool kBodySmem>
 __global__ void __launch_bounds__(kLanes) step_kernel(StepArgs a) {
-    extern __shared__ float smem[];
+    extern __shared__ __align__(128) unsigned char smem_raw[];
     const int lane = threadIdx.x;
     float* slot = a.scratch + (size_t)blockIdx.x * a.slot_words;
-    float* bc = (kBodySmem ? smem : slot + a.off_bodies) + lane;
+    float* bc = (kBodySmem ? reinterpret_cast<float*>(smem_raw + kStageBytes + kBarBytes) : slot + a.off_bodies)
+        + lane;
+    float* kc = slot + a.off_bconst + lane;
     float* sc = slot + a.off_shapes + lane;
     float* cc = slot + a.off_contacts + lane;
     float* jc = slot + a.off_joints + lane;
+    Pipe P;
+    P.buf = reinterpret_cast<float*>(smem_raw);
+    P.bar = reinterpret_cast<uint64_t*>(smem_raw + kStageBytes);
+    pipe_init(P);
     const int ntiles = (a.count + kLanes - 1) / kLanes;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
         int wi = tile * kLanes + lane;
-        if (wi >= a.count) continue;
-        if (a.active && !a.active[wi]) continue;
-        unsigned char* wp = a.data + (size_t)wi * a.stride + a.offset;
-        world_step(wp, a, bc, sc, cc, jc);
+        bool live = wi < a.count && (!a.active || a.active[wi]);
+        unsigned char* wp = a.data + (size_t)(live ? wi : 0) * a.stride + a.offset;
+        if (!world_step(live, wp, a, bc, kc, sc, cc, jc, P)) {
+            if (lane == 0) atomicExch(&g_fault, 1);
+            return;
+        }
     }
 }
 
@@ -99,13 +117,32 @@ __global__ void apply_kernel(unsigned char* data, unsigned long long stride, uns
     }
 }
 
+// One thread per world: position, rotation, lin_vel, ang_vel of one body.
+__global__ void observe_kernel(const unsigned char* data, unsigned long long stride, unsigned long long offset,
+        int count, int body, float* out) {
+    int wi = blockIdx.x * blockDim.x + threadIdx.x;
+    if (wi >= count) return;
+    const unsigned char* wp = data + (size_t)wi * stride + offset;
+    const Header* hd = reinterpret_cast<const Header*>(wp);
+    float* o = out + (size_t)wi * 13;
+    if (body < 0 || body >= hd->body_count) {
+        for (int k = 0; k < 13; k++) o[k] = NAN;
+        return;
+    }
+    const B3Body* b = reinterpret_cast<const B3Body*>(wp + B3X_WORLD_HEADER_BYTES) + body;
+    o[0] = b->position.x; o[1] = b->position.y; o[2] = b->position.z;
+    o[3] = b->rotation.v.x; o[4] = b->rotation.v.y; o[5] = b->rotation.v.z; o[6] = b->rotation.s;
+    o[7] = b->lin_vel.x; o[8] = b->lin_vel.y; o[9] = b->lin_vel.z;
+    o[10] = b->ang_vel.x; o[11] = b->ang_vel.y; o[12] = b->ang_vel.z;
+}
+
 // ---- host side --------------------------------------------------------------
 struct Plan {
     bool body_smem;
     int grid_max;             // co-resident CTAs on the device
     size_t smem_bytes;
     unsigned long long slot_words;
-    unsigned off_bodies, off_shapes, off_contacts, off_joints;
+    unsigned off_bodies, off_bconst, off_shapes, off_contacts, off_joints;
     size_t ws_bytes;
 };
 
@@ -126,10 +163,12 @@ static cudaError_t make_plan(int dev, unsigned long long sig, const Layout& L, P
     Plan p;
     size_t body_words = (size_t)L.B * NBF * kLanes;
     p.body_smem = body_words * 4 <= kBodySmemLimit;
-    p.smem_bytes = p.body_smem ? body_words * 4 : 0;
+    p.smem_bytes = kStageBytes + kBarBytes + (p.body_smem ? body_words * 4 : 0);
     unsigned w = 0;
     p.off_bodies = w;
     if (!p.body_smem) w += (unsigned)body_words;
+    p.off_bconst = w;
+    w += (unsigned)((size_t)L.B * NKF * kLanes);
     p.off_shapes = w;
     w += (unsigned)((size_t)L.S * NSF * kLanes);
     p.off_contacts = w;
@@ -143,13 +182,13 @@ static cudaError_t make_plan(int dev, unsigned long long sig, const Layout& L, P
     if (e != cudaSuccess) return e;
     int occ = 0;
     if (p.body_smem) {
-        if (p.smem_bytes > 48 * 1024) {
-            e = cudaFuncSetAttribute(step_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem_bytes);
-            if (e != cudaSuccess) return e;
-        }
+        e = cudaFuncSetAttribute(step_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem_bytes);
+        if (e != cudaSuccess) return e;
         e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, step_kernel<true>, kLanes, p.smem_bytes);
     } else {
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, step_kernel<false>, kLanes, 0);
+        e = cudaFuncSetAttribute(step_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem_bytes);
+        if (e != cudaSuccess) return e;
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, step_kernel<false>, kLanes, p.smem_bytes);
     }
     if (e != cudaSuccess) return e;
     if (occ < 1) occ = 1;
@@ -187,13 +226,14 @@ static cudaError_t launch_step(const B3Batch& batch, float dt, int substeps, con
     a.scratch = (float*)ws;
     a.slot_words = p.slot_words;
     a.off_bodies = p.off_bodies;
+    a.off_bconst = p.off_bconst;
     a.off_shapes = p.off_shapes;
     a.off_contacts = p.off_contacts;
     a.off_joints = p.off_joints;
     int ntiles = (batch.count + kLanes - 1) / kLanes;
     int grid = ntiles < grid_limit ? ntiles : grid_limit;
     if (p.body_smem) step_kernel<true><<<grid, kLanes, p.smem_bytes, stream>>>(a);
-    else step_kernel<false><<<grid, kLanes, 0, stream>>>(a);
+    else step_kernel<false><<<grid, kLanes, p.smem_bytes, stream>>>(a);
     return cudaGetLastError();
 }
 
@@ -295,6 +335,29 @@ B3X_API int b3x_batch_apply_gpu(B3Batch batch, int kind, int index, const float*
     int blocks = (batch.count + 127) / 128;
     apply_kernel<<<blocks, 128, 0, (cudaStream_t)stream>>>((unsigned char*)batch.data, batch.stride,
         batch.world_offset, batch.count, L, kind, index, values, vpw, active);
+    return cudaGetLastError();
+}
+
+// Nonzero if a step kernel on the current device ever abandoned a step
+// because a pipeline wait gave up; `clear` resets the flag.  Synchronises.
+B3X_API int b3x_fault_flags(int clear) {
+    int v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_fault, sizeof(int)) != cudaSuccess) return -1;
+    if (clear) {
+        int z = 0;
+        cudaMemcpyToSymbol(g_fault, &z, sizeof(int));
+    }
+    return v;
+}
+
+B3X_API int b3x_batch_observe_gpu(B3Batch batch, int body, float* out, void* stream, unsigned long long sig) {
+    Layout L;
+    if (!layout_from_signature(sig, &L)) return cudaErrorInvalidValue;
+    if (!batch_ok(batch, L.size) || body < 0 || body >= L.B || (batch.count && !out)) return cudaErrorInvalidValue;
+    if (!batch.count) return cudaSuccess;
+    if (!aligned8(batch)) return cudaErrorInvalidValue;
+    observe_kernel<<<(batch.count + 127) / 128, 128, 0, (cudaStream_t)stream>>>((const unsigned char*)batch.data,
+        batch.stride, batch.world_offset, batch.count, body, out);
     return cudaGetLastError();
 }
 

@@ -53,6 +53,8 @@ def lib():
         L.b3x_batch_apply_gpu.argtypes = [B3Batch, ctypes.c_int, ctypes.c_int, vp, ctypes.c_int, u8p, vp,
                                           ctypes.c_ulonglong]
         L.b3x_batch_apply_gpu.restype = ctypes.c_int
+        L.b3x_batch_observe_gpu.argtypes = [B3Batch, ctypes.c_int, vp, vp, ctypes.c_ulonglong]
+        L.b3x_batch_observe_gpu.restype = ctypes.c_int
         L.b3x_world_bytes.argtypes = [ctypes.c_ulonglong]
         L.b3x_world_bytes.restype = ctypes.c_size_t
         L.b3x_version.restype = ctypes.c_char_p
@@ -103,6 +105,12 @@ def batch_apply_gpu(worlds, kind, index, values, active=None, stream=None, caps=
     b = make_batch(worlds, stride, offset)
     return lib().b3x_batch_apply_gpu(b, kind, index, _ptr(values), values.shape[1], _ptr(active), _stream(stream),
                                      layout.signature(*caps))
+
+
+def batch_observe_gpu(worlds, body, out, stream=None, caps=None, stride=None, offset=0):
+    """Gather position/rotation/lin_vel/ang_vel (13 floats) of one body per world."""
+    b = make_batch(worlds, stride, offset)
+    return lib().b3x_batch_observe_gpu(b, body, _ptr(out), _stream(stream), layout.signature(*caps))
 
 
 def workspace_bytes(caps, device=0):
