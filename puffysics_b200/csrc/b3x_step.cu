@@ -181,15 +181,21 @@ static cudaError_t make_plan(int dev, unsigned long long sig, const Layout& L, P
     cudaError_t e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess) return e;
     int occ = 0;
-    if (p.body_smem) {
-        e = cudaFuncSetAttribute(step_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem_bytes);
-        if (e != cudaSuccess) return e;
+    // The dynamic shared memory cap is a property of the kernel function, not
+    // of a plan: raise it once to the device's opt-in maximum so plans of
+    // different capacity configurations never lower it under one another.
+    int optin = 0;
+    e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (e != cudaSuccess) return e;
+    if (p.smem_bytes > (size_t)optin) return cudaErrorInvalidValue;
+    e = cudaFuncSetAttribute(step_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, optin);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(step_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, optin);
+    if (e != cudaSuccess) return e;
+    if (p.body_smem)
         e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, step_kernel<true>, kLanes, p.smem_bytes);
-    } else {
-        e = cudaFuncSetAttribute(step_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem_bytes);
-        if (e != cudaSuccess) return e;
+    else
         e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, step_kernel<false>, kLanes, p.smem_bytes);
-    }
     if (e != cudaSuccess) return e;
     if (occ < 1) occ = 1;
     p.grid_max = sms * occ;
