@@ -823,6 +823,19 @@ B3X_API int b3x_batch_step_gpu_ws(B3Batch batch, float dt, int substeps, const u
     void* stream, unsigned long long config_signature, int joint_iters, int relax_iters,
     void* workspace, size_t workspace_bytes);
 
+/* No counterpart in the reference.  The step of b3x_batch_step_gpu for
+ * callers that cannot allocate device memory when they step (memory owned by
+ * a framework allocator or plugin host that forbids cudaMalloc, real-time
+ * loops that cannot risk an allocation's synchronisation): the workspace is a
+ * fixed 64 MiB array inside the library, reserved on every device that loads
+ * it.  Calls nothing that allocates.  The first call on a device resolves the
+ * array's device address (make it before any stream capture).  All calls on a
+ * device share the array: calls that overlap on the GPU race.  Capacity
+ * configurations needing a workspace slot above 64 MiB return
+ * cudaErrorInvalidValue; batch size is not limited. */
+B3X_API int b3x_batch_step_gpu_noalloc(B3Batch batch, float dt, int substeps, const unsigned char* active,
+    void* stream, unsigned long long config_signature, int joint_iters, int relax_iters);
+
 /* Bytes of workspace a step needs on `device` for this capacity configuration
  * (independent of the batch size); 0 if the configuration is invalid. */
 B3X_API size_t b3x_workspace_bytes(unsigned long long config_signature, int device);

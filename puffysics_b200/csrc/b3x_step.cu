@@ -367,4 +367,60 @@ B3X_API int b3x_batch_observe_gpu(B3Batch batch, int body, float* out, void* str
     return cudaGetLastError();
 }
 
+// ---- allocation-free variant ---------------------------------------------------
+// Some callers cannot allocate device memory at the moment they step: code
+// whose device memory is entirely owned by a framework's caching allocator or
+// a plugin host that forbids raw cudaMalloc, and real-time loops that cannot
+// afford the implicit synchronisation an allocation may bring.  For them,
+// b3x_batch_step_gpu_noalloc takes its workspace from this fixed array,
+// reserved on every device that loads the library until the process exits.
+constexpr size_t kNoAllocScratchBytes = 64ull << 20;   // 64 MiB per device
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+static std::mutex g_noalloc_mutex;
+static std::map<int, void*> g_noalloc_ptr;   // device -> address of g_noalloc_scratch there
+
 }  // extern "C"
+
+extern "C" {
+
+// Same step as b3x_batch_step_gpu with the workspace taken from the fixed
+// 64 MiB array above; it calls no cudaMalloc, cudaFree or other allocating
+// routine.  The first call on a device looks up the array's device address
+// (cudaGetSymbolAddress, with that device current) and caches it; make that
+// first call before any stream capture.  Every call on a device shares the
+// array, and its contents are left over from the previous call (the step
+// writes every word of it that it reads, so nothing needs clearing); calls
+// whose launches overlap on the GPU (different streams, no ordering between
+// them) race on it and must not be issued.  A capacity configuration whose
+// per-CTA workspace slot exceeds 64 MiB is rejected with
+// cudaErrorInvalidValue; smaller ones run as many persistent CTAs as slots fit
+// (at most the device's resident CTAs), so any batch size is accepted.
+B3X_API int b3x_batch_step_gpu_noalloc(B3Batch batch, float dt, int substeps, const unsigned char* active,
+        void* stream, unsigned long long sig, int ji, int ri) {
+    Layout L;
+    if (!layout_from_signature(sig, &L)) return cudaErrorInvalidValue;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    void* ptr = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+        auto it = g_noalloc_ptr.find(dev);
+        if (it == g_noalloc_ptr.end()) {
+            e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+            if (e != cudaSuccess) return e;
+            g_noalloc_ptr[dev] = ptr;
+        } else {
+            ptr = it->second;
+        }
+    }
+    Plan p;
+    e = make_plan(dev, sig, L, &p);
+    if (e != cudaSuccess) return e;
+    if (p.slot_words * 4 > kNoAllocScratchBytes) return cudaErrorInvalidValue;
+    return step_common(batch, dt, substeps, active, stream, sig, ji, ri, ptr, kNoAllocScratchBytes, false);
+}
+
+}  // extern "C"
+

@@ -46,6 +46,9 @@ def lib():
         L.b3x_batch_step_gpu_ws.argtypes = [B3Batch, ctypes.c_float, ctypes.c_int, u8p, vp, ctypes.c_ulonglong,
                                             ctypes.c_int, ctypes.c_int, vp, ctypes.c_size_t]
         L.b3x_batch_step_gpu_ws.restype = ctypes.c_int
+        L.b3x_batch_step_gpu_noalloc.argtypes = [B3Batch, ctypes.c_float, ctypes.c_int, u8p, vp,
+                                                 ctypes.c_ulonglong, ctypes.c_int, ctypes.c_int]
+        L.b3x_batch_step_gpu_noalloc.restype = ctypes.c_int
         L.b3x_workspace_bytes.argtypes = [ctypes.c_ulonglong, ctypes.c_int]
         L.b3x_workspace_bytes.restype = ctypes.c_size_t
         L.b3x_batch_restore_gpu.argtypes = [B3Batch, vp, u8p, vp, ctypes.c_ulonglong]
