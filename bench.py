@@ -17,8 +17,9 @@ value    device-resident: actions generated on the device, worlds resident in
 e2e      through the C-ABI with host buffers: each step copies that step's
          actions from pinned host memory, applies them, steps, gathers one
          observation per world and copies it back, then synchronises.
-roofline the step kernel alone, its CUDA-event duration against the
-         algorithmic bytes of a world-step (byte model in DESIGN.md).
+roofline the step's kernels alone (collide, solve, write-back), their
+         CUDA-event duration against the algorithmic bytes of a world-step
+         (byte model in DESIGN.md).
 """
 import argparse
 import json
@@ -232,6 +233,7 @@ def main():
     reset = torch.zeros(per_gpu, dtype=torch.uint8, device=dev)
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)   # > 126 MB L2
     step_no = [0]
+    step_launches = engine.step_launches(caps, per_gpu, local)
 
     def one_step(ev=None):
         """Actions (+ reset) then the step, all on `stream`; returns kernels launched."""
@@ -251,7 +253,7 @@ def main():
         rc = engine.batch_step_gpu(worlds, cfg.dt, cfg.substeps, None, stream, caps, cfg.joint_iters,
                                    cfg.relax_iters)
         assert rc == 0, rc
-        return launches + 1
+        return launches + step_launches
 
     for _ in range(max(args.warmup, 3)):
         one_step()
@@ -349,7 +351,8 @@ def main():
                 "frac": achieved / hbm_peak,
                 "traffic": traffic * per_gpu if traffic else None,
                 "peak_source": "MEASURED_PEAKS.json hbm_gbs" if peaks.get("hbm_gbs") else "fallback 6650 GB/s",
-                "kernel": "b3x::step_kernel", "kernel_ms": kern_s * 1e3,
+                "kernel": "the step: b3x::collide_kernel + b3x::solve_kernel + b3x::out_kernel per chunk "
+                          "(%d launches)" % step_launches, "kernel_ms": kern_s * 1e3,
                 "algorithmic_bytes_per_launch": alg_bytes,
                 "algorithmic_bytes_per_world_step": bytes_world}
         if flops_ws:

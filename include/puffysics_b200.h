@@ -840,6 +840,12 @@ B3X_API int b3x_batch_step_gpu_noalloc(B3Batch batch, float dt, int substeps, co
  * (independent of the batch size); 0 if the configuration is invalid. */
 B3X_API size_t b3x_workspace_bytes(unsigned long long config_signature, int device);
 
+/* No counterpart in the reference.  Number of kernel launches one
+ * b3x_batch_step_gpu call of `count` worlds makes on `device` with its own
+ * workspace (three per chunk of resident tiles); 0 if the configuration is
+ * invalid.  For launch accounting by callers and benchmarks. */
+B3X_API int b3x_step_launches(unsigned long long config_signature, int count, int device);
+
 /* Replaces b3_batch_restore_gpu (reference b3_batch.cuh:91-99): copy
  * initial[i] (contiguous snapshots of sizeof(B3World) bytes) over world i for
  * every world selected by `reset` (NULL = all).  Never allocates. */

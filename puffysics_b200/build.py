@@ -19,7 +19,9 @@ SOURCES = [os.path.join(PKG, "csrc", "b3x_step.cu"), os.path.join(PKG, "csrc", "
 HEADERS = [os.path.join(ROOT, "include", "puffysics_b200.h"),
            os.path.join(PKG, "csrc", "b3x_math.cuh"),
            os.path.join(PKG, "csrc", "b3x_narrow.cuh"),
-           os.path.join(PKG, "csrc", "b3x_world.cuh"),
+           os.path.join(PKG, "csrc", "b3x_layout.cuh"),
+           os.path.join(PKG, "csrc", "b3x_solver.cuh"),
+           os.path.join(PKG, "csrc", "b3x_phases.cuh"),
            os.path.join(PKG, "scenes", "b3_scenes.h")]
 SCENES_SRC = os.path.join(PKG, "scenes", "b3_scenes_host.c")
 # capacity configurations the host scene builders are compiled for:

@@ -35,14 +35,42 @@ B3X_HDI void m_clear(Mani& m) {
     m.normal = b3_v(0.0f, 1.0f, 0.0f);
 }
 
-B3X_HDI void m_push(Mani& m, B3Vec3 pa, B3Vec3 pb, float sep, uint32_t f) {
-    if (m.count >= B3_MAX_MANIFOLD) return;
-    int i = m.count++;
+// Append a point (dropped when the manifold is full).  The slot is selected
+// with constant indices so the manifold stays in registers.
+B3X_HDI void m_put(Mani& m, int i, B3Vec3 pa, B3Vec3 pb, float sep, uint32_t f) {
     m.pa[i] = pa;
     m.pb[i] = pb;
     m.sep[i] = sep;
     m.feat[i] = f;
 }
+B3X_HDI void m_push(Mani& m, B3Vec3 pa, B3Vec3 pb, float sep, uint32_t f) {
+    switch (m.count) {
+    case 0: m_put(m, 0, pa, pb, sep, f); break;
+    case 1: m_put(m, 1, pa, pb, sep, f); break;
+    case 2: m_put(m, 2, pa, pb, sep, f); break;
+    case 3: m_put(m, 3, pa, pb, sep, f); break;
+    default: return;
+    }
+    m.count++;
+}
+
+// Clip polygon scratch: vertex v, component c at base[(3 * v + c) * stride]
+// (shared memory, interleaved across the threads of a block).  Two polygons
+// of up to 8 vertices each.
+struct Poly {
+    float* base;
+    int stride;
+    B3X_HDI B3Vec3 get(int v) const {
+        return b3_v(base[(3 * v) * stride], base[(3 * v + 1) * stride], base[(3 * v + 2) * stride]);
+    }
+    B3X_HDI void put(int v, B3Vec3 p) const {
+        base[(3 * v) * stride] = p.x;
+        base[(3 * v + 1) * stride] = p.y;
+        base[(3 * v + 2) * stride] = p.z;
+    }
+    B3X_HDI Poly second() const { Poly q; q.base = base + 24 * stride; q.stride = stride; return q; }
+};
+static_assert(B3_MAX_MANIFOLD == 4, "manifold slots");
 
 B3X_HDI float rsq(float x) { return 1.0f / sqrtf(x); }
 
@@ -184,6 +212,8 @@ struct Obb {
 };
 
 B3X_HDI float hcomp(B3Vec3 h, int i) { return i == 0 ? h.x : (i == 1 ? h.y : h.z); }
+// axis i of a box, selected without dynamic indexing
+B3X_HDI B3Vec3 oax(const Obb& o, int i) { return i == 0 ? o.ax[0] : (i == 1 ? o.ax[1] : o.ax[2]); }
 
 // 05_collision.inl:195-201
 B3X_HDI B3Vec3 obb_support(const Obb& o, B3Vec3 dir) {
@@ -230,21 +260,21 @@ B3X_HDI bool sat_edge(float e, float ra, float rb, B3Vec3 cr, float& best, B3Vec
 
 // Sutherland-Hodgman step against one plane, at most 8 output vertices
 // (05_collision.inl:203-228).
-B3X_HD int clip_against(const B3Vec3* in, int n, B3Vec3* out, B3Vec3 pn, float po) {
+B3X_HD int clip_against(const Poly& in, int n, const Poly& out, B3Vec3 pn, float po) {
     if (n <= 0) return 0;
     int c = 0;
-    B3Vec3 prev = in[n - 1];
+    B3Vec3 prev = in.get(n - 1);
     float pd = b3_dot(prev, pn) - po;
     int pin = pd <= 0.0f;
     for (int i = 0; i < n; i++) {
-        B3Vec3 cur = in[i];
+        B3Vec3 cur = in.get(i);
         float cd = b3_dot(cur, pn) - po;
         int cin = cd <= 0.0f;
         if (cin != pin && c < 8) {
             float t = pd / (pd - cd);
-            out[c++] = b3_madd(prev, t, b3_sub(cur, prev));
+            out.put(c++, b3_madd(prev, t, b3_sub(cur, prev)));
         }
-        if (cin && c < 8) out[c++] = cur;
+        if (cin && c < 8) out.put(c++, cur);
         prev = cur;
         pd = cd;
         pin = cin;
@@ -253,7 +283,7 @@ B3X_HD int clip_against(const B3Vec3* in, int n, B3Vec3* out, B3Vec3 pn, float p
 }
 
 // Separating-axis box-box with reference-face clipping (05_collision.inl:295-461).
-B3X_HD void box_box(Mani& m, const Obb& a, const Obb& b) {
+B3X_HD void box_box(Mani& m, const Obb& a, const Obb& b, const Poly& P) {
     m_clear(m);
     B3Vec3 d = b3_sub(b.c, a.c);
     float t0 = b3_dot(d, a.ax[0]), t1 = b3_dot(d, a.ax[1]), t2 = b3_dot(d, a.ax[2]);
@@ -301,37 +331,40 @@ B3X_HD void box_box(Mani& m, const Obb& a, const Obb& b) {
         support_pair(m, a, b, n, f);
         return;
     }
-    const Obb& ref = f < 3 ? a : b;
-    const Obb& inc = f < 3 ? b : a;
+    const Obb ref = f < 3 ? a : b;
+    const Obb inc = f < 3 ? b : a;
     int rax = f < 3 ? f : f - 3;
-    float rd = b3_dot(ref.ax[rax], n);
+    float rd = b3_dot(oax(ref, rax), n);
     float rsign = (f < 3 ? rd < 0.0f : rd > 0.0f) ? -1.0f : 1.0f;
-    B3Vec3 rn = b3_mul(ref.ax[rax], rsign);
+    B3Vec3 rn = b3_mul(oax(ref, rax), rsign);
     // incident face: the face of inc most anti-parallel to rn (05_collision.inl:243-251, 422-426)
     float b0 = fabsf(b3_dot(inc.ax[0], rn)), b1 = fabsf(b3_dot(inc.ax[1], rn)), b2 = fabsf(b3_dot(inc.ax[2], rn));
     int iax = (b0 >= b1 && b0 >= b2) ? 0 : (b1 >= b2 ? 1 : 2);
-    float isign = b3_dot(inc.ax[iax], rn) > 0.0f ? -1.0f : 1.0f;
-    B3Vec3 poly[8], tmp[8];
+    float isign = b3_dot(oax(inc, iax), rn) > 0.0f ? -1.0f : 1.0f;
+    // the polygon alternates between the two scratch buffers
+    Poly cur = P, nxt = P.second();
     {
         int ta = (iax + 1) % 3, tb = (iax + 2) % 3;
-        B3Vec3 c = b3_madd(inc.c, isign * hcomp(inc.h, iax), inc.ax[iax]);
-        B3Vec3 ea = b3_mul(inc.ax[ta], hcomp(inc.h, ta));
-        B3Vec3 eb = b3_mul(inc.ax[tb], hcomp(inc.h, tb));
-        poly[0] = b3_sub(b3_sub(c, ea), eb);
-        poly[1] = b3_add(b3_sub(c, ea), eb);
-        poly[2] = b3_add(b3_add(c, ea), eb);
-        poly[3] = b3_sub(b3_add(c, ea), eb);
+        B3Vec3 c = b3_madd(inc.c, isign * hcomp(inc.h, iax), oax(inc, iax));
+        B3Vec3 ea = b3_mul(oax(inc, ta), hcomp(inc.h, ta));
+        B3Vec3 eb = b3_mul(oax(inc, tb), hcomp(inc.h, tb));
+        cur.put(0, b3_sub(b3_sub(c, ea), eb));
+        cur.put(1, b3_add(b3_sub(c, ea), eb));
+        cur.put(2, b3_add(b3_add(c, ea), eb));
+        cur.put(3, b3_sub(b3_add(c, ea), eb));
     }
     int count = 4;
     int ta = (rax + 1) % 3, tb = (rax + 2) % 3;
-    B3Vec3 face_c = b3_madd(ref.c, rsign * hcomp(ref.h, rax), ref.ax[rax]);
+    B3Vec3 face_c = b3_madd(ref.c, rsign * hcomp(ref.h, rax), oax(ref, rax));
     for (int i = 0; i < 4; i++) {
         int t = i < 2 ? ta : tb;
         float s = (i & 1) ? 1.0f : -1.0f;
-        B3Vec3 cn = b3_mul(ref.ax[t], s);
+        B3Vec3 cn = b3_mul(oax(ref, t), s);
         float co = b3_dot(cn, ref.c) + hcomp(ref.h, t);
-        count = clip_against(poly, count, tmp, cn, co);
-        for (int k = 0; k < count; k++) poly[k] = tmp[k];
+        count = clip_against(cur, count, nxt, cn, co);
+        Poly sw = cur;
+        cur = nxt;
+        nxt = sw;
         if (count == 0) {
             support_pair(m, a, b, n, f);
             return;
@@ -339,11 +372,12 @@ B3X_HD void box_box(Mani& m, const Obb& a, const Obb& b) {
     }
     float ro = b3_dot(rn, face_c);
     for (int i = 0; i < count && m.count < B3_MAX_MANIFOLD; i++) {
-        float ps = b3_dot(poly[i], rn) - ro;
+        B3Vec3 pi = cur.get(i);
+        float ps = b3_dot(pi, rn) - ro;
         if (ps <= B3_SPECULATIVE) {
-            B3Vec3 on_ref = b3_msub(poly[i], ps, rn);
-            B3Vec3 pa = f < 3 ? on_ref : poly[i];
-            B3Vec3 pb = f < 3 ? poly[i] : on_ref;
+            B3Vec3 on_ref = b3_msub(pi, ps, rn);
+            B3Vec3 pa = f < 3 ? on_ref : pi;
+            B3Vec3 pb = f < 3 ? pi : on_ref;
             m_push(m, pa, pb, b3_dot(b3_sub(pb, pa), n), (f < 3 ? 16u : 20u) + (uint32_t)i);
         }
     }
@@ -352,6 +386,7 @@ B3X_HD void box_box(Mani& m, const Obb& a, const Obb& b) {
 
 B3X_HDI void m_flip(Mani& m) {
     m.normal = b3_neg(m.normal);
+#pragma unroll
     for (int i = 0; i < B3_MAX_MANIFOLD; i++) {
         if (i < m.count) {
             B3Vec3 t = m.pa[i];
@@ -362,7 +397,7 @@ B3X_HDI void m_flip(Mani& m) {
 }
 
 // Pair dispatch by type with the A->B normal convention (05_collision.inl:472-534).
-B3X_HD void collide(Mani& m, Geo a, Geo b) {
+B3X_HD void collide(Mani& m, Geo a, Geo b, const Poly& P) {
     B3Vec3 center_a = a.p, center_b = b.p;
     bool flip = false;
     if (a.type > b.type) {
@@ -396,11 +431,12 @@ B3X_HD void collide(Mani& m, Geo a, Geo b) {
         ob.c = b.p;
         ob.h = b.half;
         b3_axes(b.q, &ob.ax[0], &ob.ax[1], &ob.ax[2]);
-        box_box(m, oa, ob);
+        box_box(m, oa, ob, P);
     }
     if (flip && m.count > 0) m_flip(m);
     if (m.count > 0) {
         if (b3_dot(m.normal, b3_sub(center_b, center_a)) < 0.0f) m.normal = b3_neg(m.normal);
+#pragma unroll
         for (int i = 0; i < B3_MAX_MANIFOLD; i++)
             if (i < m.count) m.sep[i] = b3_dot(b3_sub(m.pb[i], m.pa[i]), m.normal);
     }

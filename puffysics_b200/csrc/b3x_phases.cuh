@@ -1,0 +1,937 @@
+// b3x_phases.cuh -- the block-cooperative phases of the batched step: contact
+// generation and constraint preparation (collide_kernel) and the write-back of
+// the stepped worlds (out_kernel), one tile of 32 worlds per 128-thread block.
+//
+// Every phase is a function of (block state, thread index) and the threads of
+// a block meet only between phases (one __syncthreads per phase), so a tile
+// driver is a sequence of `x.each(phase)` calls that the GPU runs with one
+// thread per index and development tools can run with a loop.
+//
+// Caller memory is only touched through coalesced transfers: a warp reads or
+// writes consecutive words of one world's struct (B3Body, B3Shape, B3Contact,
+// B3Joint), and shared memory turns those rows into the per-lane columns of
+// the workspace and back.  Work that is independent per item (pairs,
+// candidates, contacts) is spread over the block in (item, world) order, so
+// consecutive threads touch the same item of consecutive worlds and their
+// workspace accesses coalesce as well.
+//
+// Arithmetic keeps the reference's operation order (file:line cited, paths
+// relative to the reference repository root).
+#pragma once
+#include <cstdint>
+
+#include "b3x_layout.cuh"
+#include "b3x_narrow.cuh"
+
+namespace b3x {
+
+constexpr int kCta = 128;            // threads of a collide / write-back block
+constexpr int kCtaWarps = kCta / 32;
+constexpr int kRow = NYW + 1;        // staged struct row (odd: conflict-free columns)
+
+// ---- block state ------------------------------------------------------------------
+struct CollideShared {
+    int live[kLanes], nb[kLanes], ns[kLanes], oldn[kLanes], nj[kLanes];
+    int n[kLanes], ovf[kLanes], drop[kLanes], cursor[kLanes], sorted[kLanes];
+    float grav[kLanes][3];
+    int maxnb, maxns, maxold, maxnj;
+    // pair window: candidate bits per world over the window's pairs, and the
+    // (candidate index, world) enumeration that spreads candidates over threads
+    int ptab[kPairWindow];                       // i | j << 16 of window pair t, -1 past the end
+    uint32_t cmask[kLanes][kPairWindow / 32];    // broadphase survivors of world l
+    uint32_t nmask[kLanes][kPairWindow / 32];    // candidates of world l with a manifold
+    int ccount[kLanes];
+    uint32_t wmask[kPairWindow];                 // worlds with more than ci candidates
+    int off[kPairWindow + 1];
+    int maxc, total;
+    int16_t kslot[kPairWindow][kLanes];          // contact slot of candidate (ci, l), -1 none
+    int16_t mfirst[kPairWindow][kLanes];         // warm-cache entries to match, [first, end)
+    int16_t mend[kPairWindow][kLanes];
+    union {
+        float stage[kCtaWarps][kLanes][kRow];    // gathered struct rows, [item][world][word]
+        float jstage[kLanes][NVW + 2];           // one joint of every world
+        float clip[48 * kCta];                   // narrowphase clip polygons
+    } u;
+};
+
+struct OutShared {
+    int live[kLanes], nb[kLanes], n[kLanes], nj[kLanes];
+    int maxnb, maxn, maxnj;
+    uint8_t bpred[kCtaWarps][kLanes];
+    union {
+        float bstage[kCtaWarps][kLanes][kRow];   // finalized body rows
+        float cstage[kLanes][NCW];               // one contact of every world (119: odd)
+        float jstage[kLanes][NJF + 1];           // one joint column block (97: odd)
+    } u;
+};
+
+B3X_HDI const float* world_words(const Args& a, int wi) {
+    return reinterpret_cast<const float*>(a.data + (size_t)wi * a.stride + a.offset);
+}
+B3X_HDI float* world_words_w(const Args& a, int wi) {
+    return reinterpret_cast<float*>(a.data + (size_t)wi * a.stride + a.offset);
+}
+B3X_HDI float* slot_of(const Args& a, int bt) { return a.ws + (size_t)bt * a.SP.tile_words; }
+
+// Index of the n-th set bit of a window mask (two words).
+B3X_HDI int nth_bit64(const uint32_t* m, int n) {
+    int c0 = popc32(m[0]);
+    return n < c0 ? nth_bit32(m[0], n) : 32 + nth_bit32(m[1], n - c0);
+}
+
+// ================================ collide ==========================================
+
+// Header of each world (warp w: worlds w, w+4, ...; lane = header word).
+B3X_HD void c_header(const Args& a, int tile, CollideShared& sh, int t) {
+    const int w = t >> 5, i = t & 31;
+    if (t == 0) sh.maxnb = sh.maxns = sh.maxold = sh.maxnj = 0;
+    for (int l = w; l < kLanes; l += kCtaWarps) {
+        int wi = tile * kLanes + l;
+        bool live = wi < a.count && (!a.active || a.active[wi]);
+        if (i == 0) sh.live[l] = live;
+        if (live && i < NHW) sh.u.stage[0][l][i] = ldg(world_words(a, wi) + i);
+    }
+}
+
+// Clamped counts and the step's per-world constants (09_step.inl:148-157).
+// Counts beyond the capacities would index past the arrays in the
+// reference; here they are clamped so a corrupt world cannot fault.
+B3X_HD void c_record(const Args& a, float* slot, CollideShared& sh, int l) {
+    const Layout& L = a.L;
+    const float* hw = sh.u.stage[0][l];
+    const int live = sh.live[l];
+    const int nb = live ? clampi(b3x_f2i(hw[HNB]), 0, L.B) : 0;
+    const int ns = live ? clampi(b3x_f2i(hw[HNS]), 0, L.S) : 0;
+    const int oldn = live ? clampi(b3x_f2i(hw[HNC]), 0, L.C) : 0;
+    const int nj = live ? clampi(b3x_f2i(hw[HNJ]), 0, L.J) : 0;
+    sh.nb[l] = nb;
+    sh.ns[l] = ns;
+    sh.oldn[l] = oldn;
+    sh.nj[l] = nj;
+    sh.n[l] = 0;
+    sh.ovf[l] = live ? b3x_f2i(hw[HOVC]) : 0;
+    sh.drop[l] = live ? b3x_f2i(hw[HDROP]) : 0;
+    sh.cursor[l] = 0;
+    for (int c = 0; c < 3; c++) sh.grav[l][c] = live ? hw[HGRAV + c] : 0.0f;
+    shared_max(&sh.maxnb, nb);
+    shared_max(&sh.maxns, ns);
+    shared_max(&sh.maxold, oldn);
+    shared_max(&sh.maxnj, nj);
+
+    const int subs = a.substeps;
+    const float h = a.dt / (float)subs;
+    const float inv_h = (float)subs * (1.0f / a.dt);
+    const float contact_hertz = live ? hw[HHZ] : 0.0f;
+    const float contact_damping = live ? hw[HDAMP] : 0.0f;
+    const float hertz = b3_minf(contact_hertz, 0.25f * inv_h);
+    float* rec = slot + a.SP.rec + l;
+    sti(rec, RLIVE, live);
+    sti(rec, RNB, nb);
+    sti(rec, RNS, ns);
+    sti(rec, ROLDN, oldn);
+    sti(rec, RNJ, nj);
+    COL(rec, RSPEED) = live ? hw[HSPEED] : 0.0f;
+    COL(rec, RRT) = live ? hw[HRT] : 0.0f;
+    COL(rec, RMAXLIN) = live ? hw[HMAXLIN] : 0.0f;
+    sts(rec, RCS, make_soft(hertz, contact_damping, h));
+    sts(rec, RSS, make_soft(2.0f * hertz, 0.5f * contact_damping, h));
+}
+
+// Struct rows of item k0 + w of every world into stage[w] (warp w, lane =
+// word; `words` words starting at byte `base` + k * `size` of the world).
+B3X_HD void c_gather(const Args& a, int tile, CollideShared& sh, const int* count, int k0, unsigned base,
+        unsigned size, int words, int t) {
+    const int w = t >> 5, i = t & 31, k = k0 + w;
+    for (int l = 0; l < kLanes; l++) {
+        if (k >= count[l]) continue;
+        const float* src = world_words(a, tile * kLanes + l) + (base + (size_t)size * k) / 4;
+        for (int c = i; c < words; c += 32) sh.u.stage[w][l][c] = ldg(src + c);
+    }
+}
+
+// Body k0 + w of world l: solver columns, step constants and pose
+// (inverse mass / inertia gated by type as the contact and joint prepares do,
+// 08_contacts.inl:236-239; velocity increments of 09_step.inl:5-18).
+B3X_HD void c_bodies(const Args& a, float* slot, CollideShared& sh, int k0, int t) {
+    const int w = t >> 5, l = t & 31, k = k0 + w;
+    if (k >= sh.nb[l]) return;
+    const float* y = sh.u.stage[w][l];
+    const float h = a.dt / (float)a.substeps;
+    float* bc = item(slot + a.SP.body, k, NBF) + l;
+    float* pc = item(slot + a.SP.pose, k, NPF) + l;
+    const int type = b3x_f2i(y[YTYPE]);
+    auto v3 = [&](int f) { return b3_v(y[f], y[f + 1], y[f + 2]); };
+    st3(bc, BV, v3(YLV));
+    st3(bc, BW, v3(YAV));
+    st3(bc, BDP, v3(YDP));
+    stq(bc, BDQ, b3_q(y[YDQ], y[YDQ + 1], y[YDQ + 2], y[YDQ + 3]));
+    COL(bc, BFLAGS) = y[YFLAGS];
+    COL(bc, BTYPE) = y[YTYPE];
+    if (type == B3_DYNAMIC) {
+        const float inv_mass = y[YIM];
+        B3Mat3 iw;
+        iw.cx = v3(YIW);
+        iw.cy = v3(YIW + 3);
+        iw.cz = v3(YIW + 6);
+        COL(bc, BMI) = inv_mass;
+        stm(bc, BII, iw);
+        float* kc = item(slot + a.SP.konst, k, NKF) + l;
+        const B3Vec3 gravity = b3_v(sh.grav[l][0], sh.grav[l][1], sh.grav[l][2]);
+        const float gs = inv_mass > 0.0f ? y[YGS] : 0.0f;
+        st3(kc, KDV, b3_add(b3_mul(v3(YF), h * inv_mass), b3_mul(gravity, h * gs)));
+        st3(kc, KDW, b3_mul(b3_mv(iw, v3(YT)), h));
+        COL(kc, KLD) = 1.0f / (1.0f + h * y[YLD]);
+        COL(kc, KAD) = 1.0f / (1.0f + h * y[YAD]);
+    } else {
+        COL(bc, BMI) = 0.0f;
+        stm(bc, BII, m3_zero());
+    }
+    st3(pc, PPOS, v3(YPOS));
+    stq(pc, PROT, b3_q(y[YROT], y[YROT + 1], y[YROT + 2], y[YROT + 3]));
+    st3(pc, PCEN, v3(YCEN));
+    st3(pc, PLC, v3(YLC));
+    st3(pc, PII, v3(YII));
+}
+
+// Shape k0 + w of world l: world pose and padded AABB (04_world.inl:293-336,
+// 08_contacts.inl:109-114); a shape on an invalid body never overlaps.
+B3X_HD void c_shapes(const Args& a, float* slot, CollideShared& sh, int k0, int t) {
+    const int w = t >> 5, l = t & 31, s = k0 + w;
+    if (s >= sh.ns[l]) return;
+    const float* y = sh.u.stage[w][l];
+    float* so = item(slot + a.SP.shape, s, NSF) + l;
+    const int body = b3x_f2i(y[XBODY]);
+    const int type = b3x_f2i(y[XTYPE]);
+    const float radius = y[XRAD];
+    const B3Vec3 half = b3_v(y[XHALF], y[XHALF + 1], y[XHALF + 2]);
+    COL(so, STYPE) = y[XTYPE];
+    COL(so, SBODY) = y[XBODY];
+    COL(so, SRAD) = radius;
+    st3(so, SHALF, half);
+    COL(so, SCAT) = y[XCAT];
+    COL(so, SCAT + 1) = y[XCAT + 1];
+    COL(so, SMASK) = y[XMASK];
+    COL(so, SMASK + 1) = y[XMASK + 1];
+    COL(so, SFRIC) = y[XFRIC];
+    COL(so, SREST) = y[XREST];
+    COL(so, SROLL) = y[XROLL];
+    if (body < 0 || body >= sh.nb[l]) {
+        st3(so, SLO, b3_v(INFINITY, INFINITY, INFINITY));
+        st3(so, SHI, b3_v(-INFINITY, -INFINITY, -INFINITY));
+        return;
+    }
+    const float* pc = item(slot + a.SP.pose, body, NPF) + l;
+    const B3Vec3 bp = ld3(pc, PPOS);
+    const B3Quat bq = ldq(pc, PROT);
+    const B3Vec3 p = b3_xf_point(bp, bq, b3_v(y[XLPOS], y[XLPOS + 1], y[XLPOS + 2]));
+    const B3Quat q = b3_qmul(bq, b3_q(y[XLROT], y[XLROT + 1], y[XLROT + 2], y[XLROT + 3]));
+    B3Vec3 lo, hi;
+    if (type == B3_SPHERE) {
+        B3Vec3 e = b3_v(radius, radius, radius);
+        lo = b3_sub(p, e);
+        hi = b3_add(p, e);
+    } else if (type == B3_CAPSULE) {
+        B3Vec3 yv = b3_rotate(q, b3_v(0.0f, half.y, 0.0f));
+        B3Vec3 c1 = b3_sub(p, yv), c2 = b3_add(p, yv);
+        B3Vec3 e = b3_v(radius, radius, radius);
+        lo = b3_sub(b3_v(b3_minf(c1.x, c2.x), b3_minf(c1.y, c2.y), b3_minf(c1.z, c2.z)), e);
+        hi = b3_add(b3_v(b3_maxf(c1.x, c2.x), b3_maxf(c1.y, c2.y), b3_maxf(c1.z, c2.z)), e);
+    } else {
+        B3Vec3 ax, ay, az;
+        b3_axes(q, &ax, &ay, &az);
+        B3Vec3 e = b3_v(fabsf(ax.x) * half.x + fabsf(ay.x) * half.y + fabsf(az.x) * half.z,
+            fabsf(ax.y) * half.x + fabsf(ay.y) * half.y + fabsf(az.y) * half.z,
+            fabsf(ax.z) * half.x + fabsf(ay.z) * half.y + fabsf(az.z) * half.z);
+        lo = b3_sub(p, e);
+        hi = b3_add(p, e);
+    }
+    const B3Vec3 pad = b3_v(B3_SPECULATIVE, B3_SPECULATIVE, B3_SPECULATIVE);
+    st3(so, SPOS, p);
+    stq(so, SROT, q);
+    st3(so, SLO, b3_sub(lo, pad));
+    st3(so, SHI, b3_add(hi, pad));
+}
+
+// Words of a previous-step contact that the warm-start cache keeps
+// (08_contacts.inl:68-87), in OLD field order.
+B3X_HDI int old_word(int i) {
+    return i == OSA ? WSA : i == OSB ? WSB : i == OCNT ? WCNT : i < OTWI ? WFI + (i - OFI)
+        : i == OTWI ? WTWI : i < OFEAT ? WRI + (i - ORI) : i < ONI ? PW(i - OFEAT, QFEAT) : PW(i - ONI, QNI);
+}
+
+B3X_HD void c_old_gather(const Args& a, int tile, CollideShared& sh, int k0, int t) {
+    const int w = t >> 5, i = t & 31, k = k0 + w;
+    if (i >= NOF) return;
+    const int word = old_word(i);
+    for (int l = 0; l < kLanes; l++) {
+        if (k >= sh.oldn[l]) continue;
+        const float* src = world_words(a, tile * kLanes + l) + (a.L.contact_off + (size_t)B3X_CONTACT_BYTES * k) / 4;
+        sh.u.stage[w][l][i] = ldg(src + word);
+    }
+}
+
+B3X_HD void c_old(const Args& a, float* slot, CollideShared& sh, int k0, int t) {
+    const int w = t >> 5, l = t & 31, k = k0 + w;
+    if (k >= sh.oldn[l]) return;
+    float* oc = item(slot + a.SP.old, k, NOF) + l;
+    for (int f = 0; f < NOF; f++) COL(oc, f) = sh.u.stage[w][l][f];
+}
+
+// Whether the old cache's (shape_a, shape_b) keys strictly increase (then the
+// reference matches with a merge cursor, else with a full scan; both pick
+// the same entry), 08_contacts.inl:70-79.
+B3X_HD void c_old_sorted(const Args& a, float* slot, CollideShared& sh, int l) {
+    const float* oc = slot + a.SP.old + l;
+    int sorted = 1;
+    for (int k = 1; k < sh.oldn[l]; k++) {
+        const float* p = item(oc, k - 1, NOF);
+        const float* c = item(oc, k, NOF);
+        int pa = ldi(p, OSA), pb = ldi(p, OSB), sa = ldi(c, OSA), sb = ldi(c, OSB);
+        if (pa > sa || (pa == sa && pb >= sb)) sorted = 0;
+    }
+    sh.sorted[l] = sorted;
+}
+
+// Joint q of every world into jstage (warp w: worlds w, w+4, ...).
+B3X_HD void c_joint_gather(const Args& a, int tile, CollideShared& sh, int q, int t) {
+    const int w = t >> 5, i = t & 31;
+    for (int l = w; l < kLanes; l += kCtaWarps) {
+        if (q >= sh.nj[l]) continue;
+        const float* src = world_words(a, tile * kLanes + l) + (a.L.joint_off + (size_t)B3X_JOINT_BYTES * q) / 4;
+        for (int c = i; c < NVW; c += 32) sh.u.jstage[l][c] = ldg(src + c);
+    }
+}
+
+// Prepare joint q of world l (06_joints.inl:161-202); invalid body indices
+// make the joint inert (the reference would index out of bounds).
+B3X_HD void c_joint(const Args& a, float* slot, CollideShared& sh, int q, int l) {
+    if (q >= sh.nj[l]) return;
+    const float* y = sh.u.jstage[l];
+    auto v3 = [&](int f) { return b3_v(y[f], y[f + 1], y[f + 2]); };
+    auto v4 = [&](int f) { return b3_q(y[f], y[f + 1], y[f + 2], y[f + 3]); };
+    const float h = a.dt / (float)a.substeps;
+    float* jo = item(slot + a.SP.joint, q, NJF) + l;
+    const int type = b3x_f2i(y[VTYPE]), ja = b3x_f2i(y[VBA]), jb = b3x_f2i(y[VBB]);
+    const int nb = sh.nb[l];
+    sti(jo, JTYPE, type);
+    sti(jo, JBA, ja);
+    sti(jo, JBB, jb);
+    COL(jo, JCC) = y[VCC];
+    if (ja < 0 || ja >= nb || jb < 0 || jb >= nb) {
+        sti(jo, JOK, 0);
+        return;
+    }
+    sti(jo, JOK, 1);
+    const float* bca = item(slot + a.SP.body, ja, NBF) + l;
+    const float* bcb = item(slot + a.SP.body, jb, NBF) + l;
+    const float* pa = item(slot + a.SP.pose, ja, NPF) + l;
+    const float* pb = item(slot + a.SP.pose, jb, NPF) + l;
+    const float ma = COL(bca, BMI), mb = COL(bcb, BMI);
+    const B3Mat3 ia = ldm(bca, BII), ib = ldm(bcb, BII);
+    const B3Mat3 isum = m3_add(ia, ib);
+    const int fixed = b3_dot(isum.cx, b3_cross(isum.cy, isum.cz)) < 1.0e-20f;
+    const B3Soft soft = make_soft(y[VCHZ], y[VCDMP], h);
+    const B3Quat rot_a = ldq(pa, PROT), rot_b = ldq(pb, PROT);
+    const B3Quat fqa = b3_qmul(rot_a, v4(VLRA)), fqb = b3_qmul(rot_b, v4(VLRB));
+    const B3Vec3 fpa = b3_rotate(rot_a, b3_sub(v3(VLAA), ld3(pa, PLC)));
+    const B3Vec3 fpb = b3_rotate(rot_b, b3_sub(v3(VLAB), ld3(pb, PLC)));
+    const B3Vec3 dc = b3_sub(ld3(pb, PCEN), ld3(pa, PCEN));
+    COL(jo, JIMA) = ma;
+    COL(jo, JIMB) = mb;
+    stm(jo, JIIA, ia);
+    stm(jo, JIIB, ib);
+    sti(jo, JFIX, fixed);
+    sts(jo, JSOFT, soft);
+    stq(jo, JFQA, fqa);
+    stq(jo, JFQB, fqb);
+    st3(jo, JFPA, fpa);
+    st3(jo, JFPB, fpb);
+    st3(jo, JDC, dc);
+    st3(jo, JLI, v3(VLI));
+    if (type == B3_JOINT_WELD) {
+        const float lh = y[VLHZ], ah = y[VAHZ];
+        const B3Soft ls = lh == 0.0f ? soft : make_soft(lh, y[VLDMP], h);
+        const B3Soft as = ah == 0.0f ? soft : make_soft(ah, y[VADMP], h);
+        stm(jo, JAM, m3_inv(isum));
+        COL(jo, JLH) = lh;
+        COL(jo, JAH) = ah;
+        sts(jo, JLS, ls);
+        sts(jo, JAS, as);
+        st3(jo, JAI, v3(VAI));
+    } else {
+        const B3Vec3 axis = b3_rotate(fqa, b3_v(0.0f, 0.0f, 1.0f));
+        const float kx = b3_dot(axis, b3_mv(isum, axis));
+        const float axm = kx > 0.0f ? 1.0f / kx : 0.0f;
+        const B3Quat rel = b3_qinv_mul(fqa, fqb);
+        B3Vec3 px, py;
+        hinge_perps(fqa, rel, &px, &py);
+        st3(jo, JAX, axis);
+        COL(jo, JAXM) = axm;
+        st3(jo, JPX, px);
+        st3(jo, JPY, py);
+        sts(jo, JSS, make_soft(y[VHZ], y[VDR], h));
+        COL(jo, JENS) = y[VENS];
+        COL(jo, JENM) = y[VENM];
+        COL(jo, JENL) = y[VENL];
+        COL(jo, JPI) = y[VPI];
+        COL(jo, JPI + 1) = y[VPI + 1];
+        COL(jo, JSI) = y[VSI];
+        COL(jo, JMI) = y[VMI];
+        COL(jo, JLOI) = y[VLOI];
+        COL(jo, JUPI) = y[VUPI];
+        COL(jo, JMMT) = y[VMMT];
+        COL(jo, JMS) = y[VMS];
+        COL(jo, JTA) = y[VTA];
+        COL(jo, JLA) = y[VLA];
+        COL(jo, JUA) = y[VUA];
+        if (type != B3_JOINT_REVOLUTE) st3(jo, JAI, v3(VAI));
+    }
+}
+
+// -- pair windows -----------------------------------------------------------------
+// Pair p of the lexicographic (i < j < ns) order -> (i, j).
+B3X_HDI int pair_of(int p, int ns) {
+    int i = 0;
+    while (i < ns - 1 && p >= ns - 1 - i) {
+        p -= ns - 1 - i;
+        i++;
+    }
+    if (i >= ns - 1) return -1;
+    return i | ((i + 1 + p) << 16);
+}
+
+B3X_HD void c_window_setup(CollideShared& sh, int p0, int npairs, int t) {
+    if (t < kPairWindow) sh.ptab[t] = p0 + t < npairs ? pair_of(p0 + t, sh.maxns) : -1;
+    if (t < kLanes) {
+        for (int c = 0; c < kPairWindow / 32; c++) {
+            sh.cmask[t][c] = 0;
+            sh.nmask[t][c] = 0;
+        }
+    }
+    if (t == 0) sh.maxc = 0;
+}
+
+// Broadphase of window pair pp for world l: the reference's predicate
+// (08_contacts.inl:44-58; AABB overlap first, the side-effect-free tests in
+// a cheaper order) with its joint-connection filter (08_contacts.inl:94-104).
+B3X_HD void c_broadphase(const Args& a, float* slot, CollideShared& sh, int t) {
+    const float* sc = slot + a.SP.shape;
+    for (int idx = t; idx < kPairWindow * kLanes; idx += kCta) {
+        const int pp = idx >> 5, l = idx & 31;
+        const int pr = sh.ptab[pp];
+        if (pr < 0) continue;
+        const int i = pr & 0xffff, j = pr >> 16;
+        if (j >= sh.ns[l]) continue;
+        const float* si = item(sc, i, NSF) + l;
+        const float* sj = item(sc, j, NSF) + l;
+        const B3Vec3 lo_i = ld3(si, SLO), hi_i = ld3(si, SHI), lo_j = ld3(sj, SLO), hi_j = ld3(sj, SHI);
+        if (!(lo_i.x <= hi_j.x && hi_i.x >= lo_j.x && lo_i.y <= hi_j.y && hi_i.y >= lo_j.y && lo_i.z <= hi_j.z
+                && hi_i.z >= lo_j.z))
+            continue;
+        const int bi = ldi(si, SBODY), bj = ldi(sj, SBODY);
+        if (bi == bj) continue;
+        const float* bc = slot + a.SP.body + l;
+        if (ldi(item(bc, bi, NBF), BTYPE) == B3_STATIC && ldi(item(bc, bj, NBF), BTYPE) == B3_STATIC) continue;
+        const uint64_t cat_i = (uint64_t)b3x_f2u(COL(si, SCAT)) | ((uint64_t)b3x_f2u(COL(si, SCAT + 1)) << 32);
+        const uint64_t msk_i = (uint64_t)b3x_f2u(COL(si, SMASK)) | ((uint64_t)b3x_f2u(COL(si, SMASK + 1)) << 32);
+        const uint64_t cat_j = (uint64_t)b3x_f2u(COL(sj, SCAT)) | ((uint64_t)b3x_f2u(COL(sj, SCAT + 1)) << 32);
+        const uint64_t msk_j = (uint64_t)b3x_f2u(COL(sj, SMASK)) | ((uint64_t)b3x_f2u(COL(sj, SMASK + 1)) << 32);
+        if ((cat_i & msk_j) == 0 || (cat_j & msk_i) == 0) continue;
+        bool connected = false;
+        const float* jc = slot + a.SP.joint + l;
+        for (int q = 0; q < sh.nj[l]; q++) {
+            const float* jo = item(jc, q, NJF);
+            const int ja = ldi(jo, JBA), jb = ldi(jo, JBB);
+            if (!ldi(jo, JCC) && ((ja == bi && jb == bj) || (ja == bj && jb == bi))) connected = true;
+        }
+        if (connected) continue;
+        shared_or(&sh.cmask[l][pp >> 5], 1u << (pp & 31));
+    }
+}
+
+B3X_HD void c_count(CollideShared& sh, int l) {
+    int c = 0;
+    for (int w = 0; w < kPairWindow / 32; w++) c += popc32(sh.cmask[l][w]);
+    sh.ccount[l] = c;
+    shared_max(&sh.maxc, c);
+}
+
+B3X_HD void c_enumerate(CollideShared& sh, int ci) {
+    if (ci >= sh.maxc) return;
+    uint32_t m = 0;
+    for (int l = 0; l < kLanes; l++)
+        if (sh.ccount[l] > ci) m |= 1u << l;
+    sh.wmask[ci] = m;
+}
+
+B3X_HD void c_prefix(CollideShared& sh) {
+    sh.off[0] = 0;
+    for (int ci = 0; ci < sh.maxc; ci++) sh.off[ci + 1] = sh.off[ci] + popc32(sh.wmask[ci]);
+    sh.total = sh.off[sh.maxc];
+}
+
+// Enumeration index -> (candidate index ci, world l).
+B3X_HDI void decode(const CollideShared& sh, int idx, int& ci, int& l) {
+    int lo = 0, hi = sh.maxc - 1;
+    while (lo < hi) {
+        int mid = (lo + hi + 1) >> 1;
+        if (sh.off[mid] <= idx) lo = mid;
+        else hi = mid - 1;
+    }
+    ci = lo;
+    l = nth_bit32(sh.wmask[ci], idx - sh.off[ci]);
+}
+
+// Narrowphase of every candidate of the window (05_collision.inl), stored
+// relative to the body centers (08_contacts.inl:5-39).
+B3X_HD void c_narrow(const Args& a, float* slot, CollideShared& sh, int t) {
+    const float* sc = slot + a.SP.shape;
+    Poly P;
+    P.base = sh.u.clip + t;
+    P.stride = kCta;
+    for (int idx = t; idx < sh.total; idx += kCta) {
+        int ci, l;
+        decode(sh, idx, ci, l);
+        const int pr = sh.ptab[nth_bit64(sh.cmask[l], ci)];
+        const int i = pr & 0xffff, j = pr >> 16;
+        const float* si = item(sc, i, NSF) + l;
+        const float* sj = item(sc, j, NSF) + l;
+        Geo ga, gb;
+        ga.p = ld3(si, SPOS); ga.q = ldq(si, SROT); ga.type = ldi(si, STYPE);
+        ga.radius = COL(si, SRAD); ga.half = ld3(si, SHALF);
+        gb.p = ld3(sj, SPOS); gb.q = ldq(sj, SROT); gb.type = ldi(sj, STYPE);
+        gb.radius = COL(sj, SRAD); gb.half = ld3(sj, SHALF);
+        Mani m;
+        collide(m, ga, gb, P);
+        if (m.count == 0) continue;
+        shared_or(&sh.nmask[l][ci >> 5], 1u << (ci & 31));
+        const float* pc = slot + a.SP.pose + l;
+        const B3Vec3 ca = ld3(item(pc, ldi(si, SBODY), NPF), PCEN);
+        const B3Vec3 cb = ld3(item(pc, ldi(sj, SBODY), NPF), PCEN);
+        float* md = item(slot + a.SP.cand, ci, NMF) + l;
+        sti(md, MCNT, m.count);
+        st3(md, MN, m.normal);
+#pragma unroll
+        for (int p = 0; p < B3_MAX_MANIFOLD; p++) {
+            if (p >= m.count) continue;
+            B3Vec3 ra = b3_sub(m.pa[p], ca), rb = b3_sub(m.pb[p], cb);
+            st3(md, MW(p, MRA), ra);
+            st3(md, MW(p, MRB), rb);
+            COL(md, MW(p, MBSEP)) = m.sep[p] - b3_dot(b3_sub(rb, ra), m.normal);
+            sti(md, MW(p, MFEAT), (int)m.feat[p]);
+        }
+    }
+}
+
+// Contact slots and warm-cache ranges of world l's candidates, in the
+// reference's order (08_contacts.inl:120-171): slots are handed out while the
+// capacity lasts, then overflow is counted; the old cache is walked with the
+// merge cursor when its keys are sorted.
+B3X_HD void c_rank(const Args& a, float* slot, CollideShared& sh, int l) {
+    const float* oc = slot + a.SP.old + l;
+    int n = sh.n[l], ovf = sh.ovf[l], drop = sh.drop[l], cursor = sh.cursor[l];
+    const int on = sh.oldn[l], sorted = sh.sorted[l], cnt = sh.ccount[l];
+    for (int ci = 0; ci < cnt; ci++) {
+        sh.kslot[ci][l] = -1;
+        if (!((sh.nmask[l][ci >> 5] >> (ci & 31)) & 1u)) continue;
+        if (n >= a.L.C) {
+            ovf = 1;
+            drop++;
+            continue;
+        }
+        sh.kslot[ci][l] = (int16_t)n++;
+        const int pr = sh.ptab[nth_bit64(sh.cmask[l], ci)];
+        const int i = pr & 0xffff, j = pr >> 16;
+        int first = 0, end = on;
+        if (sorted) {
+            while (cursor < on) {
+                const float* o = item(oc, cursor, NOF);
+                const int sa = ldi(o, OSA), sb = ldi(o, OSB);
+                if (sa < i || (sa == i && sb < j)) cursor++;
+                else break;
+            }
+            first = cursor;
+            end = cursor < on ? cursor + 1 : on;
+        }
+        sh.mfirst[ci][l] = (int16_t)first;
+        sh.mend[ci][l] = (int16_t)end;
+    }
+    sh.n[l] = n;
+    sh.ovf[l] = ovf;
+    sh.drop[l] = drop;
+    sh.cursor[l] = cursor;
+}
+
+// Build contact kslot of world l from its candidate: b3_contact_from_mani
+// (08_contacts.inl:5-39), the warm-start carry (08_contacts.inl:136-171) and
+// b3_prepare_one_contact (08_contacts.inl:234-291).  All 119 words except the
+// point slots past the point count go to the contact's workspace columns.
+B3X_HD void c_prepare(const Args& a, float* slot, CollideShared& sh, int t) {
+    const float* sc = slot + a.SP.shape;
+    for (int idx = t; idx < sh.total; idx += kCta) {
+        int ci, l;
+        decode(sh, idx, ci, l);
+        const int k = sh.kslot[ci][l];
+        if (k < 0) continue;
+        const int pr = sh.ptab[nth_bit64(sh.cmask[l], ci)];
+        const int i = pr & 0xffff, j = pr >> 16;
+        const float* si = item(sc, i, NSF) + l;
+        const float* sj = item(sc, j, NSF) + l;
+        const float* md = item(slot + a.SP.cand, ci, NMF) + l;
+        const int bi = ldi(si, SBODY), bj = ldi(sj, SBODY);
+        const float* ba = item(slot + a.SP.body, bi, NBF) + l;
+        const float* bb = item(slot + a.SP.body, bj, NBF) + l;
+        const int cnt = ldi(md, MCNT);
+        const B3Vec3 nrm = ld3(md, MN);
+        const B3Vec3 t1 = b3_perp(nrm);
+        const B3Vec3 t2 = b3_cross(t1, nrm);
+        const float rest_i = COL(si, SREST), rest_j = COL(sj, SREST);
+        const int stat = ldi(ba, BTYPE) != B3_DYNAMIC || ldi(bb, BTYPE) != B3_DYNAMIC;
+
+        // warm-start carry by (shape_a, shape_b) and feature id
+        uint32_t feat[B3_MAX_MANIFOLD];
+        float ni[B3_MAX_MANIFOLD];
+#pragma unroll
+        for (int p = 0; p < B3_MAX_MANIFOLD; p++) {
+            ni[p] = 0.0f;
+            feat[p] = p < cnt ? (uint32_t)ldi(md, MW(p, MFEAT)) : 0u;
+        }
+        B3Vec2 fi;
+        fi.x = 0.0f;
+        fi.y = 0.0f;
+        float twi = 0.0f;
+        B3Vec3 ri = b3_v(0.0f, 0.0f, 0.0f);
+        const float* oc = slot + a.SP.old + l;
+        for (int kk = sh.mfirst[ci][l]; kk < sh.mend[ci][l]; kk++) {
+            const float* o = item(oc, kk, NOF);
+            if (ldi(o, OSA) != i || ldi(o, OSB) != j) continue;
+            const int ocnt = clampi(ldi(o, OCNT), 0, B3_MAX_MANIFOLD);
+#pragma unroll
+            for (int p = 0; p < B3_MAX_MANIFOLD; p++) {
+                if (p >= cnt) continue;
+#pragma unroll
+                for (int q = 0; q < B3_MAX_MANIFOLD; q++)
+                    if (q < ocnt && feat[p] == b3x_f2u(COL(o, OFEAT + q))) ni[p] = COL(o, ONI + q);
+            }
+            fi.x = COL(o, OFI);
+            fi.y = COL(o, OFI + 1);
+            twi = COL(o, OTWI);
+            ri = ld3(o, ORI);
+        }
+
+        // prepare
+        const float ma = COL(ba, BMI), mb = COL(bb, BMI);
+        const B3Mat3 ia = ldm(ba, BII), ib = ldm(bb, BII);
+        const B3Vec3 va = ld3(ba, BV), wa = ld3(ba, BW), vb = ld3(bb, BV), wb = ld3(bb, BW);
+        float* co = item(slot + a.SP.cont, k, NCW) + l;
+        const float inv_tau = 1.0f / B3_SPECULATIVE;
+        B3Vec3 center_a = b3_v(0.0f, 0.0f, 0.0f), center_b = b3_v(0.0f, 0.0f, 0.0f);
+        float wsum = 0.0f;
+        B3Vec3 ras[B3_MAX_MANIFOLD];
+#pragma unroll
+        for (int p = 0; p < B3_MAX_MANIFOLD; p++) {
+            if (p >= cnt) continue;
+            const B3Vec3 ra = ld3(md, MW(p, MRA)), rb = ld3(md, MW(p, MRB));
+            const float base_sep = COL(md, MW(p, MBSEP));
+            ras[p] = ra;
+            const B3Vec3 rn_a = b3_cross(ra, nrm), rn_b = b3_cross(rb, nrm);
+            const float kn = ma + mb + b3_dot(rn_a, b3_mv(ia, rn_a)) + b3_dot(rn_b, b3_mv(ib, rn_b));
+            const float nm = kn > 0.0f ? 1.0f / kn : 0.0f;
+            const B3Vec3 vra = b3_add(va, b3_cross(wa, ra)), vrb = b3_add(vb, b3_cross(wb, rb));
+            const float relv = b3_dot(nrm, b3_sub(vrb, vra));
+            const float sep = base_sep + b3_dot(b3_sub(rb, ra), nrm);
+            const float wgt = b3_clamp(2.0f - sep * inv_tau, B3_MIN_FRICTION_W, 1.0f);
+            center_a = b3_madd(center_a, wgt, ra);
+            center_b = b3_madd(center_b, wgt, rb);
+            wsum += wgt;
+            st3(co, PW(p, QRA), ra);
+            st3(co, PW(p, QRB), rb);
+            COL(co, PW(p, QBSEP)) = base_sep;
+            COL(co, PW(p, QRELV)) = relv;
+            COL(co, PW(p, QNI)) = ni[p];
+            COL(co, PW(p, QTOT)) = 0.0f;
+            COL(co, PW(p, QNM)) = nm;
+            sti(co, PW(p, QFEAT), (int)feat[p]);
+        }
+        const float invw = wsum > 0.0f ? 1.0f / wsum : 0.0f;
+        const B3Vec3 ca = b3_mul(center_a, invw), cb = b3_mul(center_b, invw);
+#pragma unroll
+        for (int p = 0; p < B3_MAX_MANIFOLD; p++)
+            if (p < cnt) COL(co, PW(p, QLEV)) = b3_len(b3_sub(ras[p], ca));
+        const B3Vec3 rta1 = b3_cross(ca, t1), rta2 = b3_cross(ca, t2);
+        const B3Vec3 rtb1 = b3_cross(cb, t1), rtb2 = b3_cross(cb, t2);
+        B3Mat2 kt2;
+        kt2.cx.x = ma + mb + b3_dot(rta1, b3_mv(ia, rta1)) + b3_dot(rtb1, b3_mv(ib, rtb1));
+        kt2.cy.y = ma + mb + b3_dot(rta2, b3_mv(ia, rta2)) + b3_dot(rtb2, b3_mv(ib, rtb2));
+        kt2.cx.y = kt2.cy.x = b3_dot(rta1, b3_mv(ia, rta2)) + b3_dot(rtb1, b3_mv(ib, rtb2));
+        const B3Mat3 isum = m3_add(ia, ib);
+        const float ktw = b3_dot(nrm, b3_mv(isum, nrm));
+        sti(co, WSA, i);
+        sti(co, WSB, j);
+        sti(co, WBA, bi);
+        sti(co, WBB, bj);
+        sti(co, WCNT, cnt);
+        sti(co, WSTAT, stat);
+        st3(co, WN, nrm);
+        st3(co, WT1, t1);
+        st3(co, WT2, t2);
+        st3(co, WCA, ca);
+        st3(co, WCB, cb);
+        COL(co, WFRIC) = sqrtf(COL(si, SFRIC) * COL(sj, SFRIC));
+        COL(co, WREST) = rest_i > rest_j ? rest_i : rest_j;
+        COL(co, WROLL) = b3_maxf(COL(si, SROLL), COL(sj, SROLL));
+        COL(co, WTWM) = ktw > 0.0f ? 1.0f / ktw : 0.0f;
+        COL(co, WTWI) = twi;
+        COL(co, WFI) = fi.x;
+        COL(co, WFI + 1) = fi.y;
+        st3(co, WRI, ri);
+        st22(co, WTM, m2_inv(kt2));
+        stm(co, WRM, m3_inv(isum));
+        COL(co, WMA) = ma;
+        COL(co, WMB) = mb;
+        stm(co, WIA, ia);
+        stm(co, WIB, ib);
+        const float* rec = slot + a.SP.rec + l;
+        sts(co, WSOFT, lds(rec, stat ? RSS : RCS));
+    }
+}
+
+B3X_HD void c_finish(const Args& a, float* slot, CollideShared& sh, int l) {
+    float* rec = slot + a.SP.rec + l;
+    sti(rec, RN, sh.n[l]);
+    sti(rec, ROVF, sh.ovf[l]);
+    sti(rec, RDROP, sh.drop[l]);
+}
+
+// The collide phases of tile `bt` of the launch.
+template <class X>
+B3X_HD void collide_tile(X& x, const Args& a, int bt, CollideShared& sh) {
+    float* slot = slot_of(a, bt);
+    const int tile = a.tile0 + bt;
+    x.each([&](int t) { c_header(a, tile, sh, t); });
+    x.each([&](int t) { if (t < kLanes) c_record(a, slot, sh, t); });
+    for (int k0 = 0; k0 < sh.maxnb; k0 += kCtaWarps) {
+        x.each([&](int t) { c_gather(a, tile, sh, sh.nb, k0, B3X_WORLD_HEADER_BYTES, B3X_BODY_BYTES, NYW, t); });
+        x.each([&](int t) { c_bodies(a, slot, sh, k0, t); });
+    }
+    for (int k0 = 0; k0 < sh.maxns; k0 += kCtaWarps) {
+        x.each([&](int t) { c_gather(a, tile, sh, sh.ns, k0, a.L.shape_off, B3X_SHAPE_BYTES, NXW, t); });
+        x.each([&](int t) { c_shapes(a, slot, sh, k0, t); });
+    }
+    for (int k0 = 0; k0 < sh.maxold; k0 += kCtaWarps) {
+        x.each([&](int t) { c_old_gather(a, tile, sh, k0, t); });
+        x.each([&](int t) { c_old(a, slot, sh, k0, t); });
+    }
+    for (int q = 0; q < sh.maxnj; q++) {
+        x.each([&](int t) { c_joint_gather(a, tile, sh, q, t); });
+        x.each([&](int t) { if (t < kLanes) c_joint(a, slot, sh, q, t); });
+    }
+    x.each([&](int t) { if (t < kLanes) c_old_sorted(a, slot, sh, t); });
+    const int maxns = sh.maxns;
+    const int npairs = maxns * (maxns - 1) / 2;
+    for (int p0 = 0; p0 < npairs; p0 += kPairWindow) {
+        x.each([&](int t) { c_window_setup(sh, p0, npairs, t); });
+        x.each([&](int t) { c_broadphase(a, slot, sh, t); });
+        x.each([&](int t) { if (t < kLanes) c_count(sh, t); });
+        x.each([&](int t) { if (t < kPairWindow) c_enumerate(sh, t); });
+        x.each([&](int t) { if (t == 0) c_prefix(sh); });
+        if (sh.total == 0) continue;
+        x.each([&](int t) { c_narrow(a, slot, sh, t); });
+        x.each([&](int t) { if (t < kLanes) c_rank(a, slot, sh, t); });
+        x.each([&](int t) { c_prepare(a, slot, sh, t); });
+    }
+    x.each([&](int t) { if (t < kLanes) c_finish(a, slot, sh, t); });
+}
+
+// ================================ write-back =======================================
+
+B3X_HD void o_record(const Args& a, float* slot, OutShared& sh, int l) {
+    const float* rec = slot + a.SP.rec + l;
+    sh.live[l] = ldi(rec, RLIVE);
+    sh.nb[l] = ldi(rec, RNB);
+    sh.n[l] = ldi(rec, RN);
+    sh.nj[l] = ldi(rec, RNJ);
+}
+
+B3X_HD void o_maxima(OutShared& sh) {
+    int mb = 0, mn = 0, mj = 0;
+    for (int l = 0; l < kLanes; l++) {
+        mb = sh.nb[l] > mb ? sh.nb[l] : mb;
+        mn = sh.n[l] > mn ? sh.n[l] : mn;
+        mj = sh.nj[l] > mj ? sh.nj[l] : mj;
+    }
+    sh.maxnb = mb;
+    sh.maxn = mn;
+    sh.maxnj = mj;
+}
+
+// Finalize body k0 + w of world l (09_step.inl:109-130) into a staged B3Body
+// row; bpred says which word groups the reference writes for it.
+enum : uint8_t { OB_VEL = 1, OB_POSE = 2, OB_INVI = 4 };
+
+B3X_HD void o_bodies(const Args& a, float* slot, OutShared& sh, int k0, int t) {
+    const int w = t >> 5, l = t & 31, k = k0 + w;
+    if (k >= sh.nb[l]) return;
+    const float* bc = item(slot + a.SP.body, k, NBF) + l;
+    const float* pc = item(slot + a.SP.pose, k, NPF) + l;
+    float* y = sh.u.bstage[w][l];
+    auto put3 = [&](int f, B3Vec3 v) { y[f] = v.x; y[f + 1] = v.y; y[f + 2] = v.z; };
+    auto put4 = [&](int f, B3Quat q) { y[f] = q.v.x; y[f + 1] = q.v.y; y[f + 2] = q.v.z; y[f + 3] = q.s; };
+    const int type = ldi(bc, BTYPE);
+    const bool dyn_flag = (b3x_f2u(COL(bc, BFLAGS)) & B3_FLAG_DYNAMIC) != 0;
+    uint8_t pred = 0;
+    if (type != B3_STATIC || dyn_flag) {
+        put3(YLV, ld3(bc, BV));
+        put3(YAV, ld3(bc, BW));
+        pred |= OB_VEL;
+    }
+    if (type != B3_STATIC) {
+        const B3Vec3 center = b3_add(ld3(pc, PCEN), ld3(bc, BDP));
+        const B3Quat rot = b3_qnorm(b3_qmul(ldq(bc, BDQ), ldq(pc, PROT)));
+        put3(YCEN, center);
+        put4(YROT, rot);
+        put3(YPOS, b3_sub(center, b3_rotate(rot, ld3(pc, PLC))));
+        put3(YDP, b3_v(0.0f, 0.0f, 0.0f));
+        put4(YDQ, b3_q_id());
+        put3(YF, b3_v(0.0f, 0.0f, 0.0f));
+        put3(YT, b3_v(0.0f, 0.0f, 0.0f));
+        pred |= OB_POSE;
+        if (type == B3_DYNAMIC) {
+            const B3Mat3 iw = b3_world_inv_i(rot, ld3(pc, PII));
+            put3(YIW, iw.cx);
+            put3(YIW + 3, iw.cy);
+            put3(YIW + 6, iw.cz);
+            pred |= OB_INVI;
+        }
+    }
+    sh.bpred[w][l] = pred;
+}
+
+B3X_HDI bool body_word_written(int word, uint8_t pred) {
+    if (word < YLC) return pred & OB_POSE;
+    if (word < YLV) return false;
+    if (word < YF) return pred & OB_VEL;
+    if (word < YIM) return pred & OB_POSE;
+    if (word < YIW) return false;
+    if (word < YLD) return pred & OB_INVI;
+    return false;
+}
+
+B3X_HD void o_body_write(const Args& a, int tile, OutShared& sh, int k0, int t) {
+    const int w = t >> 5, i = t & 31, k = k0 + w;
+    for (int l = 0; l < kLanes; l++) {
+        if (k >= sh.nb[l]) continue;
+        const uint8_t pred = sh.bpred[w][l];
+        float* dst = world_words_w(a, tile * kLanes + l) + (B3X_WORLD_HEADER_BYTES + (size_t)B3X_BODY_BYTES * k) / 4;
+        for (int c = i; c < NYW; c += 32)
+            if (body_word_written(c, pred)) dst[c] = sh.u.bstage[w][l][c];
+    }
+}
+
+// Contact k of every world: column block -> B3Contact rows.
+B3X_HD void o_contact_stage(const Args& a, float* slot, OutShared& sh, int k, int t) {
+    const float* src = item(slot + a.SP.cont, k, NCW);
+    for (int idx = t; idx < NCW * kLanes; idx += kCta) sh.u.cstage[idx & 31][idx >> 5] = src[idx];
+}
+
+// Point slots past the point count keep their previous bytes, as in the
+// reference (b3_contact_from_mani writes only the manifold's points).
+B3X_HD void o_contact_write(const Args& a, int tile, OutShared& sh, int k, int t) {
+    const int w = t >> 5, i = t & 31;
+    for (int l = w; l < kLanes; l += kCtaWarps) {
+        if (k >= sh.n[l]) continue;
+        const float* row = sh.u.cstage[l];
+        const int cnt = clampi(b3x_f2i(row[WCNT]), 0, B3_MAX_MANIFOLD);
+        const int stale_lo = WP + cnt * NQW;
+        float* dst = world_words_w(a, tile * kLanes + l) + (a.L.contact_off + (size_t)B3X_CONTACT_BYTES * k) / 4;
+        for (int c = i; c < NCW; c += 32)
+            if (c < stale_lo || c >= WCA) dst[c] = row[c];
+    }
+}
+
+// Joint column feeding B3Joint word `word` after the step, -1 when the step
+// leaves the word as it was (06_joints.inl:161-202 writes the prepared
+// fields, the step's finalize the impulses and the hinge rows).
+B3X_HDI int joint_source(int word, bool weld) {
+    if (word == VFIX) return JFIX;
+    if (word >= VSOFT && word < VSOFT + 3) return JSOFT + (word - VSOFT);
+    if (word == VIMA) return JIMA;
+    if (word == VIMB) return JIMB;
+    if (word >= VIIA && word < VIIA + 9) return JIIA + (word - VIIA);
+    if (word >= VIIB && word < VIIB + 9) return JIIB + (word - VIIB);
+    if (word >= VFPA && word < VLI) return JFPA + (word - VFPA);     // frames, delta_center
+    if (word >= VLI && word < VLI + 3) return JLI + (word - VLI);
+    if (weld) {
+        if (word >= VAI && word < VAI + 3) return JAI + (word - VAI);
+        if (word >= VAM && word < VAM + 9) return JAM + (word - VAM);
+        if (word >= VLS && word < VLS + 3) return JLS + (word - VLS);
+        if (word >= VAS && word < VAS + 3) return JAS + (word - VAS);
+        return -1;
+    }
+    if (word >= VPI && word < VPI + 2) return JPI + (word - VPI);
+    if (word == VSI) return JSI;
+    if (word == VMI) return JMI;
+    if (word == VLOI) return JLOI;
+    if (word == VUPI) return JUPI;
+    if (word >= VAX && word < VAX + 3) return JAX + (word - VAX);
+    if (word >= VPX && word < VPX + 3) return JPX + (word - VPX);
+    if (word >= VPY && word < VPY + 3) return JPY + (word - VPY);
+    if (word == VAXM) return JAXM;
+    if (word >= VSS && word < VSS + 3) return JSS + (word - VSS);
+    return -1;
+}
+static_assert(JFPB == JFPA + 3 && JFQA == JFPB + 3 && JFQB == JFQA + 4 && JDC == JFQB + 4, "joint frame columns");
+static_assert(VFPB == VFPA + 3 && VFQA == VFPB + 3 && VFQB == VFQA + 4 && VDC == VFQB + 4 && VLI == VDC + 3,
+    "joint frame words");
+
+B3X_HD void o_joint_stage(const Args& a, float* slot, OutShared& sh, int q, int t) {
+    const float* src = item(slot + a.SP.joint, q, NJF);
+    for (int idx = t; idx < NJF * kLanes; idx += kCta) sh.u.jstage[idx & 31][idx >> 5] = src[idx];
+}
+
+B3X_HD void o_joint_write(const Args& a, int tile, OutShared& sh, int q, int t) {
+    const int w = t >> 5, i = t & 31;
+    for (int l = w; l < kLanes; l += kCtaWarps) {
+        if (q >= sh.nj[l]) continue;
+        const float* row = sh.u.jstage[l];
+        if (!b3x_f2i(row[JOK])) continue;
+        const bool weld = b3x_f2i(row[JTYPE]) == B3_JOINT_WELD;
+        float* dst = world_words_w(a, tile * kLanes + l) + (a.L.joint_off + (size_t)B3X_JOINT_BYTES * q) / 4;
+        for (int c = i; c < NVW; c += 32) {
+            const int col = joint_source(c, weld);
+            if (col >= 0) dst[c] = row[col];
+        }
+    }
+}
+
+B3X_HD void o_header(const Args& a, int tile, float* slot, OutShared& sh, int l) {
+    if (!sh.live[l]) return;
+    const float* rec = slot + a.SP.rec + l;
+    float* hw = world_words_w(a, tile * kLanes + l);
+    hw[HNC] = COL(rec, RN);
+    hw[HOVC] = COL(rec, ROVF);
+    hw[HDROP] = COL(rec, RDROP);
+}
+
+template <class X>
+B3X_HD void out_tile(X& x, const Args& a, int bt, OutShared& sh) {
+    float* slot = slot_of(a, bt);
+    const int tile = a.tile0 + bt;
+    x.each([&](int t) { if (t < kLanes) o_record(a, slot, sh, t); });
+    x.each([&](int t) { if (t == 0) o_maxima(sh); });
+    for (int k0 = 0; k0 < sh.maxnb; k0 += kCtaWarps) {
+        x.each([&](int t) { o_bodies(a, slot, sh, k0, t); });
+        x.each([&](int t) { o_body_write(a, tile, sh, k0, t); });
+    }
+    for (int k = 0; k < sh.maxn; k++) {
+        x.each([&](int t) { o_contact_stage(a, slot, sh, k, t); });
+        x.each([&](int t) { o_contact_write(a, tile, sh, k, t); });
+    }
+    for (int q = 0; q < sh.maxnj; q++) {
+        x.each([&](int t) { o_joint_stage(a, slot, sh, q, t); });
+        x.each([&](int t) { o_joint_write(a, tile, sh, q, t); });
+    }
+    x.each([&](int t) { if (t < kLanes) o_header(a, tile, slot, sh, t); });
+}
+
+}  // namespace b3x

@@ -1,30 +1,31 @@
 // b3x_step.cu -- batched rigid-body step on B200 (sm_100a) and the exported
 // C-ABI of libpuffysics_b200.so.
 //
-// Mapping.  One thread owns one world; a 32-thread CTA owns a tile of 32
-// consecutive worlds and the grid is persistent (at most SMs x resident CTAs),
-// each CTA walking tiles with a grid stride.  The caller's worlds stay in
-// their AoS B3World layout (the drop-in contract); a step reads each world's
-// header, bodies, shapes, old contacts and joints once, keeps its working
-// state in lane-interleaved structure-of-arrays columns, and writes every
-// field the reference step writes once at the end:
-//   - body state (velocities, pose deltas, inverse mass / inertia, flags) in
-//     shared memory, [body][field][lane], so the per-world dynamic body
-//     indices of the Gauss-Seidel sweeps hit distinct banks;
-//   - shape world poses / AABBs, contacts and joints in a per-CTA workspace
-//     slot in global memory, [item][field][lane]: a warp touching item k of
-//     its 32 worlds reads one contiguous 128-byte line per field, and a slot
-//     is reused tile after tile so it stays resident in L2.
-// No thread communicates with another: there are no barriers, no waits and
-// no atomics, and every loop is bounded by the world's capacities.
+// Mapping.  A tile is 32 consecutive worlds.  A step runs three kernels per
+// chunk of tiles (as many tiles as the device keeps resident), each with one
+// block per tile:
+//   collide_kernel (128 threads)  reads the caller's AoS worlds with
+//       coalesced row transfers, builds the per-lane solver columns of the
+//       tile's workspace slot, runs broadphase and narrowphase spread over
+//       (pair, world) and (candidate, world), and prepares contacts and
+//       joints (b3x_phases.cuh);
+//   solve_kernel (one warp, lane = world)  warm starts and runs the substeps:
+//       Gauss-Seidel sweeps over contacts / joints streamed through shared
+//       memory with TMA bulk copies, body state in shared memory
+//       (b3x_solver.cuh);
+//   out_kernel (128 threads)  finalizes the bodies and writes bodies,
+//       contacts, joints and header counts back to the AoS worlds, again as
+//       coalesced rows (b3x_phases.cuh).
+// Every loop is bounded by the world's capacities; the solver's pipeline
+// waits are bounded and report through b3x_fault_flags().
 //
 // Arithmetic.  The per-world work follows the reference's default
 // b3_step (src/puffysics/09_step.inl:183-258) operation by operation; the
 // library is compiled with -fmad=false and IEEE division / square root so
 // the results equal the reference CPU build (-ffp-contract=off) bit for bit,
 // atan2f (revolute twist) excepted.  Reordering is limited to hoisting pure
-// values (shape world poses, gated inverse masses) and to evaluating the
-// side-effect-free broadphase filters in a cheaper order.
+// values (shape world poses, gated inverse masses, step softness) and to
+// evaluating the side-effect-free broadphase filters in a cheaper order.
 #include <cuda_runtime.h>
 
 #include <cmath>
@@ -35,7 +36,9 @@
 #include <tuple>
 
 #include "puffysics_b200.h"
-#include "b3x_world.cuh"
+#include "b3x_layout.cuh"
+#include "b3x_solver.cuh"
+#include "b3x_phases.cuh"
 
 namespace b3x {
 
@@ -44,35 +47,61 @@ namespace b3x {
 // completed.
 __device__ int g_fault;
 
-// Shared memory of a CTA: the streaming stages, their mbarriers, then the
-// body columns when they live on chip.
-constexpr size_t kStageBytes = (size_t)kStages * kBufWords * kLanes * sizeof(float);
+// Block-wide phase runner: every thread runs the phase, then the block meets.
+struct DevExec {
+    template <class F>
+    __host__ __device__ __forceinline__ void each(F&& f) {
+#if defined(__CUDA_ARCH__)
+        f((int)threadIdx.x);
+        __syncthreads();
+#else
+        (void)f;
+#endif
+    }
+};
+
+__global__ void __launch_bounds__(kCta, 4) collide_kernel(Args a) {
+    __shared__ CollideShared sh;
+    DevExec x;
+    collide_tile(x, a, blockIdx.x, sh);
+}
+
+__global__ void __launch_bounds__(kCta, 4) out_kernel(Args a) {
+    __shared__ OutShared sh;
+    DevExec x;
+    out_tile(x, a, blockIdx.x, sh);
+}
+
+// Shared memory of a solve block: the streaming stages, their mbarriers,
+// then the body columns when they live on chip.
+constexpr size_t kStageBytes = (size_t)kStages * kStreamWords * kLanes * sizeof(float);
 constexpr size_t kBarBytes = 64;
+constexpr int kSolvedBodyFields = BDQ + 4;   // velocities and pose deltas go back
 
 template <bool kBodySmem>
-__global__ void __launch_bounds__(kLanes) step_kernel(StepArgs a) {
+__global__ void __launch_bounds__(kLanes) solve_kernel(Args a) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     const int lane = threadIdx.x;
-    float* slot = a.scratch + (size_t)blockIdx.x * a.slot_words;
-    float* bc = (kBodySmem ? reinterpret_cast<float*>(smem_raw + kStageBytes + kBarBytes) : slot + a.off_bodies)
-        + lane;
-    float* kc = slot + a.off_bconst + lane;
-    float* sc = slot + a.off_shapes + lane;
-    float* cc = slot + a.off_contacts + lane;
-    float* jc = slot + a.off_joints + lane;
+    float* slot = slot_of(a, blockIdx.x);
     Pipe P;
     P.buf = reinterpret_cast<float*>(smem_raw);
     P.bar = reinterpret_cast<uint64_t*>(smem_raw + kStageBytes);
     pipe_init(P);
-    const int ntiles = (a.count + kLanes - 1) / kLanes;
-    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-        int wi = tile * kLanes + lane;
-        bool live = wi < a.count && (!a.active || a.active[wi]);
-        unsigned char* wp = a.data + (size_t)(live ? wi : 0) * a.stride + a.offset;
-        if (!world_step(live, wp, a, bc, kc, sc, cc, jc, P)) {
-            if (lane == 0) atomicExch(&g_fault, 1);
-            return;
-        }
+    float* gb = slot + a.SP.body;
+    float* sb = reinterpret_cast<float*>(smem_raw + kStageBytes + kBarBytes);
+    const int nb = warp_max(ldi(slot + a.SP.rec + lane, RNB));
+    if (kBodySmem) {
+        // each lane copies its own column
+        for (int idx = lane; idx < nb * NBF * kLanes; idx += kLanes) sb[idx] = gb[idx];
+    }
+    float* bc = (kBodySmem ? sb : gb) + lane;
+    if (!solve_world(a, slot, lane, bc, P)) {
+        if (lane == 0) atomicExch(&g_fault, 1);
+        return;
+    }
+    if (kBodySmem) {
+        for (int k = 0; k < nb; k++)
+            for (int f = 0; f < kSolvedBodyFields; f++) COL(gb + lane, BI(k, f)) = COL(sb + lane, BI(k, f));
     }
 }
 
@@ -139,11 +168,11 @@ __global__ void observe_kernel(const unsigned char* data, unsigned long long str
 // ---- host side --------------------------------------------------------------
 struct Plan {
     bool body_smem;
-    int grid_max;             // co-resident CTAs on the device
-    size_t smem_bytes;
-    unsigned long long slot_words;
-    unsigned off_bodies, off_bconst, off_shapes, off_contacts, off_joints;
-    size_t ws_bytes;
+    Space SP;
+    size_t solve_smem;       // dynamic shared memory of a solve block
+    size_t tile_bytes;       // one tile's workspace slot
+    int chunk_tiles;         // tiles per launch with the default workspace
+    size_t ws_bytes;         // the default workspace (chunk_tiles slots)
 };
 
 static std::mutex g_mutex;
@@ -152,6 +181,8 @@ static std::map<std::tuple<int, void*, unsigned long long>, std::pair<void*, siz
 
 // Body columns live in shared memory while they fit comfortably.
 static constexpr size_t kBodySmemLimit = 64 * 1024;
+// Resident blocks per SM the default chunk is sized for.
+static constexpr int kChunkBlocksPerSM = 4;
 
 static cudaError_t make_plan(int dev, unsigned long long sig, const Layout& L, Plan* out) {
     std::lock_guard<std::mutex> lock(g_mutex);
@@ -161,45 +192,27 @@ static cudaError_t make_plan(int dev, unsigned long long sig, const Layout& L, P
         return cudaSuccess;
     }
     Plan p;
-    size_t body_words = (size_t)L.B * NBF * kLanes;
-    p.body_smem = body_words * 4 <= kBodySmemLimit;
-    p.smem_bytes = kStageBytes + kBarBytes + (p.body_smem ? body_words * 4 : 0);
-    unsigned w = 0;
-    p.off_bodies = w;
-    if (!p.body_smem) w += (unsigned)body_words;
-    p.off_bconst = w;
-    w += (unsigned)((size_t)L.B * NKF * kLanes);
-    p.off_shapes = w;
-    w += (unsigned)((size_t)L.S * NSF * kLanes);
-    p.off_contacts = w;
-    w += (unsigned)((size_t)L.C * NCF * kLanes);
-    p.off_joints = w;
-    w += (unsigned)((size_t)L.J * NJF * kLanes);
-    w = (w + 63u) & ~63u;    // 256-byte aligned slots
-    p.slot_words = w;
+    p.SP = space_from_layout(L);
+    size_t body_bytes = (size_t)L.B * NBF * kLanes * sizeof(float);
+    p.body_smem = body_bytes <= kBodySmemLimit;
+    p.solve_smem = kStageBytes + kBarBytes + (p.body_smem ? body_bytes : 0);
+    p.tile_bytes = (size_t)p.SP.tile_words * sizeof(float);
     int sms = 0;
     cudaError_t e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess) return e;
-    int occ = 0;
     // The dynamic shared memory cap is a property of the kernel function, not
     // of a plan: raise it once to the device's opt-in maximum so plans of
     // different capacity configurations never lower it under one another.
     int optin = 0;
     e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     if (e != cudaSuccess) return e;
-    if (p.smem_bytes > (size_t)optin) return cudaErrorInvalidValue;
-    e = cudaFuncSetAttribute(step_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, optin);
+    if (p.solve_smem > (size_t)optin) return cudaErrorInvalidValue;
+    e = cudaFuncSetAttribute(solve_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, optin);
     if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(step_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, optin);
+    e = cudaFuncSetAttribute(solve_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, optin);
     if (e != cudaSuccess) return e;
-    if (p.body_smem)
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, step_kernel<true>, kLanes, p.smem_bytes);
-    else
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, step_kernel<false>, kLanes, p.smem_bytes);
-    if (e != cudaSuccess) return e;
-    if (occ < 1) occ = 1;
-    p.grid_max = sms * occ;
-    p.ws_bytes = (size_t)p.grid_max * p.slot_words * 4;
+    p.chunk_tiles = sms * kChunkBlocksPerSM;
+    p.ws_bytes = (size_t)p.chunk_tiles * p.tile_bytes;
     g_plans[{dev, sig}] = p;
     *out = p;
     return cudaSuccess;
@@ -216,9 +229,10 @@ static bool aligned8(const B3Batch& b) {
     return (((uintptr_t)b.data + b.world_offset) % 8 == 0) && (b.stride % 8 == 0);
 }
 
+// The step over chunks of `chunk` tiles: collide, solve, write-back per chunk.
 static cudaError_t launch_step(const B3Batch& batch, float dt, int substeps, const unsigned char* active,
-        cudaStream_t stream, const Layout& L, int ji, int ri, const Plan& p, void* ws, int grid_limit) {
-    StepArgs a;
+        cudaStream_t stream, const Layout& L, int ji, int ri, const Plan& p, void* ws, int chunk) {
+    Args a;
     a.data = (unsigned char*)batch.data;
     a.stride = batch.stride;
     a.offset = batch.world_offset;
@@ -229,18 +243,20 @@ static cudaError_t launch_step(const B3Batch& batch, float dt, int substeps, con
     a.joint_iters = ji;
     a.relax_iters = ri;
     a.L = L;
-    a.scratch = (float*)ws;
-    a.slot_words = p.slot_words;
-    a.off_bodies = p.off_bodies;
-    a.off_bconst = p.off_bconst;
-    a.off_shapes = p.off_shapes;
-    a.off_contacts = p.off_contacts;
-    a.off_joints = p.off_joints;
-    int ntiles = (batch.count + kLanes - 1) / kLanes;
-    int grid = ntiles < grid_limit ? ntiles : grid_limit;
-    if (p.body_smem) step_kernel<true><<<grid, kLanes, p.smem_bytes, stream>>>(a);
-    else step_kernel<false><<<grid, kLanes, p.smem_bytes, stream>>>(a);
-    return cudaGetLastError();
+    a.SP = p.SP;
+    a.ws = (float*)ws;
+    const int ntiles = (batch.count + kLanes - 1) / kLanes;
+    for (int t0 = 0; t0 < ntiles; t0 += chunk) {
+        const int nt = ntiles - t0 < chunk ? ntiles - t0 : chunk;
+        a.tile0 = t0;
+        collide_kernel<<<nt, kCta, 0, stream>>>(a);
+        if (p.body_smem) solve_kernel<true><<<nt, kLanes, p.solve_smem, stream>>>(a);
+        else solve_kernel<false><<<nt, kLanes, p.solve_smem, stream>>>(a);
+        out_kernel<<<nt, kCta, 0, stream>>>(a);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
 }
 
 }  // namespace b3x
@@ -262,6 +278,15 @@ B3X_API size_t b3x_workspace_bytes(unsigned long long sig, int device) {
     Plan p;
     if (make_plan(device, sig, L, &p) != cudaSuccess) return 0;
     return p.ws_bytes;
+}
+
+B3X_API int b3x_step_launches(unsigned long long sig, int count, int device) {
+    Layout L;
+    if (!layout_from_signature(sig, &L) || count < 0) return 0;
+    Plan p;
+    if (make_plan(device, sig, L, &p) != cudaSuccess) return 0;
+    const int ntiles = (count + kLanes - 1) / kLanes;
+    return 3 * ((ntiles + p.chunk_tiles - 1) / p.chunk_tiles);
 }
 
 static int step_common(B3Batch batch, float dt, int substeps, const unsigned char* active, void* stream,
@@ -294,11 +319,11 @@ static int step_common(B3Batch batch, float dt, int substeps, const unsigned cha
         ws_bytes = p.ws_bytes;
     }
     if (ws == nullptr || ((uintptr_t)ws % 256) != 0) return cudaErrorInvalidValue;
-    // A smaller caller workspace simply runs fewer persistent CTAs.
-    long long slots = (long long)(ws_bytes / (p.slot_words * 4));
+    // A smaller caller workspace simply runs fewer tiles per launch.
+    long long slots = (long long)(ws_bytes / p.tile_bytes);
     if (slots < 1) return cudaErrorInvalidValue;
-    int grid_limit = (int)(slots < p.grid_max ? slots : p.grid_max);
-    return launch_step(batch, dt, substeps, active, (cudaStream_t)stream, L, ji, ri, p, ws, grid_limit);
+    int chunk = (int)(slots < p.chunk_tiles ? slots : p.chunk_tiles);
+    return launch_step(batch, dt, substeps, active, (cudaStream_t)stream, L, ji, ri, p, ws, chunk);
 }
 
 B3X_API int b3x_batch_step_gpu(B3Batch batch, float dt, int substeps, const unsigned char* active, void* stream,
@@ -394,8 +419,8 @@ extern "C" {
 // whose launches overlap on the GPU (different streams, no ordering between
 // them) race on it and must not be issued.  A capacity configuration whose
 // per-CTA workspace slot exceeds 64 MiB is rejected with
-// cudaErrorInvalidValue; smaller ones run as many persistent CTAs as slots fit
-// (at most the device's resident CTAs), so any batch size is accepted.
+// cudaErrorInvalidValue; smaller ones run as many tiles per launch as slots
+// fit (at most the device's resident blocks), so any batch size is accepted.
 B3X_API int b3x_batch_step_gpu_noalloc(B3Batch batch, float dt, int substeps, const unsigned char* active,
         void* stream, unsigned long long sig, int ji, int ri) {
     Layout L;
@@ -418,7 +443,7 @@ B3X_API int b3x_batch_step_gpu_noalloc(B3Batch batch, float dt, int substeps, co
     Plan p;
     e = make_plan(dev, sig, L, &p);
     if (e != cudaSuccess) return e;
-    if (p.slot_words * 4 > kNoAllocScratchBytes) return cudaErrorInvalidValue;
+    if (p.tile_bytes > kNoAllocScratchBytes) return cudaErrorInvalidValue;
     return step_common(batch, dt, substeps, active, stream, sig, ji, ri, ptr, kNoAllocScratchBytes, false);
 }
 

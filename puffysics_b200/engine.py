@@ -51,6 +51,8 @@ def lib():
         L.b3x_batch_step_gpu_noalloc.restype = ctypes.c_int
         L.b3x_workspace_bytes.argtypes = [ctypes.c_ulonglong, ctypes.c_int]
         L.b3x_workspace_bytes.restype = ctypes.c_size_t
+        L.b3x_step_launches.argtypes = [ctypes.c_ulonglong, ctypes.c_int, ctypes.c_int]
+        L.b3x_step_launches.restype = ctypes.c_int
         L.b3x_batch_restore_gpu.argtypes = [B3Batch, vp, u8p, vp, ctypes.c_ulonglong]
         L.b3x_batch_restore_gpu.restype = ctypes.c_int
         L.b3x_batch_apply_gpu.argtypes = [B3Batch, ctypes.c_int, ctypes.c_int, vp, ctypes.c_int, u8p, vp,
@@ -118,6 +120,11 @@ def batch_observe_gpu(worlds, body, out, stream=None, caps=None, stride=None, of
 
 def workspace_bytes(caps, device=0):
     return lib().b3x_workspace_bytes(layout.signature(*caps), device)
+
+
+def step_launches(caps, count, device=0):
+    """Kernel launches of one batch_step_gpu call over `count` worlds."""
+    return lib().b3x_step_launches(layout.signature(*caps), count, device)
 
 
 def world_bytes(caps):
