@@ -77,8 +77,6 @@ enum : int { BV = 0, BW = 3, BDP = 6, BDQ = 9, BMI = 13, BII = 14, BFLAGS = 23, 
 // per-body step constants: velocity / spin increments and damping factors
 // of b3_integrate_velocity_state, constant over the substeps
 enum : int { KDV = 0, KDW = 3, KLD = 6, KAD = 7, NKF = 8 };
-// body pose and the fields the finalize needs
-enum : int { PPOS = 0, PROT = 3, PCEN = 7, PLC = 10, PII = 13, NPF = 16 };
 // shape: world pose, padded AABB, geometry, filter, material
 enum : int {
     SPOS = 0, SROT = 3, SLO = 7, SHI = 10, STYPE = 13, SBODY = 14, SRAD = 15, SHALF = 16, SCAT = 19, SMASK = 21,
@@ -89,14 +87,13 @@ enum : int { OSA = 0, OSB = 1, OCNT = 2, OFI = 3, OTWI = 5, ORI = 6, OFEAT = 9, 
 // narrowphase result of one candidate pair, already relative to the body
 // centers (the reference's b3_contact_from_mani, 08_contacts.inl:5-39)
 enum : int { MCNT = 0, MN = 1, MP = 4, MRA = 0, MRB = 3, MBSEP = 6, MFEAT = 7, NMP = 8, NMF = MP + 4 * NMP };
-// joints: the solver's columns [0, kJointStream), then what only the
-// write-back reads
+// joints: the solver's columns [0, kJointStream), then the collide filter's
+// collide_connected flag
 enum : int {
     JTYPE = 0, JBA = 1, JBB = 2, JFIX = 3, JENS = 4, JENM = 5, JENL = 6, JFPA = 7, JFPB = 10, JFQA = 13,
     JFQB = 17, JDC = 21, JSOFT = 24, JLI = 27, JAI = 30, JAM = 33, JLH = 42, JAH = 43, JLS = 44, JAS = 47,
     JPI = 50, JSI = 52, JMI = 53, JLOI = 54, JUPI = 55, JMMT = 56, JMS = 57, JTA = 58, JLA = 59, JUA = 60,
-    JAX = 61, JPX = 64, JPY = 67, JAXM = 70, JSS = 71, JOK = 74,
-    JCC = 75, JIMA = 76, JIMB = 77, JIIA = 78, JIIB = 87, NJF = 96
+    JAX = 61, JPX = 64, JPY = 67, JAXM = 70, JSS = 71, JOK = 74, JCC = 75, NJF = 76
 };
 constexpr int kJointStream = JOK + 1;
 constexpr int kStreamWords = kContactStream > kJointStream ? kContactStream : kJointStream;
@@ -136,8 +133,11 @@ static inline bool layout_from_signature(unsigned long long sig, Layout* L) {
 }
 
 // Word offsets of the regions of one tile's workspace slot.
+// Besides the solver columns, the raw B3Body rows (bimg, [body][word][lane])
+// and the prepared B3Joint rows (jimg) travel from the collide kernel to the
+// write-back, which then writes whole rows.
 struct Space {
-    unsigned long long rec, body, konst, pose, shape, old, cand, cont, joint, tile_words;
+    unsigned long long rec, body, konst, bimg, shape, old, cand, cont, joint, jimg, tile_words;
 };
 
 static inline Space space_from_layout(const Layout& L) {
@@ -151,12 +151,13 @@ static inline Space space_from_layout(const Layout& L) {
     s.rec = take(1, NRF);
     s.body = take(L.B, NBF);
     s.konst = take(L.B, NKF);
-    s.pose = take(L.B, NPF);
+    s.bimg = take(L.B, NYW);
     s.shape = take(L.S, NSF);
     s.old = take(L.C, NOF);
     s.cand = take(kPairWindow, NMF);
     s.cont = take(L.C, NCW);
     s.joint = take(L.J, NJF);
+    s.jimg = take(L.J, NVW);
     s.tile_words = (w + 63) & ~63ull;   // 256-byte aligned slots
     return s;
 }
@@ -261,6 +262,21 @@ B3X_HDI void shared_max(int* p, int v) {
     atomicMax(p, v);
 #else
     if (v > *p) *p = v;
+#endif
+}
+// 4-byte asynchronous copy global -> shared (cp.async); the copies of a
+// thread complete at async_wait(), and a block barrier then publishes them.
+B3X_HDI void async_copy4(float* dst_shared, const float* src_global) {
+#if defined(__CUDA_ARCH__)
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"((uint32_t)__cvta_generic_to_shared(dst_shared)),
+                 "l"(__cvta_generic_to_global(src_global)) : "memory");
+#else
+    *dst_shared = *src_global;
+#endif
+}
+B3X_HDI void async_wait() {
+#if defined(__CUDA_ARCH__)
+    asm volatile("cp.async.wait_all;" ::: "memory");
 #endif
 }
 B3X_HDI void shared_or(uint32_t* p, uint32_t v) {

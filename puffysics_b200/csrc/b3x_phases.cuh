@@ -32,7 +32,7 @@ constexpr int kRow = NYW + 1;        // staged struct row (odd: conflict-free co
 // ---- block state ------------------------------------------------------------------
 struct CollideShared {
     int live[kLanes], nb[kLanes], ns[kLanes], oldn[kLanes], nj[kLanes];
-    int n[kLanes], ovf[kLanes], drop[kLanes], cursor[kLanes], sorted[kLanes];
+    int n[kLanes], nbase[kLanes], ovf[kLanes], drop[kLanes], sorted[kLanes];
     float grav[kLanes][3];
     int maxnb, maxns, maxold, maxnj;
     // pair window: candidate bits per world over the window's pairs, and the
@@ -44,12 +44,9 @@ struct CollideShared {
     uint32_t wmask[kPairWindow];                 // worlds with more than ci candidates
     int off[kPairWindow + 1];
     int maxc, total;
-    int16_t kslot[kPairWindow][kLanes];          // contact slot of candidate (ci, l), -1 none
-    int16_t mfirst[kPairWindow][kLanes];         // warm-cache entries to match, [first, end)
-    int16_t mend[kPairWindow][kLanes];
     union {
         float stage[kCtaWarps][kLanes][kRow];    // gathered struct rows, [item][world][word]
-        float jstage[kLanes][NVW + 2];           // one joint of every world
+        float jstage[kLanes][NVW];               // one joint of every world (115: odd)
         float clip[48 * kCta];                   // narrowphase clip polygons
     } u;
 };
@@ -57,11 +54,10 @@ struct CollideShared {
 struct OutShared {
     int live[kLanes], nb[kLanes], n[kLanes], nj[kLanes];
     int maxnb, maxn, maxnj;
-    uint8_t bpred[kCtaWarps][kLanes];
     union {
         float bstage[kCtaWarps][kLanes][kRow];   // finalized body rows
         float cstage[kLanes][NCW];               // one contact of every world (119: odd)
-        float jstage[kLanes][NJF + 1];           // one joint column block (97: odd)
+        float jstage[kLanes][NVW];               // one joint of every world (115: odd)
     } u;
 };
 
@@ -81,25 +77,29 @@ B3X_HDI int nth_bit64(const uint32_t* m, int n) {
 
 // ================================ collide ==========================================
 
-// Header of each world (warp w: worlds w, w+4, ...; lane = header word).
+// Header of each world (warp w: worlds w, w+4, ...; lane = header word),
+// copied asynchronously so all of a thread's loads are in flight at once.
 B3X_HD void c_header(const Args& a, int tile, CollideShared& sh, int t) {
     const int w = t >> 5, i = t & 31;
     if (t == 0) sh.maxnb = sh.maxns = sh.maxold = sh.maxnj = 0;
-    for (int l = w; l < kLanes; l += kCtaWarps) {
-        int wi = tile * kLanes + l;
-        bool live = wi < a.count && (!a.active || a.active[wi]);
-        if (i == 0) sh.live[l] = live;
-        if (live && i < NHW) sh.u.stage[0][l][i] = ldg(world_words(a, wi) + i);
+    if (i < NHW) {
+        for (int l = w; l < kLanes; l += kCtaWarps) {
+            int wi = tile * kLanes + l;
+            if (wi < a.count) async_copy4(&sh.u.stage[0][l][i], world_words(a, wi) + i);
+        }
     }
+    async_wait();
 }
 
 // Clamped counts and the step's per-world constants (09_step.inl:148-157).
 // Counts beyond the capacities would index past the arrays in the
 // reference; here they are clamped so a corrupt world cannot fault.
-B3X_HD void c_record(const Args& a, float* slot, CollideShared& sh, int l) {
+B3X_HD void c_record(const Args& a, int tile, float* slot, CollideShared& sh, int l) {
     const Layout& L = a.L;
     const float* hw = sh.u.stage[0][l];
-    const int live = sh.live[l];
+    const int wi = tile * kLanes + l;
+    const int live = wi < a.count && (!a.active || a.active[wi]);
+    sh.live[l] = live;
     const int nb = live ? clampi(b3x_f2i(hw[HNB]), 0, L.B) : 0;
     const int ns = live ? clampi(b3x_f2i(hw[HNS]), 0, L.S) : 0;
     const int oldn = live ? clampi(b3x_f2i(hw[HNC]), 0, L.C) : 0;
@@ -111,7 +111,6 @@ B3X_HD void c_record(const Args& a, float* slot, CollideShared& sh, int l) {
     sh.n[l] = 0;
     sh.ovf[l] = live ? b3x_f2i(hw[HOVC]) : 0;
     sh.drop[l] = live ? b3x_f2i(hw[HDROP]) : 0;
-    sh.cursor[l] = 0;
     for (int c = 0; c < 3; c++) sh.grav[l][c] = live ? hw[HGRAV + c] : 0.0f;
     shared_max(&sh.maxnb, nb);
     shared_max(&sh.maxns, ns);
@@ -145,8 +144,9 @@ B3X_HD void c_gather(const Args& a, int tile, CollideShared& sh, const int* coun
     for (int l = 0; l < kLanes; l++) {
         if (k >= count[l]) continue;
         const float* src = world_words(a, tile * kLanes + l) + (base + (size_t)size * k) / 4;
-        for (int c = i; c < words; c += 32) sh.u.stage[w][l][c] = ldg(src + c);
+        for (int c = i; c < words; c += 32) async_copy4(&sh.u.stage[w][l][c], src + c);
     }
+    async_wait();
 }
 
 // Body k0 + w of world l: solver columns, step constants and pose
@@ -158,7 +158,7 @@ B3X_HD void c_bodies(const Args& a, float* slot, CollideShared& sh, int k0, int 
     const float* y = sh.u.stage[w][l];
     const float h = a.dt / (float)a.substeps;
     float* bc = item(slot + a.SP.body, k, NBF) + l;
-    float* pc = item(slot + a.SP.pose, k, NPF) + l;
+    float* ic = item(slot + a.SP.bimg, k, NYW) + l;
     const int type = b3x_f2i(y[YTYPE]);
     auto v3 = [&](int f) { return b3_v(y[f], y[f + 1], y[f + 2]); };
     st3(bc, BV, v3(YLV));
@@ -186,11 +186,7 @@ B3X_HD void c_bodies(const Args& a, float* slot, CollideShared& sh, int k0, int 
         COL(bc, BMI) = 0.0f;
         stm(bc, BII, m3_zero());
     }
-    st3(pc, PPOS, v3(YPOS));
-    stq(pc, PROT, b3_q(y[YROT], y[YROT + 1], y[YROT + 2], y[YROT + 3]));
-    st3(pc, PCEN, v3(YCEN));
-    st3(pc, PLC, v3(YLC));
-    st3(pc, PII, v3(YII));
+    for (int f = 0; f < NYW; f++) COL(ic, f) = y[f];
 }
 
 // Shape k0 + w of world l: world pose and padded AABB (04_world.inl:293-336,
@@ -220,9 +216,9 @@ B3X_HD void c_shapes(const Args& a, float* slot, CollideShared& sh, int k0, int 
         st3(so, SHI, b3_v(-INFINITY, -INFINITY, -INFINITY));
         return;
     }
-    const float* pc = item(slot + a.SP.pose, body, NPF) + l;
-    const B3Vec3 bp = ld3(pc, PPOS);
-    const B3Quat bq = ldq(pc, PROT);
+    const float* ic = item(slot + a.SP.bimg, body, NYW) + l;
+    const B3Vec3 bp = ld3(ic, YPOS);
+    const B3Quat bq = ldq(ic, YROT);
     const B3Vec3 p = b3_xf_point(bp, bq, b3_v(y[XLPOS], y[XLPOS + 1], y[XLPOS + 2]));
     const B3Quat q = b3_qmul(bq, b3_q(y[XLROT], y[XLROT + 1], y[XLROT + 2], y[XLROT + 3]));
     B3Vec3 lo, hi;
@@ -261,13 +257,14 @@ B3X_HDI int old_word(int i) {
 
 B3X_HD void c_old_gather(const Args& a, int tile, CollideShared& sh, int k0, int t) {
     const int w = t >> 5, i = t & 31, k = k0 + w;
-    if (i >= NOF) return;
+    if (i >= NOF) return;   // (no copies of its own: nothing to wait for)
     const int word = old_word(i);
     for (int l = 0; l < kLanes; l++) {
         if (k >= sh.oldn[l]) continue;
         const float* src = world_words(a, tile * kLanes + l) + (a.L.contact_off + (size_t)B3X_CONTACT_BYTES * k) / 4;
-        sh.u.stage[w][l][i] = ldg(src + word);
+        async_copy4(&sh.u.stage[w][l][i], src + word);
     }
+    async_wait();
 }
 
 B3X_HD void c_old(const Args& a, float* slot, CollideShared& sh, int k0, int t) {
@@ -298,19 +295,27 @@ B3X_HD void c_joint_gather(const Args& a, int tile, CollideShared& sh, int q, in
     for (int l = w; l < kLanes; l += kCtaWarps) {
         if (q >= sh.nj[l]) continue;
         const float* src = world_words(a, tile * kLanes + l) + (a.L.joint_off + (size_t)B3X_JOINT_BYTES * q) / 4;
-        for (int c = i; c < NVW; c += 32) sh.u.jstage[l][c] = ldg(src + c);
+        for (int c = i; c < NVW; c += 32) async_copy4(&sh.u.jstage[l][c], src + c);
     }
+    async_wait();
 }
 
-// Prepare joint q of world l (06_joints.inl:161-202); invalid body indices
-// make the joint inert (the reference would index out of bounds).
+// Prepare joint q of world l (06_joints.inl:161-202): the solver columns, and
+// the B3Joint row with the prepared fields in place (jimg) for the write-back.
+// Invalid body indices make the joint inert (the reference would index out
+// of bounds).
 B3X_HD void c_joint(const Args& a, float* slot, CollideShared& sh, int q, int l) {
     if (q >= sh.nj[l]) return;
-    const float* y = sh.u.jstage[l];
+    float* y = sh.u.jstage[l];
     auto v3 = [&](int f) { return b3_v(y[f], y[f + 1], y[f + 2]); };
     auto v4 = [&](int f) { return b3_q(y[f], y[f + 1], y[f + 2], y[f + 3]); };
+    auto put3 = [&](int f, B3Vec3 v) { y[f] = v.x; y[f + 1] = v.y; y[f + 2] = v.z; };
+    auto put4 = [&](int f, B3Quat v) { y[f] = v.v.x; y[f + 1] = v.v.y; y[f + 2] = v.v.z; y[f + 3] = v.s; };
+    auto putm = [&](int f, const B3Mat3& m) { put3(f, m.cx); put3(f + 3, m.cy); put3(f + 6, m.cz); };
+    auto puts = [&](int f, B3Soft v) { y[f] = v.bias_rate; y[f + 1] = v.mass_scale; y[f + 2] = v.impulse_scale; };
     const float h = a.dt / (float)a.substeps;
     float* jo = item(slot + a.SP.joint, q, NJF) + l;
+    float* ji = item(slot + a.SP.jimg, q, NVW) + l;
     const int type = b3x_f2i(y[VTYPE]), ja = b3x_f2i(y[VBA]), jb = b3x_f2i(y[VBB]);
     const int nb = sh.nb[l];
     sti(jo, JTYPE, type);
@@ -324,22 +329,18 @@ B3X_HD void c_joint(const Args& a, float* slot, CollideShared& sh, int q, int l)
     sti(jo, JOK, 1);
     const float* bca = item(slot + a.SP.body, ja, NBF) + l;
     const float* bcb = item(slot + a.SP.body, jb, NBF) + l;
-    const float* pa = item(slot + a.SP.pose, ja, NPF) + l;
-    const float* pb = item(slot + a.SP.pose, jb, NPF) + l;
+    const float* ia_img = item(slot + a.SP.bimg, ja, NYW) + l;
+    const float* ib_img = item(slot + a.SP.bimg, jb, NYW) + l;
     const float ma = COL(bca, BMI), mb = COL(bcb, BMI);
     const B3Mat3 ia = ldm(bca, BII), ib = ldm(bcb, BII);
     const B3Mat3 isum = m3_add(ia, ib);
     const int fixed = b3_dot(isum.cx, b3_cross(isum.cy, isum.cz)) < 1.0e-20f;
     const B3Soft soft = make_soft(y[VCHZ], y[VCDMP], h);
-    const B3Quat rot_a = ldq(pa, PROT), rot_b = ldq(pb, PROT);
+    const B3Quat rot_a = ldq(ia_img, YROT), rot_b = ldq(ib_img, YROT);
     const B3Quat fqa = b3_qmul(rot_a, v4(VLRA)), fqb = b3_qmul(rot_b, v4(VLRB));
-    const B3Vec3 fpa = b3_rotate(rot_a, b3_sub(v3(VLAA), ld3(pa, PLC)));
-    const B3Vec3 fpb = b3_rotate(rot_b, b3_sub(v3(VLAB), ld3(pb, PLC)));
-    const B3Vec3 dc = b3_sub(ld3(pb, PCEN), ld3(pa, PCEN));
-    COL(jo, JIMA) = ma;
-    COL(jo, JIMB) = mb;
-    stm(jo, JIIA, ia);
-    stm(jo, JIIB, ib);
+    const B3Vec3 fpa = b3_rotate(rot_a, b3_sub(v3(VLAA), ld3(ia_img, YLC)));
+    const B3Vec3 fpb = b3_rotate(rot_b, b3_sub(v3(VLAB), ld3(ib_img, YLC)));
+    const B3Vec3 dc = b3_sub(ld3(ib_img, YCEN), ld3(ia_img, YCEN));
     sti(jo, JFIX, fixed);
     sts(jo, JSOFT, soft);
     stq(jo, JFQA, fqa);
@@ -348,16 +349,31 @@ B3X_HD void c_joint(const Args& a, float* slot, CollideShared& sh, int q, int l)
     st3(jo, JFPB, fpb);
     st3(jo, JDC, dc);
     st3(jo, JLI, v3(VLI));
+    y[VIMA] = ma;
+    y[VIMB] = mb;
+    putm(VIIA, ia);
+    putm(VIIB, ib);
+    y[VFIX] = b3x_i2f(fixed);
+    puts(VSOFT, soft);
+    put4(VFQA, fqa);
+    put4(VFQB, fqb);
+    put3(VFPA, fpa);
+    put3(VFPB, fpb);
+    put3(VDC, dc);
     if (type == B3_JOINT_WELD) {
         const float lh = y[VLHZ], ah = y[VAHZ];
         const B3Soft ls = lh == 0.0f ? soft : make_soft(lh, y[VLDMP], h);
         const B3Soft as = ah == 0.0f ? soft : make_soft(ah, y[VADMP], h);
-        stm(jo, JAM, m3_inv(isum));
+        const B3Mat3 am = m3_inv(isum);
+        stm(jo, JAM, am);
         COL(jo, JLH) = lh;
         COL(jo, JAH) = ah;
         sts(jo, JLS, ls);
         sts(jo, JAS, as);
         st3(jo, JAI, v3(VAI));
+        putm(VAM, am);
+        puts(VLS, ls);
+        puts(VAS, as);
     } else {
         const B3Vec3 axis = b3_rotate(fqa, b3_v(0.0f, 0.0f, 1.0f));
         const float kx = b3_dot(axis, b3_mv(isum, axis));
@@ -365,11 +381,12 @@ B3X_HD void c_joint(const Args& a, float* slot, CollideShared& sh, int q, int l)
         const B3Quat rel = b3_qinv_mul(fqa, fqb);
         B3Vec3 px, py;
         hinge_perps(fqa, rel, &px, &py);
+        const B3Soft sps = make_soft(y[VHZ], y[VDR], h);
         st3(jo, JAX, axis);
         COL(jo, JAXM) = axm;
         st3(jo, JPX, px);
         st3(jo, JPY, py);
-        sts(jo, JSS, make_soft(y[VHZ], y[VDR], h));
+        sts(jo, JSS, sps);
         COL(jo, JENS) = y[VENS];
         COL(jo, JENM) = y[VENM];
         COL(jo, JENL) = y[VENL];
@@ -385,7 +402,13 @@ B3X_HD void c_joint(const Args& a, float* slot, CollideShared& sh, int q, int l)
         COL(jo, JLA) = y[VLA];
         COL(jo, JUA) = y[VUA];
         if (type != B3_JOINT_REVOLUTE) st3(jo, JAI, v3(VAI));
+        put3(VAX, axis);
+        y[VAXM] = axm;
+        put3(VPX, px);
+        put3(VPY, py);
+        puts(VSS, sps);
     }
+    for (int f = 0; f < NVW; f++) COL(ji, f) = y[f];
 }
 
 // -- pair windows -----------------------------------------------------------------
@@ -505,9 +528,9 @@ B3X_HD void c_narrow(const Args& a, float* slot, CollideShared& sh, int t) {
         collide(m, ga, gb, P);
         if (m.count == 0) continue;
         shared_or(&sh.nmask[l][ci >> 5], 1u << (ci & 31));
-        const float* pc = slot + a.SP.pose + l;
-        const B3Vec3 ca = ld3(item(pc, ldi(si, SBODY), NPF), PCEN);
-        const B3Vec3 cb = ld3(item(pc, ldi(sj, SBODY), NPF), PCEN);
+        const float* ic = slot + a.SP.bimg + l;
+        const B3Vec3 ca = ld3(item(ic, ldi(si, SBODY), NYW), YCEN);
+        const B3Vec3 cb = ld3(item(ic, ldi(sj, SBODY), NYW), YCEN);
         float* md = item(slot + a.SP.cand, ci, NMF) + l;
         sti(md, MCNT, m.count);
         st3(md, MN, m.normal);
@@ -523,46 +546,55 @@ B3X_HD void c_narrow(const Args& a, float* slot, CollideShared& sh, int t) {
     }
 }
 
-// Contact slots and warm-cache ranges of world l's candidates, in the
-// reference's order (08_contacts.inl:120-171): slots are handed out while the
-// capacity lasts, then overflow is counted; the old cache is walked with the
-// merge cursor when its keys are sorted.
-B3X_HD void c_rank(const Args& a, float* slot, CollideShared& sh, int l) {
-    const float* oc = slot + a.SP.old + l;
-    int n = sh.n[l], ovf = sh.ovf[l], drop = sh.drop[l], cursor = sh.cursor[l];
-    const int on = sh.oldn[l], sorted = sh.sorted[l], cnt = sh.ccount[l];
-    for (int ci = 0; ci < cnt; ci++) {
-        sh.kslot[ci][l] = -1;
-        if (!((sh.nmask[l][ci >> 5] >> (ci & 31)) & 1u)) continue;
-        if (n >= a.L.C) {
-            ovf = 1;
-            drop++;
-            continue;
-        }
-        sh.kslot[ci][l] = (int16_t)n++;
-        const int pr = sh.ptab[nth_bit64(sh.cmask[l], ci)];
-        const int i = pr & 0xffff, j = pr >> 16;
-        int first = 0, end = on;
-        if (sorted) {
-            while (cursor < on) {
-                const float* o = item(oc, cursor, NOF);
-                const int sa = ldi(o, OSA), sb = ldi(o, OSB);
-                if (sa < i || (sa == i && sb < j)) cursor++;
-                else break;
-            }
-            first = cursor;
-            end = cursor < on ? cursor + 1 : on;
-        }
-        sh.mfirst[ci][l] = (int16_t)first;
-        sh.mend[ci][l] = (int16_t)end;
+// Contact slots of world l's candidates in this window (08_contacts.inl:120-134):
+// in candidate order, slots are handed out while the capacity lasts, then
+// overflow is counted.  Candidate ci with a manifold gets slot nbase + (number
+// of earlier candidates with a manifold) when that is below the capacity.
+B3X_HD void c_slots(const Args& a, CollideShared& sh, int l) {
+    int ne = 0;
+    for (int c = 0; c < kPairWindow / 32; c++) ne += popc32(sh.nmask[l][c]);
+    const int n0 = sh.n[l];
+    const int room = a.L.C - n0 > 0 ? a.L.C - n0 : 0;
+    const int kept = ne < room ? ne : room;
+    sh.nbase[l] = n0;
+    sh.n[l] = n0 + kept;
+    if (ne > kept) {
+        sh.ovf[l] = 1;
+        sh.drop[l] += ne - kept;
     }
-    sh.n[l] = n;
-    sh.ovf[l] = ovf;
-    sh.drop[l] = drop;
-    sh.cursor[l] = cursor;
 }
 
-// Build contact kslot of world l from its candidate: b3_contact_from_mani
+// Number of set bits of a window mask below bit ci.
+B3X_HDI int rank_below(const uint32_t* m, int ci) {
+    if (ci < 32) return popc32(m[0] & ((1u << ci) - 1u));
+    return popc32(m[0]) + popc32(m[1] & ((1u << (ci - 32)) - 1u));
+}
+
+// Warm-cache entries to match for the key (i, j) (08_contacts.inl:136-153):
+// with strictly increasing old keys the reference's merge cursor stands, for
+// each contact it keeps, on the first old entry not below the contact's key
+// (keys of kept contacts increase, so the cursor is that lower bound whatever
+// the candidates before); it matches [cursor, cursor + 1).  Otherwise every
+// entry is scanned.
+B3X_HDI void warm_range(const float* oc, int on, int sorted, int i, int j, int& first, int& end) {
+    if (!sorted) {
+        first = 0;
+        end = on;
+        return;
+    }
+    int lo = 0, hi = on;
+    while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        const float* o = item(oc, mid, NOF);
+        const int sa = ldi(o, OSA), sb = ldi(o, OSB);
+        if (sa < i || (sa == i && sb < j)) lo = mid + 1;
+        else hi = mid;
+    }
+    first = lo;
+    end = lo < on ? lo + 1 : on;
+}
+
+// Build the contact of candidate (ci, l) from its manifold: b3_contact_from_mani
 // (08_contacts.inl:5-39), the warm-start carry (08_contacts.inl:136-171) and
 // b3_prepare_one_contact (08_contacts.inl:234-291).  All 119 words except the
 // point slots past the point count go to the contact's workspace columns.
@@ -571,8 +603,9 @@ B3X_HD void c_prepare(const Args& a, float* slot, CollideShared& sh, int t) {
     for (int idx = t; idx < sh.total; idx += kCta) {
         int ci, l;
         decode(sh, idx, ci, l);
-        const int k = sh.kslot[ci][l];
-        if (k < 0) continue;
+        if (!((sh.nmask[l][ci >> 5] >> (ci & 31)) & 1u)) continue;
+        const int k = sh.nbase[l] + rank_below(sh.nmask[l], ci);
+        if (k >= a.L.C) continue;
         const int pr = sh.ptab[nth_bit64(sh.cmask[l], ci)];
         const int i = pr & 0xffff, j = pr >> 16;
         const float* si = item(sc, i, NSF) + l;
@@ -602,7 +635,9 @@ B3X_HD void c_prepare(const Args& a, float* slot, CollideShared& sh, int t) {
         float twi = 0.0f;
         B3Vec3 ri = b3_v(0.0f, 0.0f, 0.0f);
         const float* oc = slot + a.SP.old + l;
-        for (int kk = sh.mfirst[ci][l]; kk < sh.mend[ci][l]; kk++) {
+        int first, end;
+        warm_range(oc, sh.oldn[l], sh.sorted[l], i, j, first, end);
+        for (int kk = first; kk < end; kk++) {
             const float* o = item(oc, kk, NOF);
             if (ldi(o, OSA) != i || ldi(o, OSB) != j) continue;
             const int ocnt = clampi(ldi(o, OCNT), 0, B3_MAX_MANIFOLD);
@@ -709,7 +744,7 @@ B3X_HD void collide_tile(X& x, const Args& a, int bt, CollideShared& sh) {
     float* slot = slot_of(a, bt);
     const int tile = a.tile0 + bt;
     x.each([&](int t) { c_header(a, tile, sh, t); });
-    x.each([&](int t) { if (t < kLanes) c_record(a, slot, sh, t); });
+    x.each([&](int t) { if (t < kLanes) c_record(a, tile, slot, sh, t); });
     for (int k0 = 0; k0 < sh.maxnb; k0 += kCtaWarps) {
         x.each([&](int t) { c_gather(a, tile, sh, sh.nb, k0, B3X_WORLD_HEADER_BYTES, B3X_BODY_BYTES, NYW, t); });
         x.each([&](int t) { c_bodies(a, slot, sh, k0, t); });
@@ -737,7 +772,7 @@ B3X_HD void collide_tile(X& x, const Args& a, int bt, CollideShared& sh) {
         x.each([&](int t) { if (t == 0) c_prefix(sh); });
         if (sh.total == 0) continue;
         x.each([&](int t) { c_narrow(a, slot, sh, t); });
-        x.each([&](int t) { if (t < kLanes) c_rank(a, slot, sh, t); });
+        x.each([&](int t) { if (t < kLanes) c_slots(a, sh, t); });
         x.each([&](int t) { c_prepare(a, slot, sh, t); });
     }
     x.each([&](int t) { if (t < kLanes) c_finish(a, slot, sh, t); });
@@ -765,73 +800,57 @@ B3X_HD void o_maxima(OutShared& sh) {
     sh.maxnj = mj;
 }
 
-// Finalize body k0 + w of world l (09_step.inl:109-130) into a staged B3Body
-// row; bpred says which word groups the reference writes for it.
-enum : uint8_t { OB_VEL = 1, OB_POSE = 2, OB_INVI = 4 };
-
+// Finalize body k0 + w of world l (09_step.inl:109-130) into its B3Body row:
+// the raw row read by the collide kernel with the fields the reference's
+// step writes replaced, so the write-back stores whole rows.
 B3X_HD void o_bodies(const Args& a, float* slot, OutShared& sh, int k0, int t) {
     const int w = t >> 5, l = t & 31, k = k0 + w;
     if (k >= sh.nb[l]) return;
     const float* bc = item(slot + a.SP.body, k, NBF) + l;
-    const float* pc = item(slot + a.SP.pose, k, NPF) + l;
+    const float* ic = item(slot + a.SP.bimg, k, NYW) + l;
     float* y = sh.u.bstage[w][l];
+    for (int f = 0; f < NYW; f++) y[f] = COL(ic, f);
     auto put3 = [&](int f, B3Vec3 v) { y[f] = v.x; y[f + 1] = v.y; y[f + 2] = v.z; };
     auto put4 = [&](int f, B3Quat q) { y[f] = q.v.x; y[f + 1] = q.v.y; y[f + 2] = q.v.z; y[f + 3] = q.s; };
     const int type = ldi(bc, BTYPE);
     const bool dyn_flag = (b3x_f2u(COL(bc, BFLAGS)) & B3_FLAG_DYNAMIC) != 0;
-    uint8_t pred = 0;
     if (type != B3_STATIC || dyn_flag) {
         put3(YLV, ld3(bc, BV));
         put3(YAV, ld3(bc, BW));
-        pred |= OB_VEL;
     }
     if (type != B3_STATIC) {
-        const B3Vec3 center = b3_add(ld3(pc, PCEN), ld3(bc, BDP));
-        const B3Quat rot = b3_qnorm(b3_qmul(ldq(bc, BDQ), ldq(pc, PROT)));
+        const B3Vec3 center = b3_add(ld3(ic, YCEN), ld3(bc, BDP));
+        const B3Quat rot = b3_qnorm(b3_qmul(ldq(bc, BDQ), ldq(ic, YROT)));
         put3(YCEN, center);
         put4(YROT, rot);
-        put3(YPOS, b3_sub(center, b3_rotate(rot, ld3(pc, PLC))));
+        put3(YPOS, b3_sub(center, b3_rotate(rot, ld3(ic, YLC))));
         put3(YDP, b3_v(0.0f, 0.0f, 0.0f));
         put4(YDQ, b3_q_id());
         put3(YF, b3_v(0.0f, 0.0f, 0.0f));
         put3(YT, b3_v(0.0f, 0.0f, 0.0f));
-        pred |= OB_POSE;
         if (type == B3_DYNAMIC) {
-            const B3Mat3 iw = b3_world_inv_i(rot, ld3(pc, PII));
+            const B3Mat3 iw = b3_world_inv_i(rot, ld3(ic, YII));
             put3(YIW, iw.cx);
             put3(YIW + 3, iw.cy);
             put3(YIW + 6, iw.cz);
-            pred |= OB_INVI;
         }
     }
-    sh.bpred[w][l] = pred;
-}
-
-B3X_HDI bool body_word_written(int word, uint8_t pred) {
-    if (word < YLC) return pred & OB_POSE;
-    if (word < YLV) return false;
-    if (word < YF) return pred & OB_VEL;
-    if (word < YIM) return pred & OB_POSE;
-    if (word < YIW) return false;
-    if (word < YLD) return pred & OB_INVI;
-    return false;
 }
 
 B3X_HD void o_body_write(const Args& a, int tile, OutShared& sh, int k0, int t) {
     const int w = t >> 5, i = t & 31, k = k0 + w;
     for (int l = 0; l < kLanes; l++) {
         if (k >= sh.nb[l]) continue;
-        const uint8_t pred = sh.bpred[w][l];
         float* dst = world_words_w(a, tile * kLanes + l) + (B3X_WORLD_HEADER_BYTES + (size_t)B3X_BODY_BYTES * k) / 4;
-        for (int c = i; c < NYW; c += 32)
-            if (body_word_written(c, pred)) dst[c] = sh.u.bstage[w][l][c];
+        for (int c = i; c < NYW; c += 32) dst[c] = sh.u.bstage[w][l][c];
     }
 }
 
-// Contact k of every world: column block -> B3Contact rows.
-B3X_HD void o_contact_stage(const Args& a, float* slot, OutShared& sh, int k, int t) {
-    const float* src = item(slot + a.SP.cont, k, NCW);
-    for (int idx = t; idx < NCW * kLanes; idx += kCta) sh.u.cstage[idx & 31][idx >> 5] = src[idx];
+// An item's column block ([word][lane], `words` words) -> rows[lane][word]
+// of shared memory (row stride `words`, odd), copied asynchronously.
+B3X_HD void o_stage(const float* src, float* rows, int words, int t) {
+    for (int idx = t; idx < words * kLanes; idx += kCta) async_copy4(rows + (idx & 31) * words + (idx >> 5), src + idx);
+    async_wait();
 }
 
 // Point slots past the point count keep their previous bytes, as in the
@@ -849,58 +868,38 @@ B3X_HD void o_contact_write(const Args& a, int tile, OutShared& sh, int k, int t
     }
 }
 
-// Joint column feeding B3Joint word `word` after the step, -1 when the step
-// leaves the word as it was (06_joints.inl:161-202 writes the prepared
-// fields, the step's finalize the impulses and the hinge rows).
-B3X_HDI int joint_source(int word, bool weld) {
-    if (word == VFIX) return JFIX;
-    if (word >= VSOFT && word < VSOFT + 3) return JSOFT + (word - VSOFT);
-    if (word == VIMA) return JIMA;
-    if (word == VIMB) return JIMB;
-    if (word >= VIIA && word < VIIA + 9) return JIIA + (word - VIIA);
-    if (word >= VIIB && word < VIIB + 9) return JIIB + (word - VIIB);
-    if (word >= VFPA && word < VLI) return JFPA + (word - VFPA);     // frames, delta_center
-    if (word >= VLI && word < VLI + 3) return JLI + (word - VLI);
-    if (weld) {
-        if (word >= VAI && word < VAI + 3) return JAI + (word - VAI);
-        if (word >= VAM && word < VAM + 9) return JAM + (word - VAM);
-        if (word >= VLS && word < VLS + 3) return JLS + (word - VLS);
-        if (word >= VAS && word < VAS + 3) return JAS + (word - VAS);
-        return -1;
+// The solver's results into the prepared B3Joint row of joint q of world l:
+// linear impulse; angular impulse (weld); axial and hinge impulses and the
+// hinge rows (revolute) -- 06_joints.inl finalize.
+B3X_HD void o_joint_patch(const Args& a, float* slot, OutShared& sh, int q, int l) {
+    if (q >= sh.nj[l]) return;
+    const float* jo = item(slot + a.SP.joint, q, NJF) + l;
+    if (!ldi(jo, JOK)) return;
+    float* y = sh.u.jstage[l];
+    auto put3 = [&](int f, B3Vec3 v) { y[f] = v.x; y[f + 1] = v.y; y[f + 2] = v.z; };
+    put3(VLI, ld3(jo, JLI));
+    if (ldi(jo, JTYPE) == B3_JOINT_WELD) {
+        put3(VAI, ld3(jo, JAI));
+    } else {
+        y[VPI] = COL(jo, JPI);
+        y[VPI + 1] = COL(jo, JPI + 1);
+        y[VSI] = COL(jo, JSI);
+        y[VMI] = COL(jo, JMI);
+        y[VLOI] = COL(jo, JLOI);
+        y[VUPI] = COL(jo, JUPI);
+        put3(VPX, ld3(jo, JPX));
+        put3(VPY, ld3(jo, JPY));
     }
-    if (word >= VPI && word < VPI + 2) return JPI + (word - VPI);
-    if (word == VSI) return JSI;
-    if (word == VMI) return JMI;
-    if (word == VLOI) return JLOI;
-    if (word == VUPI) return JUPI;
-    if (word >= VAX && word < VAX + 3) return JAX + (word - VAX);
-    if (word >= VPX && word < VPX + 3) return JPX + (word - VPX);
-    if (word >= VPY && word < VPY + 3) return JPY + (word - VPY);
-    if (word == VAXM) return JAXM;
-    if (word >= VSS && word < VSS + 3) return JSS + (word - VSS);
-    return -1;
-}
-static_assert(JFPB == JFPA + 3 && JFQA == JFPB + 3 && JFQB == JFQA + 4 && JDC == JFQB + 4, "joint frame columns");
-static_assert(VFPB == VFPA + 3 && VFQA == VFPB + 3 && VFQB == VFQA + 4 && VDC == VFQB + 4 && VLI == VDC + 3,
-    "joint frame words");
-
-B3X_HD void o_joint_stage(const Args& a, float* slot, OutShared& sh, int q, int t) {
-    const float* src = item(slot + a.SP.joint, q, NJF);
-    for (int idx = t; idx < NJF * kLanes; idx += kCta) sh.u.jstage[idx & 31][idx >> 5] = src[idx];
 }
 
-B3X_HD void o_joint_write(const Args& a, int tile, OutShared& sh, int q, int t) {
+B3X_HD void o_joint_write(const Args& a, int tile, float* slot, OutShared& sh, int q, int t) {
     const int w = t >> 5, i = t & 31;
     for (int l = w; l < kLanes; l += kCtaWarps) {
         if (q >= sh.nj[l]) continue;
+        if (!ldi(item(slot + a.SP.joint, q, NJF) + l, JOK)) continue;
         const float* row = sh.u.jstage[l];
-        if (!b3x_f2i(row[JOK])) continue;
-        const bool weld = b3x_f2i(row[JTYPE]) == B3_JOINT_WELD;
         float* dst = world_words_w(a, tile * kLanes + l) + (a.L.joint_off + (size_t)B3X_JOINT_BYTES * q) / 4;
-        for (int c = i; c < NVW; c += 32) {
-            const int col = joint_source(c, weld);
-            if (col >= 0) dst[c] = row[col];
-        }
+        for (int c = i; c < NVW; c += 32) dst[c] = row[c];
     }
 }
 
@@ -924,12 +923,13 @@ B3X_HD void out_tile(X& x, const Args& a, int bt, OutShared& sh) {
         x.each([&](int t) { o_body_write(a, tile, sh, k0, t); });
     }
     for (int k = 0; k < sh.maxn; k++) {
-        x.each([&](int t) { o_contact_stage(a, slot, sh, k, t); });
+        x.each([&](int t) { o_stage(item(slot + a.SP.cont, k, NCW), &sh.u.cstage[0][0], NCW, t); });
         x.each([&](int t) { o_contact_write(a, tile, sh, k, t); });
     }
     for (int q = 0; q < sh.maxnj; q++) {
-        x.each([&](int t) { o_joint_stage(a, slot, sh, q, t); });
-        x.each([&](int t) { o_joint_write(a, tile, sh, q, t); });
+        x.each([&](int t) { o_stage(item(slot + a.SP.jimg, q, NVW), &sh.u.jstage[0][0], NVW, t); });
+        x.each([&](int t) { if (t < kLanes) o_joint_patch(a, slot, sh, q, t); });
+        x.each([&](int t) { o_joint_write(a, tile, slot, sh, q, t); });
     }
     x.each([&](int t) { if (t < kLanes) o_header(a, tile, slot, sh, t); });
 }
