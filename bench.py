@@ -17,9 +17,8 @@ value    device-resident: actions generated on the device, worlds resident in
 e2e      through the C-ABI with host buffers: each step copies that step's
          actions from pinned host memory, applies them, steps, gathers one
          observation per world and copies it back, then synchronises.
-roofline the step's kernels alone (collide, solve, write-back), their
-         CUDA-event duration against the algorithmic bytes of a world-step
-         (byte model in DESIGN.md).
+roofline the step kernel alone, its CUDA-event duration against the
+         algorithmic bytes of a world-step (byte model in DESIGN.md).
 """
 import argparse
 import json
@@ -357,8 +356,8 @@ def main():
                 "frac": achieved / hbm_peak,
                 "traffic": traffic * per_gpu if traffic else None,
                 "peak_source": "MEASURED_PEAKS.json hbm_gbs" if peaks.get("hbm_gbs") else "fallback 6650 GB/s",
-                "kernel": "the step: b3x::collide_kernel + b3x::solve_kernel + b3x::out_kernel per chunk "
-                          "(%d launches)" % step_launches, "kernel_ms": kern_s * 1e3,
+                "kernel": "b3x::step_kernel (collide, solve and write-back phases; %d launch(es) per step)"
+                          % step_launches, "kernel_ms": kern_s * 1e3,
                 "algorithmic_bytes_per_launch": alg_bytes,
                 "algorithmic_bytes_per_world_step": bytes_world}
         if flops_ws:

@@ -24,7 +24,10 @@
 
 namespace b3x {
 
-constexpr int kStages = 2;   // streamed items in flight + in use
+#ifndef B3X_STAGES
+#define B3X_STAGES 2
+#endif
+constexpr int kStages = B3X_STAGES;   // streamed items in flight + in use
 
 B3X_HDI bool body_dynamic_flag(const float* __restrict__ bc, int k) {
     return (b3x_f2u(COL(bc, BI(k, BFLAGS))) & B3_FLAG_DYNAMIC) != 0;

@@ -1,19 +1,19 @@
 // b3x_step.cu -- batched rigid-body step on B200 (sm_100a) and the exported
 // C-ABI of libpuffysics_b200.so.
 //
-// Mapping.  A tile is 32 consecutive worlds.  A step runs three kernels per
-// chunk of tiles (as many tiles as the device keeps resident), each with one
-// block per tile:
-//   collide_kernel (128 threads)  reads the caller's AoS worlds with
-//       coalesced row transfers, builds the per-lane solver columns of the
-//       tile's workspace slot, runs broadphase and narrowphase spread over
+// Mapping.  A tile is 32 consecutive worlds.  A step launches step_kernel
+// once per chunk of tiles (as many tiles as the device keeps resident), one
+// 128-thread block per tile, which runs three phases:
+//   collide (all warps)  reads the caller's AoS worlds with coalesced row
+//       transfers, builds the per-lane solver columns of the tile's
+//       workspace slot, runs broadphase and narrowphase spread over
 //       (pair, world) and (candidate, world), and prepares contacts and
 //       joints (b3x_phases.cuh);
-//   solve_kernel (one warp, lane = world)  warm starts and runs the substeps:
+//   solve (warp 0, lane = world)  warm starts and runs the substeps:
 //       Gauss-Seidel sweeps over contacts / joints streamed through shared
 //       memory with TMA bulk copies, body state in shared memory
 //       (b3x_solver.cuh);
-//   out_kernel (128 threads)  finalizes the bodies and writes bodies,
+//   write-back (all warps)  finalizes the bodies and writes bodies,
 //       contacts, joints and header counts back to the AoS worlds, again as
 //       coalesced rows (b3x_phases.cuh).
 // Every loop is bounded by the world's capacities; the solver's pipeline
@@ -60,28 +60,19 @@ struct DevExec {
     }
 };
 
-__global__ void __launch_bounds__(kCta, 4) collide_kernel(Args a) {
-    __shared__ CollideShared sh;
-    DevExec x;
-    collide_tile(x, a, blockIdx.x, sh);
-}
-
-__global__ void __launch_bounds__(kCta, 4) out_kernel(Args a) {
-    __shared__ OutShared sh;
-    DevExec x;
-    out_tile(x, a, blockIdx.x, sh);
-}
-
-// Shared memory of a solve block: the streaming stages, their mbarriers,
-// then the body columns when they live on chip.
+// Shared memory of a step block: the collide and write-back phases use it
+// as their block state; the solve phase as the streaming stages, their
+// mbarriers, then the body columns when they live on chip.
 constexpr size_t kStageBytes = (size_t)kStages * kStreamWords * kLanes * sizeof(float);
 constexpr size_t kBarBytes = 64;
 constexpr int kSolvedBodyFields = BDQ + 4;   // velocities and pose deltas go back
 
+// Warp 0's part of the step: warm start and substeps of the tile's 32 worlds.
+// Returns false when a pipeline wait gave up (nothing of the tile is then
+// written back: the step is abandoned for these worlds).
 template <bool kBodySmem>
-__global__ void __launch_bounds__(kLanes) solve_kernel(Args a) {
-    extern __shared__ __align__(128) unsigned char smem_raw[];
-    const int lane = threadIdx.x;
+__device__ bool solve_tile(const Args& a, unsigned char* smem_raw) {
+    const int lane = threadIdx.x & 31;
     float* slot = slot_of(a, blockIdx.x);
     Pipe P;
     P.buf = reinterpret_cast<float*>(smem_raw);
@@ -95,14 +86,40 @@ __global__ void __launch_bounds__(kLanes) solve_kernel(Args a) {
         for (int idx = lane; idx < nb * NBF * kLanes; idx += kLanes) sb[idx] = gb[idx];
     }
     float* bc = (kBodySmem ? sb : gb) + lane;
-    if (!solve_world(a, slot, lane, bc, P)) {
-        if (lane == 0) atomicExch(&g_fault, 1);
-        return;
-    }
-    if (kBodySmem) {
+    const bool ok = solve_world(a, slot, lane, bc, P);
+    if (ok && kBodySmem) {
         for (int k = 0; k < nb; k++)
             for (int f = 0; f < kSolvedBodyFields; f++) COL(gb + lane, BI(k, f)) = COL(sb + lane, BI(k, f));
     }
+    __syncwarp();
+    if (lane == 0) {
+        // the barriers' memory is reused by the write-back
+        for (int s = 0; s < kStages; s++)
+            asm volatile("mbarrier.inval.shared::cta.b64 [%0];" ::"r"(smem_addr(&P.bar[s])) : "memory");
+        if (!ok) atomicExch(&g_fault, 1);
+    }
+    return ok;
+}
+
+// One block per tile: collide (all warps), solve (warp 0), write-back (all
+// warps).
+template <bool kBodySmem>
+__global__ void __launch_bounds__(kCta, 4) step_kernel(Args a) {
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    __shared__ int solved;
+    DevExec x;
+    collide_tile(x, a, blockIdx.x, *reinterpret_cast<CollideShared*>(smem_raw));
+    // the solve's bulk copies (async proxy) reuse memory the collide phase
+    // accessed through the generic proxy
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncthreads();
+    if (threadIdx.x < kLanes) {
+        const bool ok = solve_tile<kBodySmem>(a, smem_raw);
+        if (threadIdx.x == 0) solved = ok;
+    }
+    __syncthreads();
+    if (!solved) return;
+    out_tile(x, a, blockIdx.x, *reinterpret_cast<OutShared*>(smem_raw));
 }
 
 // ---- restore, actions --------------------------------------------------------
@@ -169,7 +186,7 @@ __global__ void observe_kernel(const unsigned char* data, unsigned long long str
 struct Plan {
     bool body_smem;
     Space SP;
-    size_t solve_smem;       // dynamic shared memory of a solve block
+    size_t smem_bytes;       // dynamic shared memory of a step block
     size_t tile_bytes;       // one tile's workspace slot
     int chunk_tiles;         // tiles per launch with the default workspace
     size_t ws_bytes;         // the default workspace (chunk_tiles slots)
@@ -195,7 +212,10 @@ static cudaError_t make_plan(int dev, unsigned long long sig, const Layout& L, P
     p.SP = space_from_layout(L);
     size_t body_bytes = (size_t)L.B * NBF * kLanes * sizeof(float);
     p.body_smem = body_bytes <= kBodySmemLimit;
-    p.solve_smem = kStageBytes + kBarBytes + (p.body_smem ? body_bytes : 0);
+    size_t solve_smem = kStageBytes + kBarBytes + (p.body_smem ? body_bytes : 0);
+    p.smem_bytes = solve_smem;
+    if (p.smem_bytes < sizeof(CollideShared)) p.smem_bytes = sizeof(CollideShared);
+    if (p.smem_bytes < sizeof(OutShared)) p.smem_bytes = sizeof(OutShared);
     p.tile_bytes = (size_t)p.SP.tile_words * sizeof(float);
     int sms = 0;
     cudaError_t e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -206,10 +226,15 @@ static cudaError_t make_plan(int dev, unsigned long long sig, const Layout& L, P
     int optin = 0;
     e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     if (e != cudaSuccess) return e;
-    if (p.solve_smem > (size_t)optin) return cudaErrorInvalidValue;
-    e = cudaFuncSetAttribute(solve_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, optin);
+    // (the cap excludes the kernel's static shared memory)
+    cudaFuncAttributes fa;
+    e = cudaFuncGetAttributes(&fa, step_kernel<true>);
     if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(solve_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, optin);
+    const int cap = optin - (int)fa.sharedSizeBytes;
+    if (p.smem_bytes > (size_t)cap) return cudaErrorInvalidValue;
+    e = cudaFuncSetAttribute(step_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, cap);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(step_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, cap);
     if (e != cudaSuccess) return e;
     p.chunk_tiles = sms * kChunkBlocksPerSM;
     p.ws_bytes = (size_t)p.chunk_tiles * p.tile_bytes;
@@ -229,7 +254,7 @@ static bool aligned8(const B3Batch& b) {
     return (((uintptr_t)b.data + b.world_offset) % 8 == 0) && (b.stride % 8 == 0);
 }
 
-// The step over chunks of `chunk` tiles: collide, solve, write-back per chunk.
+// The step over chunks of `chunk` tiles, one step_kernel launch per chunk.
 static cudaError_t launch_step(const B3Batch& batch, float dt, int substeps, const unsigned char* active,
         cudaStream_t stream, const Layout& L, int ji, int ri, const Plan& p, void* ws, int chunk) {
     Args a;
@@ -249,10 +274,8 @@ static cudaError_t launch_step(const B3Batch& batch, float dt, int substeps, con
     for (int t0 = 0; t0 < ntiles; t0 += chunk) {
         const int nt = ntiles - t0 < chunk ? ntiles - t0 : chunk;
         a.tile0 = t0;
-        collide_kernel<<<nt, kCta, 0, stream>>>(a);
-        if (p.body_smem) solve_kernel<true><<<nt, kLanes, p.solve_smem, stream>>>(a);
-        else solve_kernel<false><<<nt, kLanes, p.solve_smem, stream>>>(a);
-        out_kernel<<<nt, kCta, 0, stream>>>(a);
+        if (p.body_smem) step_kernel<true><<<nt, kCta, p.smem_bytes, stream>>>(a);
+        else step_kernel<false><<<nt, kCta, p.smem_bytes, stream>>>(a);
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     }
@@ -286,7 +309,7 @@ B3X_API int b3x_step_launches(unsigned long long sig, int count, int device) {
     Plan p;
     if (make_plan(device, sig, L, &p) != cudaSuccess) return 0;
     const int ntiles = (count + kLanes - 1) / kLanes;
-    return 3 * ((ntiles + p.chunk_tiles - 1) / p.chunk_tiles);
+    return (ntiles + p.chunk_tiles - 1) / p.chunk_tiles;
 }
 
 static int step_common(B3Batch batch, float dt, int substeps, const unsigned char* active, void* stream,
