@@ -28,6 +28,8 @@ namespace b3x {
 constexpr int kCta = 128;            // threads of a collide / write-back block
 constexpr int kCtaWarps = kCta / 32;
 constexpr int kRow = NYW + 1;        // staged struct row (odd: conflict-free columns)
+// Collide staging area: rows of caller structs gathered for a group of worlds.
+constexpr int kStageFloats = 12 * 1024;
 
 // ---- block state ------------------------------------------------------------------
 struct CollideShared {
@@ -45,7 +47,8 @@ struct CollideShared {
     int off[kPairWindow + 1];
     int maxc, total;
     union {
-        float stage[kCtaWarps][kLanes][kRow];    // gathered struct rows, [item][world][word]
+        float hdr[kLanes][NHW];                  // world headers (17: odd)
+        float flat[kStageFloats];                // gathered struct rows of a group of worlds
         float jstage[kLanes][NVW];               // one joint of every world (115: odd)
         float clip[48 * kCta];                   // narrowphase clip polygons
     } u;
@@ -54,11 +57,7 @@ struct CollideShared {
 struct OutShared {
     int live[kLanes], nb[kLanes], n[kLanes], nj[kLanes];
     int maxnb, maxn, maxnj;
-    union {
-        float bstage[kCtaWarps][kLanes][kRow];   // finalized body rows
-        float cstage[kLanes][NCW];               // one contact of every world (119: odd)
-        float jstage[kLanes][NVW];               // one joint of every world (115: odd)
-    } u;
+    float flat[kStageFloats];                    // rows of several items of every world
 };
 
 B3X_HDI const float* world_words(const Args& a, int wi) {
@@ -85,7 +84,7 @@ B3X_HD void c_header(const Args& a, int tile, CollideShared& sh, int t) {
     if (i < NHW) {
         for (int l = w; l < kLanes; l += kCtaWarps) {
             int wi = tile * kLanes + l;
-            if (wi < a.count) async_copy4(&sh.u.stage[0][l][i], world_words(a, wi) + i);
+            if (wi < a.count) async_copy4(&sh.u.hdr[l][i], world_words(a, wi) + i);
         }
     }
     async_wait();
@@ -96,7 +95,7 @@ B3X_HD void c_header(const Args& a, int tile, CollideShared& sh, int t) {
 // reference; here they are clamped so a corrupt world cannot fault.
 B3X_HD void c_record(const Args& a, int tile, float* slot, CollideShared& sh, int l) {
     const Layout& L = a.L;
-    const float* hw = sh.u.stage[0][l];
+    const float* hw = sh.u.hdr[l];
     const int wi = tile * kLanes + l;
     const int live = wi < a.count && (!a.active || a.active[wi]);
     sh.live[l] = live;
@@ -109,6 +108,7 @@ B3X_HD void c_record(const Args& a, int tile, float* slot, CollideShared& sh, in
     sh.oldn[l] = oldn;
     sh.nj[l] = nj;
     sh.n[l] = 0;
+    sh.sorted[l] = 1;
     sh.ovf[l] = live ? b3x_f2i(hw[HOVC]) : 0;
     sh.drop[l] = live ? b3x_f2i(hw[HDROP]) : 0;
     for (int c = 0; c < 3; c++) sh.grav[l][c] = live ? hw[HGRAV + c] : 0.0f;
@@ -136,26 +136,58 @@ B3X_HD void c_record(const Args& a, int tile, float* slot, CollideShared& sh, in
     sts(rec, RSS, make_soft(2.0f * hertz, 0.5f * contact_damping, h));
 }
 
-// Struct rows of item k0 + w of every world into stage[w] (warp w, lane =
-// word; `words` words starting at byte `base` + k * `size` of the world).
-B3X_HD void c_gather(const Args& a, int tile, CollideShared& sh, const int* count, int k0, unsigned base,
-        unsigned size, int words, int t) {
-    const int w = t >> 5, i = t & 31, k = k0 + w;
-    for (int l = 0; l < kLanes; l++) {
-        if (k >= count[l]) continue;
-        const float* src = world_words(a, tile * kLanes + l) + (base + (size_t)size * k) / 4;
-        for (int c = i; c < words; c += 32) async_copy4(&sh.u.stage[w][l][c], src + c);
+// ---- grouped gathers -------------------------------------------------------------
+// A group is worlds [l0, l0 + G) of the tile.  Item k of group world g lands in
+// the staging row (g * M + k) of stride RS (M * RS odd, so lanes reading one
+// field of consecutive worlds hit distinct banks).  Warps take whole worlds:
+// the items of a world are one contiguous region of the caller's struct
+// array, copied with consecutive words on consecutive lanes.
+template <int PER>
+B3X_HD void c_gather_group(const Args& a, int tile, CollideShared& sh, const int* count, int l0, int G, int M,
+        int RS, unsigned base, int dst, int t) {
+    const int w = t >> 5, i = t & 31;
+    for (int g = w; g < G; g += kCtaWarps) {
+        const int l = l0 + g;
+        const int words = count[l] * PER;
+        const float* src = world_words(a, tile * kLanes + l) + base / 4;
+        float* row0 = sh.u.flat + dst + g * M * RS;
+        for (int idx = i; idx < words; idx += 32) {
+            const int k = idx / PER, c = idx - k * PER;
+            async_copy4(row0 + k * RS + c, src + idx);
+        }
     }
-    async_wait();
 }
 
-// Body k0 + w of world l: solver columns, step constants and pose
+// Words of a previous-step contact that the warm-start cache keeps
+// (08_contacts.inl:68-87), in OLD field order.
+B3X_HDI int old_word(int i) {
+    return i == OSA ? WSA : i == OSB ? WSB : i == OCNT ? WCNT : i < OTWI ? WFI + (i - OFI)
+        : i == OTWI ? WTWI : i < OFEAT ? WRI + (i - ORI) : i < ONI ? PW(i - OFEAT, QFEAT) : PW(i - ONI, QNI);
+}
+
+B3X_HD void c_gather_old(const Args& a, int tile, CollideShared& sh, int l0, int G, int M, int dst, int t) {
+    const int w = t >> 5, i = t & 31;
+    if (i >= NOF) return;
+    const int word = old_word(i);
+    for (int g = w; g < G; g += kCtaWarps) {
+        const int l = l0 + g;
+        const float* src = world_words(a, tile * kLanes + l) + a.L.contact_off / 4 + word;
+        float* row0 = sh.u.flat + dst + g * M * NOF;
+        for (int k = 0; k < sh.oldn[l]; k++) async_copy4(row0 + k * NOF + i, src + k * (B3X_CONTACT_BYTES / 4));
+    }
+}
+
+// Thread t's staged items of a group: j -> (item k = j / G, group world g =
+// j % G), so consecutive threads take one item of consecutive worlds and
+// their workspace column stores coalesce.
+#define FOR_GROUP_ITEMS(t, G, M, k, g) \
+    for (int j_ = (t), k = j_ / (G), g = j_ - k * (G); j_ < (G) * (M); \
+         j_ += kCta, k = j_ / (G), g = j_ - k * (G))
+
+// Body k of world l (row y): solver columns, step constants and the raw row
 // (inverse mass / inertia gated by type as the contact and joint prepares do,
 // 08_contacts.inl:236-239; velocity increments of 09_step.inl:5-18).
-B3X_HD void c_bodies(const Args& a, float* slot, CollideShared& sh, int k0, int t) {
-    const int w = t >> 5, l = t & 31, k = k0 + w;
-    if (k >= sh.nb[l]) return;
-    const float* y = sh.u.stage[w][l];
+B3X_HD void c_body(const Args& a, float* slot, const CollideShared& sh, int k, int l, const float* y) {
     const float h = a.dt / (float)a.substeps;
     float* bc = item(slot + a.SP.body, k, NBF) + l;
     float* ic = item(slot + a.SP.bimg, k, NYW) + l;
@@ -189,12 +221,9 @@ B3X_HD void c_bodies(const Args& a, float* slot, CollideShared& sh, int k0, int 
     for (int f = 0; f < NYW; f++) COL(ic, f) = y[f];
 }
 
-// Shape k0 + w of world l: world pose and padded AABB (04_world.inl:293-336,
+// Shape s of world l (row y): world pose and padded AABB (04_world.inl:293-336,
 // 08_contacts.inl:109-114); a shape on an invalid body never overlaps.
-B3X_HD void c_shapes(const Args& a, float* slot, CollideShared& sh, int k0, int t) {
-    const int w = t >> 5, l = t & 31, s = k0 + w;
-    if (s >= sh.ns[l]) return;
-    const float* y = sh.u.stage[w][l];
+B3X_HD void c_shape(const Args& a, float* slot, const CollideShared& sh, int s, int l, const float* y) {
     float* so = item(slot + a.SP.shape, s, NSF) + l;
     const int body = b3x_f2i(y[XBODY]);
     const int type = b3x_f2i(y[XTYPE]);
@@ -248,45 +277,29 @@ B3X_HD void c_shapes(const Args& a, float* slot, CollideShared& sh, int k0, int 
     st3(so, SHI, b3_add(hi, pad));
 }
 
-// Words of a previous-step contact that the warm-start cache keeps
-// (08_contacts.inl:68-87), in OLD field order.
-B3X_HDI int old_word(int i) {
-    return i == OSA ? WSA : i == OSB ? WSB : i == OCNT ? WCNT : i < OTWI ? WFI + (i - OFI)
-        : i == OTWI ? WTWI : i < OFEAT ? WRI + (i - ORI) : i < ONI ? PW(i - OFEAT, QFEAT) : PW(i - ONI, QNI);
+// Rounds of a group plan: G worlds per round, balanced over the tile.
+B3X_HDI int group_size(int per_world_floats, int budget) {
+    int g = per_world_floats > 0 ? budget / per_world_floats : kLanes;
+    if (g >= kLanes) return kLanes;
+    if (g < 1) g = 1;
+    const int rounds = (kLanes + g - 1) / g;
+    return (kLanes + rounds - 1) / rounds;
 }
 
-B3X_HD void c_old_gather(const Args& a, int tile, CollideShared& sh, int k0, int t) {
-    const int w = t >> 5, i = t & 31, k = k0 + w;
-    if (i >= NOF) return;   // (no copies of its own: nothing to wait for)
-    const int word = old_word(i);
-    for (int l = 0; l < kLanes; l++) {
-        if (k >= sh.oldn[l]) continue;
-        const float* src = world_words(a, tile * kLanes + l) + (a.L.contact_off + (size_t)B3X_CONTACT_BYTES * k) / 4;
-        async_copy4(&sh.u.stage[w][l][i], src + word);
-    }
-    async_wait();
-}
-
-B3X_HD void c_old(const Args& a, float* slot, CollideShared& sh, int k0, int t) {
-    const int w = t >> 5, l = t & 31, k = k0 + w;
-    if (k >= sh.oldn[l]) return;
+// Old contact k of world l from its staged row y: the warm-start cache
+// columns, and whether the cache's (shape_a, shape_b) keys strictly increase
+// (then the reference matches with a merge cursor, else with a full scan;
+// both pick the same entry), 08_contacts.inl:70-79.  `prev` is the staged
+// row of contact k - 1.
+B3X_HD void c_old_row(const Args& a, float* slot, CollideShared& sh, int k, int l, const float* y,
+        const float* prev) {
     float* oc = item(slot + a.SP.old, k, NOF) + l;
-    for (int f = 0; f < NOF; f++) COL(oc, f) = sh.u.stage[w][l][f];
-}
-
-// Whether the old cache's (shape_a, shape_b) keys strictly increase (then the
-// reference matches with a merge cursor, else with a full scan; both pick
-// the same entry), 08_contacts.inl:70-79.
-B3X_HD void c_old_sorted(const Args& a, float* slot, CollideShared& sh, int l) {
-    const float* oc = slot + a.SP.old + l;
-    int sorted = 1;
-    for (int k = 1; k < sh.oldn[l]; k++) {
-        const float* p = item(oc, k - 1, NOF);
-        const float* c = item(oc, k, NOF);
-        int pa = ldi(p, OSA), pb = ldi(p, OSB), sa = ldi(c, OSA), sb = ldi(c, OSB);
-        if (pa > sa || (pa == sa && pb >= sb)) sorted = 0;
+    for (int f = 0; f < NOF; f++) COL(oc, f) = y[f];
+    if (k > 0) {
+        const int pa = b3x_f2i(prev[OSA]), pb = b3x_f2i(prev[OSB]);
+        const int sa = b3x_f2i(y[OSA]), sb = b3x_f2i(y[OSB]);
+        if (pa > sa || (pa == sa && pb >= sb)) sh.sorted[l] = 0;
     }
-    sh.sorted[l] = sorted;
 }
 
 // Joint q of every world into jstage (warp w: worlds w, w+4, ...).
@@ -424,7 +437,10 @@ B3X_HDI int pair_of(int p, int ns) {
 }
 
 B3X_HD void c_window_setup(CollideShared& sh, int p0, int npairs, int t) {
-    if (t < kPairWindow) sh.ptab[t] = p0 + t < npairs ? pair_of(p0 + t, sh.maxns) : -1;
+    if (t < kPairWindow) {
+        sh.ptab[t] = p0 + t < npairs ? pair_of(p0 + t, sh.maxns) : -1;
+        sh.wmask[t] = 0;
+    }
     if (t < kLanes) {
         for (int c = 0; c < kPairWindow / 32; c++) {
             sh.cmask[t][c] = 0;
@@ -437,9 +453,9 @@ B3X_HD void c_window_setup(CollideShared& sh, int p0, int npairs, int t) {
 // Broadphase of window pair pp for world l: the reference's predicate
 // (08_contacts.inl:44-58; AABB overlap first, the side-effect-free tests in
 // a cheaper order) with its joint-connection filter (08_contacts.inl:94-104).
-B3X_HD void c_broadphase(const Args& a, float* slot, CollideShared& sh, int t) {
+B3X_HD void c_broadphase(const Args& a, float* slot, CollideShared& sh, int npw, int t) {
     const float* sc = slot + a.SP.shape;
-    for (int idx = t; idx < kPairWindow * kLanes; idx += kCta) {
+    for (int idx = t; idx < npw * kLanes; idx += kCta) {
         const int pp = idx >> 5, l = idx & 31;
         const int pr = sh.ptab[pp];
         if (pr < 0) continue;
@@ -472,19 +488,13 @@ B3X_HD void c_broadphase(const Args& a, float* slot, CollideShared& sh, int t) {
     }
 }
 
+// Candidates of world l, and its bit in wmask[ci] for every ci it has.
 B3X_HD void c_count(CollideShared& sh, int l) {
     int c = 0;
     for (int w = 0; w < kPairWindow / 32; w++) c += popc32(sh.cmask[l][w]);
     sh.ccount[l] = c;
     shared_max(&sh.maxc, c);
-}
-
-B3X_HD void c_enumerate(CollideShared& sh, int ci) {
-    if (ci >= sh.maxc) return;
-    uint32_t m = 0;
-    for (int l = 0; l < kLanes; l++)
-        if (sh.ccount[l] > ci) m |= 1u << l;
-    sh.wmask[ci] = m;
+    for (int ci = 0; ci < c; ci++) shared_or(&sh.wmask[ci], 1u << l);
 }
 
 B3X_HD void c_prefix(CollideShared& sh) {
@@ -576,11 +586,21 @@ B3X_HDI int rank_below(const uint32_t* m, int ci) {
 // (keys of kept contacts increase, so the cursor is that lower bound whatever
 // the candidates before); it matches [cursor, cursor + 1).  Otherwise every
 // entry is scanned.
-B3X_HDI void warm_range(const float* oc, int on, int sorted, int i, int j, int& first, int& end) {
+B3X_HDI void warm_range(const float* oc, int on, int sorted, int i, int j, int guess, int& first, int& end) {
     if (!sorted) {
         first = 0;
         end = on;
         return;
+    }
+    // a cache that this step's contacts will mostly reproduce: try the
+    // entry at the contact's own slot first (keys are unique when sorted)
+    if (guess < on) {
+        const float* o = item(oc, guess, NOF);
+        if (ldi(o, OSA) == i && ldi(o, OSB) == j) {
+            first = guess;
+            end = guess + 1;
+            return;
+        }
     }
     int lo = 0, hi = on;
     while (lo < hi) {
@@ -636,7 +656,7 @@ B3X_HD void c_prepare(const Args& a, float* slot, CollideShared& sh, int t) {
         B3Vec3 ri = b3_v(0.0f, 0.0f, 0.0f);
         const float* oc = slot + a.SP.old + l;
         int first, end;
-        warm_range(oc, sh.oldn[l], sh.sorted[l], i, j, first, end);
+        warm_range(oc, sh.oldn[l], sh.sorted[l], i, j, k, first, end);
         for (int kk = first; kk < end; kk++) {
             const float* o = item(oc, kk, NOF);
             if (ldi(o, OSA) != i || ldi(o, OSB) != j) continue;
@@ -745,30 +765,81 @@ B3X_HD void collide_tile(X& x, const Args& a, int bt, CollideShared& sh) {
     const int tile = a.tile0 + bt;
     x.each([&](int t) { c_header(a, tile, sh, t); });
     x.each([&](int t) { if (t < kLanes) c_record(a, tile, slot, sh, t); });
-    for (int k0 = 0; k0 < sh.maxnb; k0 += kCtaWarps) {
-        x.each([&](int t) { c_gather(a, tile, sh, sh.nb, k0, B3X_WORLD_HEADER_BYTES, B3X_BODY_BYTES, NYW, t); });
-        x.each([&](int t) { c_bodies(a, slot, sh, k0, t); });
+    {
+        // bodies: whole body arrays of G worlds per round
+        const int M = sh.maxnb | 1, RS = kRow;
+        const int G = group_size(M * RS, kStageFloats);
+        for (int l0 = 0; l0 < kLanes; l0 += G) {
+            const int Gr = kLanes - l0 < G ? kLanes - l0 : G;
+            x.each([&](int t) {
+                c_gather_group<NYW>(a, tile, sh, sh.nb, l0, Gr, M, RS, B3X_WORLD_HEADER_BYTES, 0, t);
+                async_wait();
+            });
+            x.each([&](int t) {
+                FOR_GROUP_ITEMS(t, Gr, M, k, g) {
+                    if (k < sh.nb[l0 + g]) c_body(a, slot, sh, k, l0 + g, sh.u.flat + (g * M + k) * RS);
+                }
+            });
+        }
     }
-    for (int k0 = 0; k0 < sh.maxns; k0 += kCtaWarps) {
-        x.each([&](int t) { c_gather(a, tile, sh, sh.ns, k0, a.L.shape_off, B3X_SHAPE_BYTES, NXW, t); });
-        x.each([&](int t) { c_shapes(a, slot, sh, k0, t); });
-    }
-    for (int k0 = 0; k0 < sh.maxold; k0 += kCtaWarps) {
-        x.each([&](int t) { c_old_gather(a, tile, sh, k0, t); });
-        x.each([&](int t) { c_old(a, slot, sh, k0, t); });
+    {
+        // shapes and the old contacts' warm-cache words, together when both fit
+        const int Ms = sh.maxns | 1, Mo = sh.maxold | 1;
+        const int per_s = Ms * (NXW + 1), per_o = Mo * NOF;
+        const bool joint_round = kLanes * (per_s + per_o) <= kStageFloats;
+        const int Gs = joint_round ? kLanes : group_size(per_s, kStageFloats);
+        for (int l0 = 0; l0 < kLanes; l0 += Gs) {
+            const int Gr = kLanes - l0 < Gs ? kLanes - l0 : Gs;
+            const int odst = Gr * per_s;
+            x.each([&](int t) {
+                c_gather_group<NXW>(a, tile, sh, sh.ns, l0, Gr, Ms, NXW + 1, a.L.shape_off, 0, t);
+                if (joint_round) c_gather_old(a, tile, sh, l0, Gr, Mo, odst, t);
+                async_wait();
+            });
+            x.each([&](int t) {
+                FOR_GROUP_ITEMS(t, Gr, Ms, k, g) {
+                    if (k < sh.ns[l0 + g]) c_shape(a, slot, sh, k, l0 + g, sh.u.flat + (g * Ms + k) * (NXW + 1));
+                }
+                if (joint_round) {
+                    FOR_GROUP_ITEMS(t, Gr, Mo, k, g) {
+                        if (k < sh.oldn[l0 + g]) {
+                            const float* y = sh.u.flat + odst + (g * Mo + k) * NOF;
+                            c_old_row(a, slot, sh, k, l0 + g, y, y - NOF);
+                        }
+                    }
+                }
+            });
+        }
+        if (!joint_round) {
+            const int Go = group_size(per_o, kStageFloats);
+            for (int l0 = 0; l0 < kLanes; l0 += Go) {
+                const int Gr = kLanes - l0 < Go ? kLanes - l0 : Go;
+                x.each([&](int t) {
+                    c_gather_old(a, tile, sh, l0, Gr, Mo, 0, t);
+                    async_wait();
+                });
+                x.each([&](int t) {
+                    FOR_GROUP_ITEMS(t, Gr, Mo, k, g) {
+                        if (k < sh.oldn[l0 + g]) {
+                            const float* y = sh.u.flat + (g * Mo + k) * NOF;
+                            c_old_row(a, slot, sh, k, l0 + g, y, y - NOF);
+                        }
+                    }
+                });
+            }
+        }
     }
     for (int q = 0; q < sh.maxnj; q++) {
         x.each([&](int t) { c_joint_gather(a, tile, sh, q, t); });
         x.each([&](int t) { if (t < kLanes) c_joint(a, slot, sh, q, t); });
     }
-    x.each([&](int t) { if (t < kLanes) c_old_sorted(a, slot, sh, t); });
     const int maxns = sh.maxns;
     const int npairs = maxns * (maxns - 1) / 2;
     for (int p0 = 0; p0 < npairs; p0 += kPairWindow) {
         x.each([&](int t) { c_window_setup(sh, p0, npairs, t); });
-        x.each([&](int t) { c_broadphase(a, slot, sh, t); });
+        const int npw = npairs - p0 < kPairWindow ? npairs - p0 : kPairWindow;
+        x.each([&](int t) { c_broadphase(a, slot, sh, npw, t); });
         x.each([&](int t) { if (t < kLanes) c_count(sh, t); });
-        x.each([&](int t) { if (t < kPairWindow) c_enumerate(sh, t); });
         x.each([&](int t) { if (t == 0) c_prefix(sh); });
         if (sh.total == 0) continue;
         x.each([&](int t) { c_narrow(a, slot, sh, t); });
@@ -800,15 +871,20 @@ B3X_HD void o_maxima(OutShared& sh) {
     sh.maxnj = mj;
 }
 
-// Finalize body k0 + w of world l (09_step.inl:109-130) into its B3Body row:
-// the raw row read by the collide kernel with the fields the reference's
-// step writes replaced, so the write-back stores whole rows.
-B3X_HD void o_bodies(const Args& a, float* slot, OutShared& sh, int k0, int t) {
-    const int w = t >> 5, l = t & 31, k = k0 + w;
-    if (k >= sh.nb[l]) return;
+// Items [k0, k0 + K) of every world are staged as rows ((k - k0) * 32 + l) of
+// odd stride RS; the write-back stores each world's run of items as one
+// contiguous region with consecutive words on consecutive lanes.
+B3X_HDI float* out_row(OutShared& sh, int l, int kk, int K, int RS) {
+    (void)K;
+    return sh.flat + (kk * kLanes + l) * RS;
+}
+
+// Finalize body k of world l (09_step.inl:109-130) into its B3Body row: the
+// raw row read by the collide phase with the fields the reference's step
+// writes replaced, so the write-back stores whole rows.
+B3X_HD void o_body(const Args& a, float* slot, int k, int l, float* y) {
     const float* bc = item(slot + a.SP.body, k, NBF) + l;
     const float* ic = item(slot + a.SP.bimg, k, NYW) + l;
-    float* y = sh.u.bstage[w][l];
     for (int f = 0; f < NYW; f++) y[f] = COL(ic, f);
     auto put3 = [&](int f, B3Vec3 v) { y[f] = v.x; y[f + 1] = v.y; y[f + 2] = v.z; };
     auto put4 = [&](int f, B3Quat q) { y[f] = q.v.x; y[f + 1] = q.v.y; y[f + 2] = q.v.z; y[f + 3] = q.s; };
@@ -837,45 +913,60 @@ B3X_HD void o_bodies(const Args& a, float* slot, OutShared& sh, int k0, int t) {
     }
 }
 
-B3X_HD void o_body_write(const Args& a, int tile, OutShared& sh, int k0, int t) {
-    const int w = t >> 5, i = t & 31, k = k0 + w;
-    for (int l = 0; l < kLanes; l++) {
-        if (k >= sh.nb[l]) continue;
-        float* dst = world_words_w(a, tile * kLanes + l) + (B3X_WORLD_HEADER_BYTES + (size_t)B3X_BODY_BYTES * k) / 4;
-        for (int c = i; c < NYW; c += 32) dst[c] = sh.u.bstage[w][l][c];
+B3X_HD void o_bodies(const Args& a, float* slot, OutShared& sh, int k0, int K, int t) {
+    for (int j = t; j < K * kLanes; j += kCta) {
+        const int kk = j >> 5, l = j & 31;
+        if (k0 + kk < sh.nb[l]) o_body(a, slot, k0 + kk, l, out_row(sh, l, kk, K, kRow));
     }
 }
 
-// An item's column block ([word][lane], `words` words) -> rows[lane][word]
-// of shared memory (row stride `words`, odd), copied asynchronously.
-B3X_HD void o_stage(const float* src, float* rows, int words, int t) {
-    for (int idx = t; idx < words * kLanes; idx += kCta) async_copy4(rows + (idx & 31) * words + (idx >> 5), src + idx);
+B3X_HD void o_body_write(const Args& a, int tile, OutShared& sh, int k0, int K, int t) {
+    const int w = t >> 5, i = t & 31;
+    for (int l = w; l < kLanes; l += kCtaWarps) {
+        const int n = (sh.nb[l] < k0 + K ? sh.nb[l] : k0 + K) - k0;
+        if (n <= 0) continue;
+        float* dst = world_words_w(a, tile * kLanes + l) + (B3X_WORLD_HEADER_BYTES + (size_t)B3X_BODY_BYTES * k0) / 4;
+        for (int idx = i; idx < n * NYW; idx += 32) {
+            const int kk = idx / NYW, c = idx - kk * NYW;
+            dst[idx] = out_row(sh, l, kk, K, kRow)[c];
+        }
+    }
+}
+
+// Items [k0, k0 + K) of a [item][word][lane] region -> rows, copied
+// asynchronously (`words` words per item, row stride RS).
+B3X_HD void o_stage(const float* src, OutShared& sh, int K, int words, int RS, int t) {
+    for (int idx = t; idx < K * words * kLanes; idx += kCta) {
+        const int l = idx & 31, r = idx >> 5, kk = r / words, c = r - kk * words;
+        async_copy4(out_row(sh, l, kk, K, RS) + c, src + idx);
+    }
     async_wait();
 }
 
-// Point slots past the point count keep their previous bytes, as in the
-// reference (b3_contact_from_mani writes only the manifold's points).
-B3X_HD void o_contact_write(const Args& a, int tile, OutShared& sh, int k, int t) {
+// Contacts [k0, k0 + K) of every world.  Point slots past a contact's point
+// count keep their previous bytes, as in the reference (b3_contact_from_mani
+// writes only the manifold's points).
+B3X_HD void o_contact_write(const Args& a, int tile, OutShared& sh, int k0, int K, int t) {
     const int w = t >> 5, i = t & 31;
     for (int l = w; l < kLanes; l += kCtaWarps) {
-        if (k >= sh.n[l]) continue;
-        const float* row = sh.u.cstage[l];
-        const int cnt = clampi(b3x_f2i(row[WCNT]), 0, B3_MAX_MANIFOLD);
-        const int stale_lo = WP + cnt * NQW;
-        float* dst = world_words_w(a, tile * kLanes + l) + (a.L.contact_off + (size_t)B3X_CONTACT_BYTES * k) / 4;
-        for (int c = i; c < NCW; c += 32)
-            if (c < stale_lo || c >= WCA) dst[c] = row[c];
+        const int n = (sh.n[l] < k0 + K ? sh.n[l] : k0 + K) - k0;
+        if (n <= 0) continue;
+        float* dst = world_words_w(a, tile * kLanes + l) + (a.L.contact_off + (size_t)B3X_CONTACT_BYTES * k0) / 4;
+        for (int idx = i; idx < n * NCW; idx += 32) {
+            const int kk = idx / NCW, c = idx - kk * NCW;
+            const float* row = out_row(sh, l, kk, K, NCW);
+            const int cnt = clampi(b3x_f2i(row[WCNT]), 0, B3_MAX_MANIFOLD);
+            if (c < WP + cnt * NQW || c >= WCA) dst[idx] = row[c];
+        }
     }
 }
 
 // The solver's results into the prepared B3Joint row of joint q of world l:
 // linear impulse; angular impulse (weld); axial and hinge impulses and the
 // hinge rows (revolute) -- 06_joints.inl finalize.
-B3X_HD void o_joint_patch(const Args& a, float* slot, OutShared& sh, int q, int l) {
-    if (q >= sh.nj[l]) return;
+B3X_HD void o_joint_patch(const Args& a, float* slot, int q, int l, float* y) {
     const float* jo = item(slot + a.SP.joint, q, NJF) + l;
     if (!ldi(jo, JOK)) return;
-    float* y = sh.u.jstage[l];
     auto put3 = [&](int f, B3Vec3 v) { y[f] = v.x; y[f + 1] = v.y; y[f + 2] = v.z; };
     put3(VLI, ld3(jo, JLI));
     if (ldi(jo, JTYPE) == B3_JOINT_WELD) {
@@ -892,15 +983,35 @@ B3X_HD void o_joint_patch(const Args& a, float* slot, OutShared& sh, int q, int 
     }
 }
 
-B3X_HD void o_joint_write(const Args& a, int tile, float* slot, OutShared& sh, int q, int t) {
+B3X_HD void o_joints(const Args& a, float* slot, OutShared& sh, int q0, int K, int t) {
+    for (int j = t; j < K * kLanes; j += kCta) {
+        const int kk = j >> 5, l = j & 31;
+        if (q0 + kk < sh.nj[l]) o_joint_patch(a, slot, q0 + kk, l, out_row(sh, l, kk, K, NVW));
+    }
+}
+
+// Joints [q0, q0 + K) of every world; invalid joints (body index out of
+// range) are left as they were.
+B3X_HD void o_joint_write(const Args& a, int tile, float* slot, OutShared& sh, int q0, int K, int t) {
     const int w = t >> 5, i = t & 31;
     for (int l = w; l < kLanes; l += kCtaWarps) {
-        if (q >= sh.nj[l]) continue;
-        if (!ldi(item(slot + a.SP.joint, q, NJF) + l, JOK)) continue;
-        const float* row = sh.u.jstage[l];
-        float* dst = world_words_w(a, tile * kLanes + l) + (a.L.joint_off + (size_t)B3X_JOINT_BYTES * q) / 4;
-        for (int c = i; c < NVW; c += 32) dst[c] = row[c];
+        const int n = (sh.nj[l] < q0 + K ? sh.nj[l] : q0 + K) - q0;
+        if (n <= 0) continue;
+        float* dst = world_words_w(a, tile * kLanes + l) + (a.L.joint_off + (size_t)B3X_JOINT_BYTES * q0) / 4;
+        for (int idx = i; idx < n * NVW; idx += 32) {
+            const int kk = idx / NVW, c = idx - kk * NVW;
+            if (ldi(item(slot + a.SP.joint, q0 + kk, NJF) + l, JOK)) dst[idx] = out_row(sh, l, kk, K, NVW)[c];
+        }
     }
+}
+
+// Items per write-back round: as many as the staging area holds, balanced.
+B3X_HDI int out_items(int count, int row_floats) {
+    int k = kStageFloats / (kLanes * row_floats);
+    if (k < 1) k = 1;
+    if (count <= 0) return 1;
+    const int rounds = (count + k - 1) / k;
+    return (count + rounds - 1) / rounds;
 }
 
 B3X_HD void o_header(const Args& a, int tile, float* slot, OutShared& sh, int l) {
@@ -918,18 +1029,29 @@ B3X_HD void out_tile(X& x, const Args& a, int bt, OutShared& sh) {
     const int tile = a.tile0 + bt;
     x.each([&](int t) { if (t < kLanes) o_record(a, slot, sh, t); });
     x.each([&](int t) { if (t == 0) o_maxima(sh); });
-    for (int k0 = 0; k0 < sh.maxnb; k0 += kCtaWarps) {
-        x.each([&](int t) { o_bodies(a, slot, sh, k0, t); });
-        x.each([&](int t) { o_body_write(a, tile, sh, k0, t); });
+    {
+        const int K = out_items(sh.maxnb, kRow);
+        for (int k0 = 0; k0 < sh.maxnb; k0 += K) {
+            x.each([&](int t) { o_bodies(a, slot, sh, k0, K, t); });
+            x.each([&](int t) { o_body_write(a, tile, sh, k0, K, t); });
+        }
     }
-    for (int k = 0; k < sh.maxn; k++) {
-        x.each([&](int t) { o_stage(item(slot + a.SP.cont, k, NCW), &sh.u.cstage[0][0], NCW, t); });
-        x.each([&](int t) { o_contact_write(a, tile, sh, k, t); });
+    {
+        const int K = out_items(sh.maxn, NCW);
+        for (int k0 = 0; k0 < sh.maxn; k0 += K) {
+            const int Kr = sh.maxn - k0 < K ? sh.maxn - k0 : K;
+            x.each([&](int t) { o_stage(item(slot + a.SP.cont, k0, NCW), sh, Kr, NCW, NCW, t); });
+            x.each([&](int t) { o_contact_write(a, tile, sh, k0, Kr, t); });
+        }
     }
-    for (int q = 0; q < sh.maxnj; q++) {
-        x.each([&](int t) { o_stage(item(slot + a.SP.jimg, q, NVW), &sh.u.jstage[0][0], NVW, t); });
-        x.each([&](int t) { if (t < kLanes) o_joint_patch(a, slot, sh, q, t); });
-        x.each([&](int t) { o_joint_write(a, tile, slot, sh, q, t); });
+    {
+        const int K = out_items(sh.maxnj, NVW);
+        for (int q0 = 0; q0 < sh.maxnj; q0 += K) {
+            const int Kr = sh.maxnj - q0 < K ? sh.maxnj - q0 : K;
+            x.each([&](int t) { o_stage(item(slot + a.SP.jimg, q0, NVW), sh, Kr, NVW, NVW, t); });
+            x.each([&](int t) { o_joints(a, slot, sh, q0, Kr, t); });
+            x.each([&](int t) { o_joint_write(a, tile, slot, sh, q0, Kr, t); });
+        }
     }
     x.each([&](int t) { if (t < kLanes) o_header(a, tile, slot, sh, t); });
 }
