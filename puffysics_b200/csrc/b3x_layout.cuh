@@ -50,8 +50,11 @@ enum : int {
     WMA = WRM + 9, WMB = WMA + 1, WIA = WMB + 1, WIB = WIA + 9, WSOFT = WIB + 9, NCW = WSOFT + 3
 };
 static_assert(NCW * 4 == B3X_CONTACT_BYTES, "contact word layout");
-// The solver reads / writes contact words [0, kContactStream) only.
-constexpr int kContactStream = WTM + 4;
+// The workspace keeps contact words [0, kCW): everything the solver reads or
+// writes; the write-back derives the rest (masses, inertias, rolling mass,
+// softness) from the body columns.
+constexpr int kCW = WTM + 4;
+constexpr int kContactStream = kCW;
 // B3Joint (115 words)
 enum : int {
     VTYPE = 0, VBA = 1, VBB = 2, VCC = 3, VFIX = 4, VLAA = 5, VLAB = 8, VLRA = 11, VLRB = 15, VCHZ = 19,
@@ -84,9 +87,9 @@ enum : int {
 };
 // warm-start cache of the previous step's contacts
 enum : int { OSA = 0, OSB = 1, OCNT = 2, OFI = 3, OTWI = 5, ORI = 6, OFEAT = 9, ONI = 13, NOF = 17 };
-// narrowphase result of one candidate pair, already relative to the body
-// centers (the reference's b3_contact_from_mani, 08_contacts.inl:5-39)
-enum : int { MCNT = 0, MN = 1, MP = 4, MRA = 0, MRB = 3, MBSEP = 6, MFEAT = 7, NMP = 8, NMF = MP + 4 * NMP };
+// body pose: the first 13 words of B3Body (position, rotation, center,
+// local center)
+enum : int { PPOS = YPOS, PROT = YROT, PCEN = YCEN, PLC = YLC, NPF = YLC + 3 };
 // joints: the solver's columns [0, kJointStream), then the collide filter's
 // collide_connected flag
 enum : int {
@@ -133,11 +136,13 @@ static inline bool layout_from_signature(unsigned long long sig, Layout* L) {
 }
 
 // Word offsets of the regions of one tile's workspace slot.
-// Besides the solver columns, the raw B3Body rows (bimg, [body][word][lane])
-// and the prepared B3Joint rows (jimg) travel from the collide kernel to the
-// write-back, which then writes whole rows.
+// Besides the solver columns, the prepared B3Joint rows (jimg) travel from the
+// collide phase to the write-back, which then writes whole rows.  The contact
+// region holds kPairWindow items beyond the capacity: a pair window first
+// writes each new contact at a provisional slot (the contacts before the
+// window plus its candidate index), then compacts.
 struct Space {
-    unsigned long long rec, body, konst, bimg, shape, old, cand, cont, joint, jimg, tile_words;
+    unsigned long long rec, body, konst, pose, shape, old, cont, joint, jimg, tile_words;
 };
 
 static inline Space space_from_layout(const Layout& L) {
@@ -151,11 +156,10 @@ static inline Space space_from_layout(const Layout& L) {
     s.rec = take(1, NRF);
     s.body = take(L.B, NBF);
     s.konst = take(L.B, NKF);
-    s.bimg = take(L.B, NYW);
+    s.pose = take(L.B, NPF);
     s.shape = take(L.S, NSF);
     s.old = take(L.C, NOF);
-    s.cand = take(kPairWindow, NMF);
-    s.cont = take(L.C, NCW);
+    s.cont = take((unsigned long long)L.C + kPairWindow, kCW);
     s.joint = take(L.J, NJF);
     s.jimg = take(L.J, NVW);
     s.tile_words = (w + 63) & ~63ull;   // 256-byte aligned slots
@@ -213,8 +217,6 @@ B3X_HDI float* item(float* base, int k, int nf) { return base + (size_t)k * nf *
 B3X_HDI const float* item(const float* base, int k, int nf) { return base + (size_t)k * nf * kLanes; }
 // word of contact point p
 B3X_HDI int PW(int p, int f) { return WP + p * NQW + f; }
-// candidate point field
-B3X_HDI int MW(int p, int f) { return MP + p * NMP + f; }
 // body column field of body k (body columns are [body][field][lane])
 B3X_HDI int BI(int k, int f) { return k * NBF + f; }
 

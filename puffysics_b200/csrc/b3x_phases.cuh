@@ -34,7 +34,7 @@ constexpr int kStageFloats = 12 * 1024;
 // ---- block state ------------------------------------------------------------------
 struct CollideShared {
     int live[kLanes], nb[kLanes], ns[kLanes], oldn[kLanes], nj[kLanes];
-    int n[kLanes], nbase[kLanes], ovf[kLanes], drop[kLanes], sorted[kLanes];
+    int n[kLanes], ovf[kLanes], drop[kLanes], sorted[kLanes];
     float grav[kLanes][3];
     int maxnb, maxns, maxold, maxnj;
     // pair window: candidate bits per world over the window's pairs, and the
@@ -51,7 +51,9 @@ struct CollideShared {
         float flat[kStageFloats];                // gathered struct rows of a group of worlds
         float jstage[kLanes][NVW];               // one joint of every world (115: odd)
         float clip[48 * kCta];                   // narrowphase clip polygons
+        uint32_t moves[kPairWindow][kLanes];     // compaction: p | k << 16 of move m of world l
     } u;
+    int nmoves[kLanes], maxmoves;
 };
 
 struct OutShared {
@@ -184,13 +186,13 @@ B3X_HD void c_gather_old(const Args& a, int tile, CollideShared& sh, int l0, int
     for (int j_ = (t), k = j_ / (G), g = j_ - k * (G); j_ < (G) * (M); \
          j_ += kCta, k = j_ / (G), g = j_ - k * (G))
 
-// Body k of world l (row y): solver columns, step constants and the raw row
+// Body k of world l (row y): solver columns, step constants and pose
 // (inverse mass / inertia gated by type as the contact and joint prepares do,
 // 08_contacts.inl:236-239; velocity increments of 09_step.inl:5-18).
 B3X_HD void c_body(const Args& a, float* slot, const CollideShared& sh, int k, int l, const float* y) {
     const float h = a.dt / (float)a.substeps;
     float* bc = item(slot + a.SP.body, k, NBF) + l;
-    float* ic = item(slot + a.SP.bimg, k, NYW) + l;
+    float* pc = item(slot + a.SP.pose, k, NPF) + l;
     const int type = b3x_f2i(y[YTYPE]);
     auto v3 = [&](int f) { return b3_v(y[f], y[f + 1], y[f + 2]); };
     st3(bc, BV, v3(YLV));
@@ -218,7 +220,7 @@ B3X_HD void c_body(const Args& a, float* slot, const CollideShared& sh, int k, i
         COL(bc, BMI) = 0.0f;
         stm(bc, BII, m3_zero());
     }
-    for (int f = 0; f < NYW; f++) COL(ic, f) = y[f];
+    for (int f = 0; f < NPF; f++) COL(pc, f) = y[f];
 }
 
 // Shape s of world l (row y): world pose and padded AABB (04_world.inl:293-336,
@@ -245,9 +247,9 @@ B3X_HD void c_shape(const Args& a, float* slot, const CollideShared& sh, int s, 
         st3(so, SHI, b3_v(-INFINITY, -INFINITY, -INFINITY));
         return;
     }
-    const float* ic = item(slot + a.SP.bimg, body, NYW) + l;
-    const B3Vec3 bp = ld3(ic, YPOS);
-    const B3Quat bq = ldq(ic, YROT);
+    const float* pc = item(slot + a.SP.pose, body, NPF) + l;
+    const B3Vec3 bp = ld3(pc, PPOS);
+    const B3Quat bq = ldq(pc, PROT);
     const B3Vec3 p = b3_xf_point(bp, bq, b3_v(y[XLPOS], y[XLPOS + 1], y[XLPOS + 2]));
     const B3Quat q = b3_qmul(bq, b3_q(y[XLROT], y[XLROT + 1], y[XLROT + 2], y[XLROT + 3]));
     B3Vec3 lo, hi;
@@ -342,8 +344,8 @@ B3X_HD void c_joint(const Args& a, float* slot, CollideShared& sh, int q, int l)
     sti(jo, JOK, 1);
     const float* bca = item(slot + a.SP.body, ja, NBF) + l;
     const float* bcb = item(slot + a.SP.body, jb, NBF) + l;
-    const float* ia_img = item(slot + a.SP.bimg, ja, NYW) + l;
-    const float* ib_img = item(slot + a.SP.bimg, jb, NYW) + l;
+    const float* ia_img = item(slot + a.SP.pose, ja, NPF) + l;
+    const float* ib_img = item(slot + a.SP.pose, jb, NPF) + l;
     const float ma = COL(bca, BMI), mb = COL(bcb, BMI);
     const B3Mat3 ia = ldm(bca, BII), ib = ldm(bcb, BII);
     const B3Mat3 isum = m3_add(ia, ib);
@@ -447,7 +449,10 @@ B3X_HD void c_window_setup(CollideShared& sh, int p0, int npairs, int t) {
             sh.nmask[t][c] = 0;
         }
     }
-    if (t == 0) sh.maxc = 0;
+    if (t == 0) {
+        sh.maxc = 0;
+        sh.maxmoves = 0;
+    }
 }
 
 // Broadphase of window pair pp for world l: the reference's predicate
@@ -515,69 +520,46 @@ B3X_HDI void decode(const CollideShared& sh, int idx, int& ci, int& l) {
     l = nth_bit32(sh.wmask[ci], idx - sh.off[ci]);
 }
 
-// Narrowphase of every candidate of the window (05_collision.inl), stored
-// relative to the body centers (08_contacts.inl:5-39).
-B3X_HD void c_narrow(const Args& a, float* slot, CollideShared& sh, int t) {
-    const float* sc = slot + a.SP.shape;
-    Poly P;
-    P.base = sh.u.clip + t;
-    P.stride = kCta;
-    for (int idx = t; idx < sh.total; idx += kCta) {
-        int ci, l;
-        decode(sh, idx, ci, l);
-        const int pr = sh.ptab[nth_bit64(sh.cmask[l], ci)];
-        const int i = pr & 0xffff, j = pr >> 16;
-        const float* si = item(sc, i, NSF) + l;
-        const float* sj = item(sc, j, NSF) + l;
-        Geo ga, gb;
-        ga.p = ld3(si, SPOS); ga.q = ldq(si, SROT); ga.type = ldi(si, STYPE);
-        ga.radius = COL(si, SRAD); ga.half = ld3(si, SHALF);
-        gb.p = ld3(sj, SPOS); gb.q = ldq(sj, SROT); gb.type = ldi(sj, STYPE);
-        gb.radius = COL(sj, SRAD); gb.half = ld3(sj, SHALF);
-        Mani m;
-        collide(m, ga, gb, P);
-        if (m.count == 0) continue;
-        shared_or(&sh.nmask[l][ci >> 5], 1u << (ci & 31));
-        const float* ic = slot + a.SP.bimg + l;
-        const B3Vec3 ca = ld3(item(ic, ldi(si, SBODY), NYW), YCEN);
-        const B3Vec3 cb = ld3(item(ic, ldi(sj, SBODY), NYW), YCEN);
-        float* md = item(slot + a.SP.cand, ci, NMF) + l;
-        sti(md, MCNT, m.count);
-        st3(md, MN, m.normal);
-#pragma unroll
-        for (int p = 0; p < B3_MAX_MANIFOLD; p++) {
-            if (p >= m.count) continue;
-            B3Vec3 ra = b3_sub(m.pa[p], ca), rb = b3_sub(m.pb[p], cb);
-            st3(md, MW(p, MRA), ra);
-            st3(md, MW(p, MRB), rb);
-            COL(md, MW(p, MBSEP)) = m.sep[p] - b3_dot(b3_sub(rb, ra), m.normal);
-            sti(md, MW(p, MFEAT), (int)m.feat[p]);
-        }
-    }
-}
-
 // Contact slots of world l's candidates in this window (08_contacts.inl:120-134):
 // in candidate order, slots are handed out while the capacity lasts, then
-// overflow is counted.  Candidate ci with a manifold gets slot nbase + (number
-// of earlier candidates with a manifold) when that is below the capacity.
-B3X_HD void c_slots(const Args& a, CollideShared& sh, int l) {
-    int ne = 0;
-    for (int c = 0; c < kPairWindow / 32; c++) ne += popc32(sh.nmask[l][c]);
-    const int n0 = sh.n[l];
-    const int room = a.L.C - n0 > 0 ? a.L.C - n0 : 0;
-    const int kept = ne < room ? ne : room;
-    sh.nbase[l] = n0;
-    sh.n[l] = n0 + kept;
-    if (ne > kept) {
-        sh.ovf[l] = 1;
-        sh.drop[l] += ne - kept;
+// overflow is counted.  The contacts were written at their provisional slots
+// (contacts before the window + candidate index); those that land lower are
+// listed as moves p -> k, in increasing order.
+B3X_HD void c_compact_plan(const Args& a, CollideShared& sh, int l) {
+    const int base = sh.n[l];
+    int n = base, m = 0;
+    for (int ci = 0; ci < sh.ccount[l]; ci++) {
+        if (!((sh.nmask[l][ci >> 5] >> (ci & 31)) & 1u)) continue;
+        if (n >= a.L.C) {
+            sh.ovf[l] = 1;
+            sh.drop[l]++;
+            continue;
+        }
+        const int k = n++, p = base + ci;
+        if (k != p) sh.u.moves[m++][l] = (uint32_t)p | ((uint32_t)k << 16);
     }
+    sh.n[l] = n;
+    sh.nmoves[l] = m;
+    shared_max(&sh.maxmoves, m);
 }
 
-// Number of set bits of a window mask below bit ci.
-B3X_HDI int rank_below(const uint32_t* m, int ci) {
-    if (ci < 32) return popc32(m[0] & ((1u << ci) - 1u));
-    return popc32(m[0]) + popc32(m[1] & ((1u << (ci - 32)) - 1u));
+// Move m of every world (thread: world t % 32, a quarter of the words).  A
+// move's destination is below its own source and above every earlier
+// source but may be an earlier move's source, so rounds go in increasing m.
+B3X_HD void c_compact_move(const Args& a, float* slot, CollideShared& sh, int m, int t) {
+    const int l = t & 31, q = t >> 5;
+    if (m >= sh.nmoves[l]) return;
+    const uint32_t mv = sh.u.moves[m][l];
+    const float* __restrict__ src = item(slot + a.SP.cont, (int)(mv & 0xffffu), kCW) + l;
+    float* __restrict__ dst = item(slot + a.SP.cont, (int)(mv >> 16), kCW) + l;
+    constexpr int kPart = (kCW + kCtaWarps - 1) / kCtaWarps;
+    float v[kPart];
+#pragma unroll
+    for (int f = 0; f < kPart; f++)
+        if (q * kPart + f < kCW) v[f] = COL(src, q * kPart + f);
+#pragma unroll
+    for (int f = 0; f < kPart; f++)
+        if (q * kPart + f < kCW) COL(dst, q * kPart + f) = v[f];
 }
 
 // Warm-cache entries to match for the key (i, j) (08_contacts.inl:136-153):
@@ -614,41 +596,51 @@ B3X_HDI void warm_range(const float* oc, int on, int sorted, int i, int j, int g
     end = lo < on ? lo + 1 : on;
 }
 
-// Build the contact of candidate (ci, l) from its manifold: b3_contact_from_mani
-// (08_contacts.inl:5-39), the warm-start carry (08_contacts.inl:136-171) and
-// b3_prepare_one_contact (08_contacts.inl:234-291).  All 119 words except the
-// point slots past the point count go to the contact's workspace columns.
-B3X_HD void c_prepare(const Args& a, float* slot, CollideShared& sh, int t) {
+// Every candidate of the window (spread over (candidate, world)): the
+// narrowphase (05_collision.inl), and for a manifold the contact built from
+// it -- b3_contact_from_mani (08_contacts.inl:5-39), the warm-start carry
+// (08_contacts.inl:136-171) and b3_prepare_one_contact
+// (08_contacts.inl:234-291) -- written at the provisional slot
+// n + ci (words [0, kCW); point slots past the point count are not written).
+B3X_HD void c_contacts(const Args& a, float* slot, CollideShared& sh, int t) {
     const float* sc = slot + a.SP.shape;
+    Poly P;
+    P.base = sh.u.clip + t;
+    P.stride = kCta;
     for (int idx = t; idx < sh.total; idx += kCta) {
         int ci, l;
         decode(sh, idx, ci, l);
-        if (!((sh.nmask[l][ci >> 5] >> (ci & 31)) & 1u)) continue;
-        const int k = sh.nbase[l] + rank_below(sh.nmask[l], ci);
-        if (k >= a.L.C) continue;
         const int pr = sh.ptab[nth_bit64(sh.cmask[l], ci)];
         const int i = pr & 0xffff, j = pr >> 16;
         const float* si = item(sc, i, NSF) + l;
         const float* sj = item(sc, j, NSF) + l;
-        const float* md = item(slot + a.SP.cand, ci, NMF) + l;
+        Geo ga, gb;
+        ga.p = ld3(si, SPOS); ga.q = ldq(si, SROT); ga.type = ldi(si, STYPE);
+        ga.radius = COL(si, SRAD); ga.half = ld3(si, SHALF);
+        gb.p = ld3(sj, SPOS); gb.q = ldq(sj, SROT); gb.type = ldi(sj, STYPE);
+        gb.radius = COL(sj, SRAD); gb.half = ld3(sj, SHALF);
+        Mani m;
+        collide(m, ga, gb, P);
+        if (m.count == 0) continue;
+        shared_or(&sh.nmask[l][ci >> 5], 1u << (ci & 31));
+
         const int bi = ldi(si, SBODY), bj = ldi(sj, SBODY);
         const float* ba = item(slot + a.SP.body, bi, NBF) + l;
         const float* bb = item(slot + a.SP.body, bj, NBF) + l;
-        const int cnt = ldi(md, MCNT);
-        const B3Vec3 nrm = ld3(md, MN);
+        const B3Vec3 ca = ld3(item(slot + a.SP.pose, bi, NPF) + l, PCEN);
+        const B3Vec3 cb = ld3(item(slot + a.SP.pose, bj, NPF) + l, PCEN);
+        const int cnt = m.count;
+        const int p = sh.n[l] + ci;
+        const B3Vec3 nrm = m.normal;
         const B3Vec3 t1 = b3_perp(nrm);
         const B3Vec3 t2 = b3_cross(t1, nrm);
         const float rest_i = COL(si, SREST), rest_j = COL(sj, SREST);
         const int stat = ldi(ba, BTYPE) != B3_DYNAMIC || ldi(bb, BTYPE) != B3_DYNAMIC;
 
         // warm-start carry by (shape_a, shape_b) and feature id
-        uint32_t feat[B3_MAX_MANIFOLD];
         float ni[B3_MAX_MANIFOLD];
 #pragma unroll
-        for (int p = 0; p < B3_MAX_MANIFOLD; p++) {
-            ni[p] = 0.0f;
-            feat[p] = p < cnt ? (uint32_t)ldi(md, MW(p, MFEAT)) : 0u;
-        }
+        for (int q = 0; q < B3_MAX_MANIFOLD; q++) ni[q] = 0.0f;
         B3Vec2 fi;
         fi.x = 0.0f;
         fi.y = 0.0f;
@@ -656,17 +648,17 @@ B3X_HD void c_prepare(const Args& a, float* slot, CollideShared& sh, int t) {
         B3Vec3 ri = b3_v(0.0f, 0.0f, 0.0f);
         const float* oc = slot + a.SP.old + l;
         int first, end;
-        warm_range(oc, sh.oldn[l], sh.sorted[l], i, j, k, first, end);
+        warm_range(oc, sh.oldn[l], sh.sorted[l], i, j, p, first, end);
         for (int kk = first; kk < end; kk++) {
             const float* o = item(oc, kk, NOF);
             if (ldi(o, OSA) != i || ldi(o, OSB) != j) continue;
             const int ocnt = clampi(ldi(o, OCNT), 0, B3_MAX_MANIFOLD);
 #pragma unroll
-            for (int p = 0; p < B3_MAX_MANIFOLD; p++) {
-                if (p >= cnt) continue;
+            for (int q = 0; q < B3_MAX_MANIFOLD; q++) {
+                if (q >= cnt) continue;
 #pragma unroll
-                for (int q = 0; q < B3_MAX_MANIFOLD; q++)
-                    if (q < ocnt && feat[p] == b3x_f2u(COL(o, OFEAT + q))) ni[p] = COL(o, ONI + q);
+                for (int r = 0; r < B3_MAX_MANIFOLD; r++)
+                    if (r < ocnt && m.feat[q] == b3x_f2u(COL(o, OFEAT + r))) ni[q] = COL(o, ONI + r);
             }
             fi.x = COL(o, OFI);
             fi.y = COL(o, OFI + 1);
@@ -678,17 +670,17 @@ B3X_HD void c_prepare(const Args& a, float* slot, CollideShared& sh, int t) {
         const float ma = COL(ba, BMI), mb = COL(bb, BMI);
         const B3Mat3 ia = ldm(ba, BII), ib = ldm(bb, BII);
         const B3Vec3 va = ld3(ba, BV), wa = ld3(ba, BW), vb = ld3(bb, BV), wb = ld3(bb, BW);
-        float* co = item(slot + a.SP.cont, k, NCW) + l;
+        float* co = item(slot + a.SP.cont, p, kCW) + l;
         const float inv_tau = 1.0f / B3_SPECULATIVE;
         B3Vec3 center_a = b3_v(0.0f, 0.0f, 0.0f), center_b = b3_v(0.0f, 0.0f, 0.0f);
         float wsum = 0.0f;
         B3Vec3 ras[B3_MAX_MANIFOLD];
 #pragma unroll
-        for (int p = 0; p < B3_MAX_MANIFOLD; p++) {
-            if (p >= cnt) continue;
-            const B3Vec3 ra = ld3(md, MW(p, MRA)), rb = ld3(md, MW(p, MRB));
-            const float base_sep = COL(md, MW(p, MBSEP));
-            ras[p] = ra;
+        for (int q = 0; q < B3_MAX_MANIFOLD; q++) {
+            if (q >= cnt) continue;
+            const B3Vec3 ra = b3_sub(m.pa[q], ca), rb = b3_sub(m.pb[q], cb);
+            const float base_sep = m.sep[q] - b3_dot(b3_sub(rb, ra), nrm);
+            ras[q] = ra;
             const B3Vec3 rn_a = b3_cross(ra, nrm), rn_b = b3_cross(rb, nrm);
             const float kn = ma + mb + b3_dot(rn_a, b3_mv(ia, rn_a)) + b3_dot(rn_b, b3_mv(ib, rn_b));
             const float nm = kn > 0.0f ? 1.0f / kn : 0.0f;
@@ -699,28 +691,27 @@ B3X_HD void c_prepare(const Args& a, float* slot, CollideShared& sh, int t) {
             center_a = b3_madd(center_a, wgt, ra);
             center_b = b3_madd(center_b, wgt, rb);
             wsum += wgt;
-            st3(co, PW(p, QRA), ra);
-            st3(co, PW(p, QRB), rb);
-            COL(co, PW(p, QBSEP)) = base_sep;
-            COL(co, PW(p, QRELV)) = relv;
-            COL(co, PW(p, QNI)) = ni[p];
-            COL(co, PW(p, QTOT)) = 0.0f;
-            COL(co, PW(p, QNM)) = nm;
-            sti(co, PW(p, QFEAT), (int)feat[p]);
+            st3(co, PW(q, QRA), ra);
+            st3(co, PW(q, QRB), rb);
+            COL(co, PW(q, QBSEP)) = base_sep;
+            COL(co, PW(q, QRELV)) = relv;
+            COL(co, PW(q, QNI)) = ni[q];
+            COL(co, PW(q, QTOT)) = 0.0f;
+            COL(co, PW(q, QNM)) = nm;
+            sti(co, PW(q, QFEAT), (int)m.feat[q]);
         }
         const float invw = wsum > 0.0f ? 1.0f / wsum : 0.0f;
-        const B3Vec3 ca = b3_mul(center_a, invw), cb = b3_mul(center_b, invw);
+        const B3Vec3 cA = b3_mul(center_a, invw), cB = b3_mul(center_b, invw);
 #pragma unroll
-        for (int p = 0; p < B3_MAX_MANIFOLD; p++)
-            if (p < cnt) COL(co, PW(p, QLEV)) = b3_len(b3_sub(ras[p], ca));
-        const B3Vec3 rta1 = b3_cross(ca, t1), rta2 = b3_cross(ca, t2);
-        const B3Vec3 rtb1 = b3_cross(cb, t1), rtb2 = b3_cross(cb, t2);
+        for (int q = 0; q < B3_MAX_MANIFOLD; q++)
+            if (q < cnt) COL(co, PW(q, QLEV)) = b3_len(b3_sub(ras[q], cA));
+        const B3Vec3 rta1 = b3_cross(cA, t1), rta2 = b3_cross(cA, t2);
+        const B3Vec3 rtb1 = b3_cross(cB, t1), rtb2 = b3_cross(cB, t2);
         B3Mat2 kt2;
         kt2.cx.x = ma + mb + b3_dot(rta1, b3_mv(ia, rta1)) + b3_dot(rtb1, b3_mv(ib, rtb1));
         kt2.cy.y = ma + mb + b3_dot(rta2, b3_mv(ia, rta2)) + b3_dot(rtb2, b3_mv(ib, rtb2));
         kt2.cx.y = kt2.cy.x = b3_dot(rta1, b3_mv(ia, rta2)) + b3_dot(rtb1, b3_mv(ib, rtb2));
-        const B3Mat3 isum = m3_add(ia, ib);
-        const float ktw = b3_dot(nrm, b3_mv(isum, nrm));
+        const float ktw = b3_dot(nrm, b3_mv(m3_add(ia, ib), nrm));
         sti(co, WSA, i);
         sti(co, WSB, j);
         sti(co, WBA, bi);
@@ -730,8 +721,8 @@ B3X_HD void c_prepare(const Args& a, float* slot, CollideShared& sh, int t) {
         st3(co, WN, nrm);
         st3(co, WT1, t1);
         st3(co, WT2, t2);
-        st3(co, WCA, ca);
-        st3(co, WCB, cb);
+        st3(co, WCA, cA);
+        st3(co, WCB, cB);
         COL(co, WFRIC) = sqrtf(COL(si, SFRIC) * COL(sj, SFRIC));
         COL(co, WREST) = rest_i > rest_j ? rest_i : rest_j;
         COL(co, WROLL) = b3_maxf(COL(si, SROLL), COL(sj, SROLL));
@@ -741,13 +732,6 @@ B3X_HD void c_prepare(const Args& a, float* slot, CollideShared& sh, int t) {
         COL(co, WFI + 1) = fi.y;
         st3(co, WRI, ri);
         st22(co, WTM, m2_inv(kt2));
-        stm(co, WRM, m3_inv(isum));
-        COL(co, WMA) = ma;
-        COL(co, WMB) = mb;
-        stm(co, WIA, ia);
-        stm(co, WIB, ib);
-        const float* rec = slot + a.SP.rec + l;
-        sts(co, WSOFT, lds(rec, stat ? RSS : RCS));
     }
 }
 
@@ -842,9 +826,9 @@ B3X_HD void collide_tile(X& x, const Args& a, int bt, CollideShared& sh) {
         x.each([&](int t) { if (t < kLanes) c_count(sh, t); });
         x.each([&](int t) { if (t == 0) c_prefix(sh); });
         if (sh.total == 0) continue;
-        x.each([&](int t) { c_narrow(a, slot, sh, t); });
-        x.each([&](int t) { if (t < kLanes) c_slots(a, sh, t); });
-        x.each([&](int t) { c_prepare(a, slot, sh, t); });
+        x.each([&](int t) { c_contacts(a, slot, sh, t); });
+        x.each([&](int t) { if (t < kLanes) c_compact_plan(a, sh, t); });
+        for (int m = 0; m < sh.maxmoves; m++) x.each([&](int t) { c_compact_move(a, slot, sh, m, t); });
     }
     x.each([&](int t) { if (t < kLanes) c_finish(a, slot, sh, t); });
 }
@@ -879,13 +863,28 @@ B3X_HDI float* out_row(OutShared& sh, int l, int kk, int K, int RS) {
     return sh.flat + (kk * kLanes + l) * RS;
 }
 
-// Finalize body k of world l (09_step.inl:109-130) into its B3Body row: the
-// raw row read by the collide phase with the fields the reference's step
-// writes replaced, so the write-back stores whole rows.
+// Bodies [k0, k0 + K) of every world: each world's run of B3Body rows,
+// gathered from the caller's array (rows stay untouched until written back).
+B3X_HD void o_body_gather(const Args& a, int tile, OutShared& sh, int k0, int K, int t) {
+    const int w = t >> 5, i = t & 31;
+    for (int l = w; l < kLanes; l += kCtaWarps) {
+        const int n = (sh.nb[l] < k0 + K ? sh.nb[l] : k0 + K) - k0;
+        if (n <= 0) continue;
+        const float* src = world_words(a, tile * kLanes + l) + (B3X_WORLD_HEADER_BYTES + (size_t)B3X_BODY_BYTES * k0) / 4;
+        for (int idx = i; idx < n * NYW; idx += 32) {
+            const int kk = idx / NYW, c = idx - kk * NYW;
+            async_copy4(out_row(sh, l, kk, K, kRow) + c, src + idx);
+        }
+    }
+    async_wait();
+}
+
+// Finalize body k of world l (09_step.inl:109-130) in its B3Body row y: the
+// fields the reference's step writes are replaced, the others keep their
+// bytes, so the write-back stores whole rows.
 B3X_HD void o_body(const Args& a, float* slot, int k, int l, float* y) {
     const float* bc = item(slot + a.SP.body, k, NBF) + l;
-    const float* ic = item(slot + a.SP.bimg, k, NYW) + l;
-    for (int f = 0; f < NYW; f++) y[f] = COL(ic, f);
+    auto get3 = [&](int f) { return b3_v(y[f], y[f + 1], y[f + 2]); };
     auto put3 = [&](int f, B3Vec3 v) { y[f] = v.x; y[f + 1] = v.y; y[f + 2] = v.z; };
     auto put4 = [&](int f, B3Quat q) { y[f] = q.v.x; y[f + 1] = q.v.y; y[f + 2] = q.v.z; y[f + 3] = q.s; };
     const int type = ldi(bc, BTYPE);
@@ -895,17 +894,17 @@ B3X_HD void o_body(const Args& a, float* slot, int k, int l, float* y) {
         put3(YAV, ld3(bc, BW));
     }
     if (type != B3_STATIC) {
-        const B3Vec3 center = b3_add(ld3(ic, YCEN), ld3(bc, BDP));
-        const B3Quat rot = b3_qnorm(b3_qmul(ldq(bc, BDQ), ldq(ic, YROT)));
+        const B3Vec3 center = b3_add(get3(YCEN), ld3(bc, BDP));
+        const B3Quat rot = b3_qnorm(b3_qmul(ldq(bc, BDQ), b3_q(y[YROT], y[YROT + 1], y[YROT + 2], y[YROT + 3])));
         put3(YCEN, center);
         put4(YROT, rot);
-        put3(YPOS, b3_sub(center, b3_rotate(rot, ld3(ic, YLC))));
+        put3(YPOS, b3_sub(center, b3_rotate(rot, get3(YLC))));
         put3(YDP, b3_v(0.0f, 0.0f, 0.0f));
         put4(YDQ, b3_q_id());
         put3(YF, b3_v(0.0f, 0.0f, 0.0f));
         put3(YT, b3_v(0.0f, 0.0f, 0.0f));
         if (type == B3_DYNAMIC) {
-            const B3Mat3 iw = b3_world_inv_i(rot, ld3(ic, YII));
+            const B3Mat3 iw = b3_world_inv_i(rot, get3(YII));
             put3(YIW, iw.cx);
             put3(YIW + 3, iw.cy);
             put3(YIW + 6, iw.cz);
@@ -934,13 +933,43 @@ B3X_HD void o_body_write(const Args& a, int tile, OutShared& sh, int k0, int K, 
 }
 
 // Items [k0, k0 + K) of a [item][word][lane] region -> rows, copied
-// asynchronously (`words` words per item, row stride RS).
+// asynchronously (`words` words per item, row stride RS >= words).
 B3X_HD void o_stage(const float* src, OutShared& sh, int K, int words, int RS, int t) {
     for (int idx = t; idx < K * words * kLanes; idx += kCta) {
         const int l = idx & 31, r = idx >> 5, kk = r / words, c = r - kk * words;
         async_copy4(out_row(sh, l, kk, K, RS) + c, src + idx);
     }
     async_wait();
+}
+
+// The words of contact k of world l the workspace does not keep, from the
+// body columns and the step softness, as b3_prepare_one_contact
+// (08_contacts.inl:234-245) computes them.
+B3X_HD void o_contact_fill(const Args& a, float* slot, int l, float* row) {
+    const int ba = b3x_f2i(row[WBA]), bb = b3x_f2i(row[WBB]);
+    const float* ca = item(slot + a.SP.body, ba, NBF) + l;
+    const float* cb = item(slot + a.SP.body, bb, NBF) + l;
+    const B3Mat3 ia = ldm(ca, BII), ib = ldm(cb, BII);
+    const B3Mat3 rm = m3_inv(m3_add(ia, ib));
+    auto put3 = [&](int f, B3Vec3 v) { row[f] = v.x; row[f + 1] = v.y; row[f + 2] = v.z; };
+    auto putm = [&](int f, const B3Mat3& m) { put3(f, m.cx); put3(f + 3, m.cy); put3(f + 6, m.cz); };
+    putm(WRM, rm);
+    row[WMA] = COL(ca, BMI);
+    row[WMB] = COL(cb, BMI);
+    putm(WIA, ia);
+    putm(WIB, ib);
+    const float* rec = slot + a.SP.rec + l;
+    const B3Soft soft = lds(rec, b3x_f2i(row[WSTAT]) ? RSS : RCS);
+    row[WSOFT] = soft.bias_rate;
+    row[WSOFT + 1] = soft.mass_scale;
+    row[WSOFT + 2] = soft.impulse_scale;
+}
+
+B3X_HD void o_contacts(const Args& a, float* slot, OutShared& sh, int k0, int K, int t) {
+    for (int j = t; j < K * kLanes; j += kCta) {
+        const int kk = j >> 5, l = j & 31;
+        if (k0 + kk < sh.n[l]) o_contact_fill(a, slot, l, out_row(sh, l, kk, K, NCW));
+    }
 }
 
 // Contacts [k0, k0 + K) of every world.  Point slots past a contact's point
@@ -1032,6 +1061,7 @@ B3X_HD void out_tile(X& x, const Args& a, int bt, OutShared& sh) {
     {
         const int K = out_items(sh.maxnb, kRow);
         for (int k0 = 0; k0 < sh.maxnb; k0 += K) {
+            x.each([&](int t) { o_body_gather(a, tile, sh, k0, K, t); });
             x.each([&](int t) { o_bodies(a, slot, sh, k0, K, t); });
             x.each([&](int t) { o_body_write(a, tile, sh, k0, K, t); });
         }
@@ -1040,7 +1070,8 @@ B3X_HD void out_tile(X& x, const Args& a, int bt, OutShared& sh) {
         const int K = out_items(sh.maxn, NCW);
         for (int k0 = 0; k0 < sh.maxn; k0 += K) {
             const int Kr = sh.maxn - k0 < K ? sh.maxn - k0 : K;
-            x.each([&](int t) { o_stage(item(slot + a.SP.cont, k0, NCW), sh, Kr, NCW, NCW, t); });
+            x.each([&](int t) { o_stage(item(slot + a.SP.cont, k0, kCW), sh, Kr, kCW, NCW, t); });
+            x.each([&](int t) { o_contacts(a, slot, sh, k0, Kr, t); });
             x.each([&](int t) { o_contact_write(a, tile, sh, k0, Kr, t); });
         }
     }

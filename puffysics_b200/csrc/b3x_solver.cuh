@@ -594,7 +594,7 @@ B3X_HD bool solve_world(const Args& a, float* slot, int lane, float* __restrict_
     const int wn = warp_max(n), wj = warp_max(nj);
     bool any_rest = false;
     // -- warm start contacts, then joints (09_step.inl:160-163)
-    if (!stream_items(P, cc, NCW, kContactStream, wn, [&](int k, const float* src) {
+    if (!stream_items(P, cc, kCW, kContactStream, wn, [&](int k, const float* src) {
             if (k < n) {
                 warm_contact(bc, src);
                 any_rest |= COL(src, WREST) != 0.0f;
@@ -608,8 +608,8 @@ B3X_HD bool solve_world(const Args& a, float* slot, int lane, float* __restrict_
         return false;
 
     auto contact_pass = [&](int use_bias) {
-        return stream_items(P, cc, NCW, kContactStream, wn, [&](int k, const float* src) {
-            if (k < n) solve_contact(bc, src, item(cc, k, NCW), inv_h, contact_speed, use_bias, cs, ss);
+        return stream_items(P, cc, kCW, kContactStream, wn, [&](int k, const float* src) {
+            if (k < n) solve_contact(bc, src, item(cc, k, kCW), inv_h, contact_speed, use_bias, cs, ss);
         });
     };
     auto joint_pass = [&](int use_bias) {
@@ -654,8 +654,8 @@ B3X_HD bool solve_world(const Args& a, float* slot, int lane, float* __restrict_
         // restitution (08_contacts.inl:439-480): skipped when no contact of
         // the warp's worlds has a nonzero coefficient
         if (any_rest) {
-            if (!stream_items(P, cc, NCW, kContactStream, wn, [&](int k, const float* src) {
-                    if (k < n) restitute_contact(bc, src, item(cc, k, NCW), restitution_threshold);
+            if (!stream_items(P, cc, kCW, kContactStream, wn, [&](int k, const float* src) {
+                    if (k < n) restitute_contact(bc, src, item(cc, k, kCW), restitution_threshold);
                 }))
                 return false;
         }
