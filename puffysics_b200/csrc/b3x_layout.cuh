@@ -276,6 +276,27 @@ B3X_HDI void async_copy4(float* dst_shared, const float* src_global) {
     *dst_shared = *src_global;
 #endif
 }
+// The same for the caller's world array, which a step reads once and writes
+// once: its lines are marked first for eviction from L2, so the workspace,
+// which the step re-reads many times, stays resident.
+B3X_HDI void async_copy4_world(float* dst_shared, const float* src_global) {
+#if defined(__CUDA_ARCH__)
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    asm volatile("cp.async.ca.shared.global.L2::cache_hint [%0], [%1], 4, %2;"
+                 ::"r"((uint32_t)__cvta_generic_to_shared(dst_shared)),
+                 "l"(__cvta_generic_to_global(src_global)), "l"(pol) : "memory");
+#else
+    *dst_shared = *src_global;
+#endif
+}
+B3X_HDI void store_world(float* p, float v) {
+#if defined(__CUDA_ARCH__)
+    __stcs(p, v);
+#else
+    *p = v;
+#endif
+}
 B3X_HDI void async_wait() {
 #if defined(__CUDA_ARCH__)
     asm volatile("cp.async.wait_all;" ::: "memory");

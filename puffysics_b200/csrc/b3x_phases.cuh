@@ -86,7 +86,7 @@ B3X_HD void c_header(const Args& a, int tile, CollideShared& sh, int t) {
     if (i < NHW) {
         for (int l = w; l < kLanes; l += kCtaWarps) {
             int wi = tile * kLanes + l;
-            if (wi < a.count) async_copy4(&sh.u.hdr[l][i], world_words(a, wi) + i);
+            if (wi < a.count) async_copy4_world(&sh.u.hdr[l][i], world_words(a, wi) + i);
         }
     }
     async_wait();
@@ -155,7 +155,7 @@ B3X_HD void c_gather_group(const Args& a, int tile, CollideShared& sh, const int
         float* row0 = sh.u.flat + dst + g * M * RS;
         for (int idx = i; idx < words; idx += 32) {
             const int k = idx / PER, c = idx - k * PER;
-            async_copy4(row0 + k * RS + c, src + idx);
+            async_copy4_world(row0 + k * RS + c, src + idx);
         }
     }
 }
@@ -175,7 +175,7 @@ B3X_HD void c_gather_old(const Args& a, int tile, CollideShared& sh, int l0, int
         const int l = l0 + g;
         const float* src = world_words(a, tile * kLanes + l) + a.L.contact_off / 4 + word;
         float* row0 = sh.u.flat + dst + g * M * NOF;
-        for (int k = 0; k < sh.oldn[l]; k++) async_copy4(row0 + k * NOF + i, src + k * (B3X_CONTACT_BYTES / 4));
+        for (int k = 0; k < sh.oldn[l]; k++) async_copy4_world(row0 + k * NOF + i, src + k * (B3X_CONTACT_BYTES / 4));
     }
 }
 
@@ -310,7 +310,7 @@ B3X_HD void c_joint_gather(const Args& a, int tile, CollideShared& sh, int q, in
     for (int l = w; l < kLanes; l += kCtaWarps) {
         if (q >= sh.nj[l]) continue;
         const float* src = world_words(a, tile * kLanes + l) + (a.L.joint_off + (size_t)B3X_JOINT_BYTES * q) / 4;
-        for (int c = i; c < NVW; c += 32) async_copy4(&sh.u.jstage[l][c], src + c);
+        for (int c = i; c < NVW; c += 32) async_copy4_world(&sh.u.jstage[l][c], src + c);
     }
     async_wait();
 }
@@ -873,7 +873,7 @@ B3X_HD void o_body_gather(const Args& a, int tile, OutShared& sh, int k0, int K,
         const float* src = world_words(a, tile * kLanes + l) + (B3X_WORLD_HEADER_BYTES + (size_t)B3X_BODY_BYTES * k0) / 4;
         for (int idx = i; idx < n * NYW; idx += 32) {
             const int kk = idx / NYW, c = idx - kk * NYW;
-            async_copy4(out_row(sh, l, kk, K, kRow) + c, src + idx);
+            async_copy4_world(out_row(sh, l, kk, K, kRow) + c, src + idx);
         }
     }
     async_wait();
@@ -927,7 +927,7 @@ B3X_HD void o_body_write(const Args& a, int tile, OutShared& sh, int k0, int K, 
         float* dst = world_words_w(a, tile * kLanes + l) + (B3X_WORLD_HEADER_BYTES + (size_t)B3X_BODY_BYTES * k0) / 4;
         for (int idx = i; idx < n * NYW; idx += 32) {
             const int kk = idx / NYW, c = idx - kk * NYW;
-            dst[idx] = out_row(sh, l, kk, K, kRow)[c];
+            store_world(dst + idx, out_row(sh, l, kk, K, kRow)[c]);
         }
     }
 }
@@ -985,7 +985,7 @@ B3X_HD void o_contact_write(const Args& a, int tile, OutShared& sh, int k0, int 
             const int kk = idx / NCW, c = idx - kk * NCW;
             const float* row = out_row(sh, l, kk, K, NCW);
             const int cnt = clampi(b3x_f2i(row[WCNT]), 0, B3_MAX_MANIFOLD);
-            if (c < WP + cnt * NQW || c >= WCA) dst[idx] = row[c];
+            if (c < WP + cnt * NQW || c >= WCA) store_world(dst + idx, row[c]);
         }
     }
 }
@@ -1029,7 +1029,7 @@ B3X_HD void o_joint_write(const Args& a, int tile, float* slot, OutShared& sh, i
         float* dst = world_words_w(a, tile * kLanes + l) + (a.L.joint_off + (size_t)B3X_JOINT_BYTES * q0) / 4;
         for (int idx = i; idx < n * NVW; idx += 32) {
             const int kk = idx / NVW, c = idx - kk * NVW;
-            if (ldi(item(slot + a.SP.joint, q0 + kk, NJF) + l, JOK)) dst[idx] = out_row(sh, l, kk, K, NVW)[c];
+            if (ldi(item(slot + a.SP.joint, q0 + kk, NJF) + l, JOK)) store_world(dst + idx, out_row(sh, l, kk, K, NVW)[c]);
         }
     }
 }
