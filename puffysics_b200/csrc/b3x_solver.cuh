@@ -116,6 +116,18 @@ __device__ __forceinline__ bool stage_wait(Pipe& P, int s) {
     P.phase ^= 1u << s;
     return true;
 }
+
+// Copy one block of `bytes` into stage s and wait for it (same bookkeeping as
+// a streamed item).  Returns false if the wait gave up.
+__device__ __forceinline__ bool load_block(Pipe& P, int s, const float* src, uint32_t bytes) {
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) bulk_load(P, s, src, bytes);
+    if (!__all_sync(0xffffffffu, stage_wait(P, s))) {
+        P.ok = 0;
+        return false;
+    }
+    return true;
+}
 #endif
 
 // Run fn(k, col) for k in [0, n), col = item k's column for this lane, items
@@ -592,6 +604,11 @@ B3X_HD bool solve_world(const Args& a, float* slot, int lane, float* __restrict_
     const float restitution_threshold = COL(rec, RRT);
 
     const int wn = warp_max(n), wj = warp_max(nj);
+    // the tile's step constants of its bodies in use (one contiguous block)
+    const uint32_t konst_bytes = (uint32_t)((size_t)warp_max(nb) * NKF * kLanes * sizeof(float));
+    constexpr uint32_t kStageBytesEach = (uint32_t)((size_t)kStreamWords * kLanes * sizeof(float));
+    (void)konst_bytes;
+    (void)kStageBytesEach;
     bool any_rest = false;
     // -- warm start contacts, then joints (09_step.inl:160-163)
     if (!stream_items(P, cc, kCW, kContactStream, wn, [&](int k, const float* src) {
@@ -618,10 +635,18 @@ B3X_HD bool solve_world(const Args& a, float* slot, int lane, float* __restrict_
         });
     };
     for (int s = 0; s < subs; s++) {
-        // integrate velocities (09_step.inl:5-18, 41-53) with the step constants
+        // integrate velocities (09_step.inl:5-18, 41-53) with the step
+        // constants, copied into a stage with one bulk copy when they fit
+        const float* kcs = kc;
+#if defined(__CUDA_ARCH__)
+        if (konst_bytes <= kStageBytesEach) {
+            if (!load_block(P, 0, kc - lane, konst_bytes)) return false;
+            kcs = P.buf + lane;
+        }
+#endif
         for (int k = 0; k < nb; k++) {
             if (ldi(bc, BI(k, BTYPE)) != B3_DYNAMIC) continue;
-            const float* kk = item(kc, k, NKF);
+            const float* kk = item(kcs, k, NKF);
             st3(bc, BI(k, BV), b3_madd(ld3(kk, KDV), COL(kk, KLD), ld3(bc, BI(k, BV))));
             st3(bc, BI(k, BW), b3_madd(ld3(kk, KDW), COL(kk, KAD), ld3(bc, BI(k, BW))));
         }

@@ -109,9 +109,10 @@ __global__ void __launch_bounds__(kCta, 4) step_kernel(Args a) {
     __shared__ int solved;
     DevExec x;
     collide_tile(x, a, blockIdx.x, *reinterpret_cast<CollideShared*>(smem_raw));
-    // the solve's bulk copies (async proxy) reuse memory the collide phase
-    // accessed through the generic proxy
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    // the solve's bulk copies (async proxy) read workspace data every thread
+    // wrote and reuse shared memory the collide phase accessed, both through
+    // the generic proxy: each thread orders its accesses before the barrier
+    asm volatile("fence.proxy.async;" ::: "memory");
     __syncthreads();
     if (threadIdx.x < kLanes) {
         const bool ok = solve_tile<kBodySmem>(a, smem_raw);
