@@ -170,25 +170,40 @@ B3X_HDI bool stream_items(Pipe& P, const float* g, int words, int copy_words, in
 }
 
 // ---- contacts -----------------------------------------------------------------
-// Warm start one contact (08_contacts.inl:194-232, 293-313).
+// Warm start one contact (08_contacts.inl:194-232, 293-313), with the two
+// bodies' velocities kept in registers across the contact's impulses (each
+// body's updates in the reference's order).
 B3X_HDI void warm_contact(float* __restrict__ bc, const float* __restrict__ src) {
     int ba = ldi(src, WBA), bb = ldi(src, WBB);
     int cnt = ldi(src, WCNT);
     float ma = COL(bc, BI(ba, BMI)), mb = COL(bc, BI(bb, BMI));
     B3Mat3 ia = ldm(bc, BI(ba, BII)), ib = ldm(bc, BI(bb, BII));
+    const bool da = body_dynamic_flag(bc, ba), db = body_dynamic_flag(bc, bb);
+    B3Vec3 va = ld3(bc, BI(ba, BV)), wa = ld3(bc, BI(ba, BW));
+    B3Vec3 vb = ld3(bc, BI(bb, BV)), wb = ld3(bc, BI(bb, BW));
+    auto impulse = [](B3Vec3& v, B3Vec3& w, float m, const B3Mat3& i, B3Vec3 r, B3Vec3 p, float s) {
+        v = b3_madd(v, s * m, p);
+        w = b3_add(w, b3_mv(i, b3_mul(b3_cross(r, p), s)));
+    };
     B3Vec3 nrm = ld3(src, WN);
     for (int p = 0; p < B3_MAX_MANIFOLD; p++) {
         if (p >= cnt) break;
         B3Vec3 P = b3_mul(nrm, COL(src, PW(p, QNI)));
-        apply_impulse(bc, ba, ma, ia, ld3(src, PW(p, QRA)), P, -1);
-        apply_impulse(bc, bb, mb, ib, ld3(src, PW(p, QRB)), P, 1);
+        if (da) impulse(va, wa, ma, ia, ld3(src, PW(p, QRA)), P, -1.0f);
+        if (db) impulse(vb, wb, mb, ib, ld3(src, PW(p, QRB)), P, 1.0f);
     }
     B3Vec3 f = b3_add(b3_mul(ld3(src, WT1), COL(src, WFI)), b3_mul(ld3(src, WT2), COL(src, WFI + 1)));
-    apply_impulse(bc, ba, ma, ia, ld3(src, WCA), f, -1);
-    apply_impulse(bc, bb, mb, ib, ld3(src, WCB), f, 1);
+    if (da) impulse(va, wa, ma, ia, ld3(src, WCA), f, -1.0f);
+    if (db) impulse(vb, wb, mb, ib, ld3(src, WCB), f, 1.0f);
     B3Vec3 tr = b3_add(b3_mul(nrm, COL(src, WTWI)), ld3(src, WRI));
-    if (body_dynamic_flag(bc, ba)) st3(bc, BI(ba, BW), b3_sub(ld3(bc, BI(ba, BW)), b3_mv(ia, tr)));
-    if (body_dynamic_flag(bc, bb)) st3(bc, BI(bb, BW), b3_add(ld3(bc, BI(bb, BW)), b3_mv(ib, tr)));
+    if (da) {
+        st3(bc, BI(ba, BV), va);
+        st3(bc, BI(ba, BW), b3_sub(wa, b3_mv(ia, tr)));
+    }
+    if (db) {
+        st3(bc, BI(bb, BV), vb);
+        st3(bc, BI(bb, BW), b3_add(wb, b3_mv(ib, tr)));
+    }
 }
 
 // One contact of a sweep (08_contacts.inl:315-413, rolling 07_packed.inl:24-45).
