@@ -129,6 +129,112 @@ def cpu_reference_run(cfg, steps, warmup, budget_s):
                       "partitions, one pthread per host thread, %.2f s" % (worlds, steps, warmup, cpu_model(), secs)}
 
 
+def reference_gpu_run(cfg, steps, warmup, budget_s=20.0):
+    """Time the reference's own GPU batch step (b3_batch_step_gpu: one thread
+    per AoS world, oracle/_ref/libb3refgpu_<cfg>.so built from the reference
+    sources with its stock nvcc flags) on this GPU: the scene's actions
+    (applied with the reference's b3_apply_* in a per-world kernel) plus one
+    b3_batch_step_gpu per step, CUDA events on the launching stream.  None when
+    there is no GPU or the library was not built."""
+    import ctypes
+    try:
+        import torch
+        if not torch.cuda.is_available():
+            return None
+    except ImportError:
+        return None
+    path = os.path.join(ROOT, "oracle", "_ref", "libb3refgpu_%s.so" % cfg.name)
+    if not os.path.exists(path):
+        return None
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as orc
+    L = ctypes.CDLL(path)
+    vp, sz = ctypes.c_void_p, ctypes.c_size_t
+    L.refgpu_world_bytes.restype = sz
+    L.refgpu_batch_step.argtypes = [vp, sz, sz, ctypes.c_int, ctypes.c_float, ctypes.c_int, vp, vp]
+    L.refgpu_batch_step.restype = ctypes.c_int
+    L.refgpu_apply.argtypes = [vp, sz, sz, ctypes.c_int, ctypes.c_int, ctypes.c_ulonglong, ctypes.c_ulonglong,
+                               ctypes.c_ulonglong, vp]
+    L.refgpu_apply.restype = ctypes.c_int
+    n = min(cfg.worlds, 131072)
+    kind = "ref" if orc.available(cfg.name, "ref") else "port"
+    host = orc.Oracle(cfg.name, kind).build(n, cfg.scene, SEED)
+    wb = host.shape[1]
+    assert wb == L.refgpu_world_bytes()
+    dev = torch.device("cuda", torch.cuda.current_device())
+    worlds = torch.from_numpy(host).to(dev)
+    del host
+    stream = torch.cuda.current_stream(dev)
+    sp = ctypes.c_void_p(stream.cuda_stream)
+    step_no = [0]
+
+    def one():
+        step_no[0] += 1
+        assert L.refgpu_apply(worlds.data_ptr(), wb, 0, n, cfg.scene, SEED, 0, step_no[0], sp) == 0
+        assert L.refgpu_batch_step(worlds.data_ptr(), wb, 0, n, cfg.dt, cfg.substeps, None, sp) == 0
+
+    for _ in range(max(warmup, 3)):
+        one()
+    torch.cuda.synchronize(dev)
+    t0 = time.time()
+    one()
+    torch.cuda.synchronize(dev)
+    est = max(time.time() - t0, 1e-4)
+    k = int(max(3, min(steps or 100, budget_s / est)))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(k):
+        one()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1)
+    return {"value": n * k / (ms / 1e3), "unit": UNIT, "ms_per_step": ms / k, "worlds": n, "steps": k,
+            "kernel": "reference b3_batch_step_gpu (b3_batch.cuh:63-89), one thread per world, nvcc -O3 sm_100a",
+            "note": "the reference's GPU kernel on this GPU, timed like the step (actions + step, events)"}
+
+
+def thread_path_run(cfg, worlds, steps, warmup, stream):
+    """Time this library's per-thread device b3_step (include/puffysics.cuh,
+    one thread per world, libb3thread_<cfg>.so) on a copy of the worlds: the
+    scene's actions plus one launch per step, CUDA events on `stream`."""
+    import torch
+    from puffysics_b200 import engine, synth
+    try:
+        engine.thread_lib(cfg.name)
+    except RuntimeError:
+        return None
+    w = worlds.clone()
+    n = w.shape[0]
+    kind, aidx, nv = cfg.action
+    vals = torch.zeros((n, max(nv, 1)), dtype=torch.float32, device=w.device)
+    step_no = [10 ** 6]
+
+    def one():
+        step_no[0] += 1
+        if nv:
+            assert synth.actions_gpu(vals, n, cfg.scene, SEED, 0, step_no[0], stream) == nv
+            assert engine.batch_apply_gpu(w, kind, aidx, vals, None, stream, cfg.caps) == 0
+        assert engine.thread_step_gpu(cfg.name, w, cfg.dt, cfg.substeps, stream=stream) == 0
+
+    for _ in range(max(warmup, 3)):
+        one()
+    torch.cuda.synchronize(w.device)
+    t0 = time.time()
+    one()
+    torch.cuda.synchronize(w.device)
+    k = int(max(3, min(steps, 10.0 / max(time.time() - t0, 1e-4))))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(k):
+        one()
+    e1.record(stream)
+    torch.cuda.synchronize(w.device)
+    ms = e0.elapsed_time(e1)
+    del w
+    return {"value": n * k / (ms / 1e3), "unit": UNIT, "ms_per_step": ms / k, "worlds": n, "steps": k,
+            "kernel": "per-thread device b3_step of include/puffysics.cuh (one thread per world)"}
+
+
 class ClockSampler:
     """NVML clocks and throttle reasons sampled every 20 ms (read only)."""
 
@@ -190,6 +296,7 @@ def main():
     if args.impl == "reference":
         if rank == 0:
             ref = cpu_reference_run(cfg, args.steps, args.warmup, budget_s=max(30.0, args.cpu_seconds))
+            ref_gpu = reference_gpu_run(cfg, args.steps, args.warmup)
             print(json.dumps({"impl": "reference", "metric": METRIC, "value": ref["value"], "unit": UNIT,
                               "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
                               "ms_per_step": None, "higher_is_better": True, "scaling": "weak",
@@ -199,7 +306,8 @@ def main():
                                          "solver_iters": cfg.joint_iters},
                               "cpu_baseline": ref,
                               "e2e": {"value": ref["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
-                                      "d2h_bytes_per_step": 0}}), flush=True)
+                                      "d2h_bytes_per_step": 0},
+                              "reference_gpu": ref_gpu}), flush=True)
         return
 
     import torch
@@ -388,6 +496,8 @@ def main():
                 "clocks": sampler.summary(),
                 "diagnostics": {"worlds": int(tot[0]), "contacts": int(tot[1]), "overflowed_worlds": int(tot[2]),
                                 "dropped_contacts": int(tot[3])}}
+        if world == 1:
+            line["per_thread_path"] = thread_path_run(cfg, worlds, K, args.warmup, stream)
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_reference_run(cfg, steps=None, warmup=2, budget_s=args.cpu_seconds)
         print(json.dumps(line), flush=True)

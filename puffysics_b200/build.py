@@ -24,11 +24,19 @@ HEADERS = [os.path.join(ROOT, "include", "puffysics_b200.h"),
            os.path.join(PKG, "csrc", "b3x_phases.cuh"),
            os.path.join(PKG, "scenes", "b3_scenes.h")]
 SCENES_SRC = os.path.join(PKG, "scenes", "b3_scenes_host.c")
+THREAD_SRC = os.path.join(PKG, "csrc", "b3x_thread_step.cu")
+THREAD_HEADERS = [os.path.join(ROOT, "include", "puffysics.cuh"),
+                  os.path.join(PKG, "csrc", "b3x_world_step.cuh")]
 # capacity configurations the host scene builders are compiled for:
 # name -> (bodies, shapes, contacts, joints)
 SCENE_CONFIGS = {"hover": (2, 2, 4, 1), "stack": (9, 9, 32, 1), "chain": (12, 12, 32, 10),
                  "pile": (37, 37, 128, 1), "hovertask": (2, 2, 4, 2), "default": (80, 128, 128, 32),
                  "stacksmall": (9, 9, 4, 1)}
+# per-thread step launchers (include/puffysics.cuh's device b3_step): name ->
+# (bodies, shapes, contacts, joints, B3_JOINT_ITERS), the capacities of the
+# benchmark configurations and of the reference's defaults
+THREAD_CONFIGS = {"hover": (2, 2, 4, 1, 8), "stack": (9, 9, 32, 1, 8), "chain": (12, 12, 32, 10, 8),
+                  "pile": (37, 37, 128, 1, 8), "hovertask": (2, 2, 4, 2, 2), "default": (80, 128, 128, 32, 2)}
 CC = os.environ.get("CC", "gcc")
 
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc" if os.path.exists("/usr/local/cuda/bin/nvcc") else "nvcc")
@@ -44,6 +52,36 @@ def nvcc_cmd(out=LIB, extra=()):
             + list(extra) + SOURCES + ["-o", out])
 
 
+def thread_lib(name):
+    return os.path.join(LIB_DIR, "libb3thread_%s.so" % name)
+
+
+def thread_cmd(name):
+    b, s, c, j, it = THREAD_CONFIGS[name]
+    caps = ["-DB3_MAX_BODIES=%d" % b, "-DB3_MAX_SHAPES=%d" % s, "-DB3_MAX_CONTACTS=%d" % c,
+            "-DB3_MAX_JOINTS=%d" % j, "-DB3_JOINT_ITERS=%d" % it]
+    return ([NVCC] + ARCH + ["-lineinfo", "-O3", "-std=c++17"] + PARITY
+            + ["-Xcompiler", "-fPIC,-fvisibility=hidden", "-shared", "-cudart", "static",
+               "-I" + os.path.join(ROOT, "include"), "-I" + os.path.join(PKG, "csrc")]
+            + caps + [THREAD_SRC, "-o", thread_lib(name)])
+
+
+def build_thread_libs(force=False):
+    """The per-thread step launchers, one per capacity configuration, compiled
+    concurrently."""
+    deps = [THREAD_SRC, __file__] + HEADERS + THREAD_HEADERS
+    todo = [n for n in THREAD_CONFIGS if force or _newer(thread_lib(n), deps)]
+    procs = [(n, subprocess.Popen(thread_cmd(n), stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True))
+             for n in todo]
+    errors = []
+    for n, p in procs:
+        out, _ = p.communicate()
+        if p.returncode != 0:
+            errors.append("per-thread library %s failed:\n%s\n%s" % (n, " ".join(thread_cmd(n)), out))
+    if errors:
+        raise RuntimeError("\n".join(errors))
+
+
 def scenes_lib(name):
     return os.path.join(LIB_DIR, "libb3scenes_%s.so" % name)
 
@@ -57,7 +95,9 @@ def _newer(out, deps):
 
 def up_to_date():
     deps = SOURCES + HEADERS + [__file__]
-    return not _newer(LIB, deps) and not any(_newer(scenes_lib(n), [SCENES_SRC] + HEADERS) for n in SCENE_CONFIGS)
+    thread_deps = [THREAD_SRC, __file__] + HEADERS + THREAD_HEADERS
+    return (not _newer(LIB, deps) and not any(_newer(scenes_lib(n), [SCENES_SRC] + HEADERS) for n in SCENE_CONFIGS)
+            and not any(_newer(thread_lib(n), thread_deps) for n in THREAD_CONFIGS))
 
 
 def build_scenes(force=False):
@@ -83,6 +123,7 @@ def build(force=False, verbose=False):
         return LIB
     os.makedirs(LIB_DIR, exist_ok=True)
     build_scenes(force)
+    build_thread_libs(force)
     if not force and not _newer(LIB, SOURCES + HEADERS + [__file__]):
         return LIB
     cmd = nvcc_cmd(extra=["-Xptxas", "-v"] if verbose else [])

@@ -11,6 +11,11 @@
 #include "puffysics_b200.h"
 #include "b3x_math.cuh"
 
+// Linkage of the out-of-line narrowphase functions (external in the library).
+#ifndef B3X_NARROW
+#define B3X_NARROW B3X_HD
+#endif
+
 namespace b3x {
 
 struct Mani {
@@ -75,7 +80,7 @@ static_assert(B3_MAX_MANIFOLD == 4, "manifold slots");
 B3X_HDI float rsq(float x) { return 1.0f / sqrtf(x); }
 
 // 05_collision.inl:5-13
-B3X_HD B3Vec3 closest_on_segment(B3Vec3 a, B3Vec3 b, B3Vec3 p) {
+B3X_NARROW B3Vec3 closest_on_segment(B3Vec3 a, B3Vec3 b, B3Vec3 p) {
     B3Vec3 ab = b3_sub(b, a);
     float d = b3_len2(ab);
     if (d <= 1.0e-12f) return a;
@@ -84,7 +89,7 @@ B3X_HD B3Vec3 closest_on_segment(B3Vec3 a, B3Vec3 b, B3Vec3 p) {
 }
 
 // 05_collision.inl:15-55
-B3X_HD void closest_between_segments(B3Vec3 a1, B3Vec3 a2, B3Vec3 b1, B3Vec3 b2, B3Vec3* pa, B3Vec3* pb) {
+B3X_NARROW void closest_between_segments(B3Vec3 a1, B3Vec3 a2, B3Vec3 b1, B3Vec3 b2, B3Vec3* pa, B3Vec3* pb) {
     B3Vec3 d1 = b3_sub(a2, a1);
     B3Vec3 d2 = b3_sub(b2, b1);
     B3Vec3 r = b3_sub(a1, b1);
@@ -124,7 +129,7 @@ B3X_HD void closest_between_segments(B3Vec3 a1, B3Vec3 a2, B3Vec3 b1, B3Vec3 b2,
 }
 
 // 05_collision.inl:83-98
-B3X_HD void sphere_sphere(Mani& m, B3Vec3 ca, float ra, B3Vec3 cb, float rb, uint32_t f) {
+B3X_NARROW void sphere_sphere(Mani& m, B3Vec3 ca, float ra, B3Vec3 cb, float rb, uint32_t f) {
     m_clear(m);
     B3Vec3 d = b3_sub(cb, ca);
     float dist2 = b3_len2(d);
@@ -137,7 +142,7 @@ B3X_HD void sphere_sphere(Mani& m, B3Vec3 ca, float ra, B3Vec3 cb, float rb, uin
 }
 
 // 05_collision.inl:100-129
-B3X_HD B3Vec3 closest_on_box(B3Vec3 c, B3Quat q, B3Vec3 half, B3Vec3 p, int* inside, int* face) {
+B3X_NARROW B3Vec3 closest_on_box(B3Vec3 c, B3Quat q, B3Vec3 half, B3Vec3 p, int* inside, int* face) {
     B3Vec3 local = b3_inv_rotate(q, b3_sub(p, c));
     B3Vec3 cl = b3_v(b3_clamp(local.x, -half.x, half.x), b3_clamp(local.y, -half.y, half.y),
         b3_clamp(local.z, -half.z, half.z));
@@ -164,7 +169,7 @@ B3X_HD B3Vec3 closest_on_box(B3Vec3 c, B3Quat q, B3Vec3 half, B3Vec3 p, int* ins
 }
 
 // 05_collision.inl:131-150
-B3X_HD void ball_vs_point(Mani& m, B3Vec3 p, float r, B3Vec3 q, int inside, B3Vec3 n_fb, uint32_t f) {
+B3X_NARROW void ball_vs_point(Mani& m, B3Vec3 p, float r, B3Vec3 q, int inside, B3Vec3 n_fb, uint32_t f) {
     B3Vec3 d = b3_sub(p, q);
     float dist2 = b3_len2(d);
     if (!inside && dist2 > r * r) return;
@@ -183,7 +188,7 @@ B3X_HD void ball_vs_point(Mani& m, B3Vec3 p, float r, B3Vec3 q, int inside, B3Ve
 }
 
 // 05_collision.inl:152-162
-B3X_HD void sphere_box(Mani& m, B3Vec3 sc, float r, B3Vec3 bc, B3Quat bq, B3Vec3 half) {
+B3X_NARROW void sphere_box(Mani& m, B3Vec3 sc, float r, B3Vec3 bc, B3Quat bq, B3Vec3 half) {
     m_clear(m);
     int inside, face;
     B3Vec3 q = closest_on_box(bc, bq, half, sc, &inside, &face);
@@ -194,7 +199,7 @@ B3X_HD void sphere_box(Mani& m, B3Vec3 sc, float r, B3Vec3 bc, B3Quat bq, B3Vec3
 }
 
 // 05_collision.inl:164-175
-B3X_HD void capsule_box(Mani& m, B3Vec3 c1, B3Vec3 c2, float r, B3Vec3 bc, B3Quat bq, B3Vec3 half) {
+B3X_NARROW void capsule_box(Mani& m, B3Vec3 c1, B3Vec3 c2, float r, B3Vec3 bc, B3Quat bq, B3Vec3 half) {
     m_clear(m);
     B3Vec3 mid = b3_mul(b3_add(c1, c2), 0.5f);
     int inside, face;
@@ -260,7 +265,7 @@ B3X_HDI bool sat_edge(float e, float ra, float rb, B3Vec3 cr, float& best, B3Vec
 
 // Sutherland-Hodgman step against one plane, at most 8 output vertices
 // (05_collision.inl:203-228).
-B3X_HD int clip_against(const Poly& in, int n, const Poly& out, B3Vec3 pn, float po) {
+B3X_NARROW int clip_against(const Poly& in, int n, const Poly& out, B3Vec3 pn, float po) {
     if (n <= 0) return 0;
     int c = 0;
     B3Vec3 prev = in.get(n - 1);
@@ -283,7 +288,7 @@ B3X_HD int clip_against(const Poly& in, int n, const Poly& out, B3Vec3 pn, float
 }
 
 // Separating-axis box-box with reference-face clipping (05_collision.inl:295-461).
-B3X_HD void box_box(Mani& m, const Obb& a, const Obb& b, const Poly& P) {
+B3X_NARROW void box_box(Mani& m, const Obb& a, const Obb& b, const Poly& P) {
     m_clear(m);
     B3Vec3 d = b3_sub(b.c, a.c);
     float t0 = b3_dot(d, a.ax[0]), t1 = b3_dot(d, a.ax[1]), t2 = b3_dot(d, a.ax[2]);
@@ -397,7 +402,7 @@ B3X_HDI void m_flip(Mani& m) {
 }
 
 // Pair dispatch by type with the A->B normal convention (05_collision.inl:472-534).
-B3X_HD void collide(Mani& m, Geo a, Geo b, const Poly& P) {
+B3X_NARROW void collide(Mani& m, Geo a, Geo b, const Poly& P) {
     B3Vec3 center_a = a.p, center_b = b.p;
     bool flip = false;
     if (a.type > b.type) {

@@ -1,0 +1,53 @@
+// b3x_thread_step.cu -- launchers of the header's per-thread device b3_step
+// (include/puffysics.cuh), built once per capacity configuration into
+// libb3thread_<config>.so.
+//
+// These are the entry points of the compatibility path: one thread steps one
+// world in place (the reference's own GPU form, b3_batch.cuh:63-89, with this
+// library's device step).  They exist so that the per-thread step can be
+// checked against the reference on the GPU and timed beside the batched
+// kernel; the capacities (B3_MAX_*) and solver iteration counts
+// (B3_JOINT_ITERS, B3_RELAX_ITERS) are those this file is compiled with.
+#include <cmath>
+
+#include <cuda_runtime.h>
+
+#include "puffysics.cuh"
+
+#define B3T_API extern "C" __attribute__((visibility("default")))
+
+namespace {
+
+constexpr int kThreads = 32;   // one warp per block, as the reference launches
+
+__global__ void thread_batch_kernel(B3Batch batch, float dt, int substeps, const unsigned char* active) {
+    size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < (size_t)batch.count && (!active || active[i])) b3_step(b3_batch_world(batch, (int)i), dt, substeps);
+}
+
+}  // namespace
+
+// Capacity signature the library was compiled for (B3_CONFIG_SIGNATURE).
+B3T_API unsigned long long b3x_thread_signature(void) { return B3_CONFIG_SIGNATURE; }
+B3T_API int b3x_thread_joint_iters(void) { return B3_JOINT_ITERS; }
+B3T_API int b3x_thread_relax_iters(void) { return B3_RELAX_ITERS; }
+
+// b3_batch_step_gpu semantics (b3_batch.cuh:81-89): invalid batch, dt not
+// finite or negative, or substeps < 1 -> cudaErrorInvalidValue with no
+// launch; count == 0 or dt == 0 -> no-op; otherwise one thread per world on
+// `stream`, no allocation, no synchronisation.
+B3T_API int b3x_thread_step_gpu(B3Batch batch, float dt, int substeps, const unsigned char* active, void* stream) {
+    if (!b3_batch_valid(batch) || !std::isfinite(dt) || dt < 0.0f || substeps < 1) return (int)cudaErrorInvalidValue;
+    if (batch.count == 0 || dt == 0.0f) return (int)cudaSuccess;
+    unsigned blocks = ((unsigned)batch.count + kThreads - 1) / kThreads;
+    thread_batch_kernel<<<blocks, kThreads, 0, (cudaStream_t)stream>>>(batch, dt, substeps, active);
+    return (int)cudaGetLastError();
+}
+
+// b3_step_kernel (reference 09_step.inl:325-333) over contiguous worlds.
+B3T_API int b3x_thread_step_worlds_gpu(B3World* worlds, int n, float dt, int substeps, void* stream) {
+    if (n < 0 || (n > 0 && !worlds)) return (int)cudaErrorInvalidValue;
+    if (n == 0) return (int)cudaSuccess;
+    b3_step_kernel<<<(n + kThreads - 1) / kThreads, kThreads, 0, (cudaStream_t)stream>>>(worlds, n, dt, substeps);
+    return (int)cudaGetLastError();
+}

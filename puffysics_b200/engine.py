@@ -129,3 +129,41 @@ def step_launches(caps, count, device=0):
 
 def world_bytes(caps):
     return lib().b3x_world_bytes(layout.signature(*caps))
+
+
+# ---- per-thread device b3_step (include/puffysics.cuh) ------------------------------
+_thread_libs = {}
+
+
+def thread_lib(name):
+    """libb3thread_<name>.so: launchers of the header's per-thread device
+    b3_step compiled with the capacities of configuration `name` (raises if it
+    has not been built)."""
+    if name not in _thread_libs:
+        path = os.path.join(_PKG, "_lib", "libb3thread_%s.so" % name)
+        if not os.path.exists(path):
+            raise RuntimeError("%s is not built; run python -m puffysics_b200.build" % path)
+        L = ctypes.CDLL(path)
+        L.b3x_thread_signature.restype = ctypes.c_ulonglong
+        L.b3x_thread_joint_iters.restype = ctypes.c_int
+        L.b3x_thread_relax_iters.restype = ctypes.c_int
+        L.b3x_thread_step_gpu.argtypes = [B3Batch, ctypes.c_float, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]
+        L.b3x_thread_step_gpu.restype = ctypes.c_int
+        L.b3x_thread_step_worlds_gpu.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_int,
+                                                 ctypes.c_void_p]
+        L.b3x_thread_step_worlds_gpu.restype = ctypes.c_int
+        _thread_libs[name] = L
+    return _thread_libs[name]
+
+
+def thread_step_gpu(name, worlds, dt, substeps, active=None, stream=None, stride=None, offset=0, count=None):
+    """Step the selected worlds with one thread per world (device b3_step over
+    a batch, b3_batch_step_gpu semantics).  Returns a cudaError_t code."""
+    b = make_batch(worlds, stride, offset, count)
+    return thread_lib(name).b3x_thread_step_gpu(b, dt, substeps, _ptr(active), _stream(stream))
+
+
+def thread_step_worlds_gpu(name, worlds, dt, substeps, stream=None):
+    """b3_step_kernel over contiguous worlds (a (count, sizeof(B3World)) tensor)."""
+    return thread_lib(name).b3x_thread_step_worlds_gpu(_ptr(worlds) if worlds.numel() else None, worlds.shape[0],
+                                                       dt, substeps, _stream(stream))

@@ -100,3 +100,58 @@ def test_product_scene_builder_matches_reference_builder(name):
     ours = SceneLib(cfg).build(6, 4242, first=10)
     theirs = orc.Oracle(name, kind).build(6, cfg.scene, 4242, first=10)
     assert np.array_equal(ours, theirs)
+
+
+THREAD_EXPORTS = ["b3x_thread_signature", "b3x_thread_joint_iters", "b3x_thread_relax_iters",
+                  "b3x_thread_step_gpu", "b3x_thread_step_worlds_gpu"]
+
+
+@pytest.mark.parametrize("name", sorted(build.THREAD_CONFIGS))
+def test_thread_libraries_export_launchers(lib, name):
+    """libb3thread_<cfg>.so (include/puffysics.cuh's device b3_step) loads,
+    exports its launchers, reports its capacities, and rejects invalid
+    arguments before any device call."""
+    from puffysics_b200 import engine
+    L = engine.thread_lib(name)
+    for n in THREAD_EXPORTS:
+        assert hasattr(L, n)
+    b, s, c, j, it = build.THREAD_CONFIGS[name]
+    assert L.b3x_thread_signature() == layout.signature(b, s, c, j)
+    assert L.b3x_thread_joint_iters() == it and L.b3x_thread_relax_iters() == it
+    wb = layout.world_bytes(b, s, c, j)
+    bad = [engine.B3Batch(None, wb, 0, 3), engine.B3Batch(None, wb, 0, -1), engine.B3Batch(64, wb - 8, 0, 1),
+           engine.B3Batch(64, wb, 8, 1)]
+    for bt in bad:
+        assert L.b3x_thread_step_gpu(bt, 1 / 60, 4, None, None) == 1
+    ok = engine.B3Batch(64, wb, 0, 1)
+    assert L.b3x_thread_step_gpu(ok, float("inf"), 4, None, None) == 1
+    assert L.b3x_thread_step_gpu(ok, 1 / 60, 0, None, None) == 1
+    assert L.b3x_thread_step_gpu(engine.B3Batch(None, wb, 0, 0), 1 / 60, 4, None, None) == 0
+    assert L.b3x_thread_step_worlds_gpu(None, -1, 1 / 60, 4, None) == 1
+    assert L.b3x_thread_step_worlds_gpu(None, 0, 1 / 60, 4, None) == 0
+
+
+def test_device_b3_step_in_adapter_kernels(tmp_path):
+    """An adapter that calls b3_step from its own kernel, in two translation
+    units that both include "puffysics.cuh", compiles for sm_100a and links
+    (the header's device step has no duplicate external symbols)."""
+    a = tmp_path / "env_a.cu"
+    b = tmp_path / "env_b.cu"
+    body = ('#include "puffysics.cuh"\n'
+            "typedef struct Env { float reward; B3World world; } Env;\n"
+            "__global__ void %s(Env* envs, int n) {\n"
+            "  int i = blockIdx.x * blockDim.x + threadIdx.x;\n"
+            "  if (i < n) { b3_apply_force(&envs[i].world, 1, b3_v(0, 1, 0));\n"
+            "    b3_step(&envs[i].world, 1.0f / 60.0f, 4); envs[i].reward = envs[i].world.bodies[1].position.y; }\n"
+            "}\n")
+    a.write_text(body % "step_a" + "void launch_b(Env*, int);\n"
+                 "void launch_a(Env* e, int n) { step_a<<<(n + 31) / 32, 32>>>(e, n);"
+                 " b3_step_kernel<<<1, 32>>>(nullptr, 0, 0.0f, 1); launch_b(e, n); }\n")
+    b.write_text(body % "step_b" + "void launch_b(Env* e, int n) { step_b<<<(n + 31) / 32, 32>>>(e, n); }\n"
+                 "int main() { return 0; }\n")
+    out = tmp_path / "adapter"
+    cmd = [build.NVCC] + build.ARCH + ["-O1", "-std=c++17", "-DB3_MAX_BODIES=2", "-DB3_MAX_SHAPES=2",
+                                       "-DB3_MAX_CONTACTS=4", "-DB3_MAX_JOINTS=1",
+                                       "-I" + os.path.join(ROOT, "include"), str(a), str(b), "-o", str(out)]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    assert res.returncode == 0, res.stdout + res.stderr
