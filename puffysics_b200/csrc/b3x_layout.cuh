@@ -54,7 +54,13 @@ static_assert(NCW * 4 == B3X_CONTACT_BYTES, "contact word layout");
 // writes; the write-back derives the rest (masses, inertias, rolling mass,
 // softness) from the body columns.
 constexpr int kCW = WTM + 4;
-constexpr int kContactStream = kCW;
+// A workspace contact item is those words, then the separation of each point
+// as the last relax sweep computed it (WSEP + p): positions do not move
+// between a substep's relax sweep and the next substep's bias sweep, so that
+// sweep reads the separations instead of recomputing them.
+constexpr int WSEP = kCW;
+constexpr int kCI = kCW + B3_MAX_MANIFOLD;
+constexpr int kContactStream = kCI;
 // B3Joint (115 words)
 enum : int {
     VTYPE = 0, VBA = 1, VBB = 2, VCC = 3, VFIX = 4, VLAA = 5, VLAB = 8, VLRA = 11, VLRB = 15, VCHZ = 19,
@@ -74,9 +80,12 @@ enum : int {
     RLIVE = 0, RNB = 1, RNS = 2, ROLDN = 3, RNJ = 4, RN = 5, ROVF = 6, RDROP = 7, RSPEED = 8, RRT = 9,
     RMAXLIN = 10, RCS = 11, RSS = 14, NRF = 17
 };
-// body solver state: velocities, pose deltas, type-gated inverse mass and
-// world inverse inertia, flags, type
-enum : int { BV = 0, BW = 3, BDP = 6, BDQ = 9, BMI = 13, BII = 14, BFLAGS = 23, BTYPE = 24, NBF = 25 };
+// body solver state (region body): velocities and pose deltas, the fields
+// the solver writes
+enum : int { BV = 0, BW = 3, BDP = 6, BDQ = 9, NBF = 13 };
+// body constants of the step (region bodyk): inverse mass and world inverse
+// inertia gated by type, flags, type
+enum : int { BMI = 0, BII = 1, BFLAGS = 10, BTYPE = 11, NBC = 12 };
 // per-body step constants: velocity / spin increments and damping factors
 // of b3_integrate_velocity_state, constant over the substeps
 enum : int { KDV = 0, KDW = 3, KLD = 6, KAD = 7, NKF = 8 };
@@ -142,7 +151,7 @@ static inline bool layout_from_signature(unsigned long long sig, Layout* L) {
 // writes each new contact at a provisional slot (the contacts before the
 // window plus its candidate index), then compacts.
 struct Space {
-    unsigned long long rec, body, konst, pose, shape, old, cont, joint, jimg, tile_words;
+    unsigned long long rec, body, bodyk, konst, pose, shape, old, cont, joint, jimg, tile_words;
 };
 
 static inline Space space_from_layout(const Layout& L) {
@@ -155,11 +164,12 @@ static inline Space space_from_layout(const Layout& L) {
     };
     s.rec = take(1, NRF);
     s.body = take(L.B, NBF);
+    s.bodyk = take(L.B, NBC);
     s.konst = take(L.B, NKF);
     s.pose = take(L.B, NPF);
     s.shape = take(L.S, NSF);
     s.old = take(L.C, NOF);
-    s.cont = take((unsigned long long)L.C + kPairWindow, kCW);
+    s.cont = take((unsigned long long)L.C + kPairWindow, kCI);
     s.joint = take(L.J, NJF);
     s.jimg = take(L.J, NVW);
     s.tile_words = (w + 63) & ~63ull;   // 256-byte aligned slots
@@ -219,6 +229,8 @@ B3X_HDI const float* item(const float* base, int k, int nf) { return base + (siz
 B3X_HDI int PW(int p, int f) { return WP + p * NQW + f; }
 // body column field of body k (body columns are [body][field][lane])
 B3X_HDI int BI(int k, int f) { return k * NBF + f; }
+// constant field f of body k (bodyk columns are [body][field][lane])
+B3X_HDI int BK(int k, int f) { return k * NBC + f; }
 
 B3X_HDI int clampi(int v, int lo, int hi) { return v < lo ? lo : (v > hi ? hi : v); }
 

@@ -192,6 +192,7 @@ B3X_HD void c_gather_old(const Args& a, int tile, CollideShared& sh, int l0, int
 B3X_HD void c_body(const Args& a, float* slot, const CollideShared& sh, int k, int l, const float* y) {
     const float h = a.dt / (float)a.substeps;
     float* bc = item(slot + a.SP.body, k, NBF) + l;
+    float* kb = item(slot + a.SP.bodyk, k, NBC) + l;
     float* pc = item(slot + a.SP.pose, k, NPF) + l;
     const int type = b3x_f2i(y[YTYPE]);
     auto v3 = [&](int f) { return b3_v(y[f], y[f + 1], y[f + 2]); };
@@ -199,16 +200,16 @@ B3X_HD void c_body(const Args& a, float* slot, const CollideShared& sh, int k, i
     st3(bc, BW, v3(YAV));
     st3(bc, BDP, v3(YDP));
     stq(bc, BDQ, b3_q(y[YDQ], y[YDQ + 1], y[YDQ + 2], y[YDQ + 3]));
-    COL(bc, BFLAGS) = y[YFLAGS];
-    COL(bc, BTYPE) = y[YTYPE];
+    COL(kb, BFLAGS) = y[YFLAGS];
+    COL(kb, BTYPE) = y[YTYPE];
     if (type == B3_DYNAMIC) {
         const float inv_mass = y[YIM];
         B3Mat3 iw;
         iw.cx = v3(YIW);
         iw.cy = v3(YIW + 3);
         iw.cz = v3(YIW + 6);
-        COL(bc, BMI) = inv_mass;
-        stm(bc, BII, iw);
+        COL(kb, BMI) = inv_mass;
+        stm(kb, BII, iw);
         float* kc = item(slot + a.SP.konst, k, NKF) + l;
         const B3Vec3 gravity = b3_v(sh.grav[l][0], sh.grav[l][1], sh.grav[l][2]);
         const float gs = inv_mass > 0.0f ? y[YGS] : 0.0f;
@@ -217,8 +218,8 @@ B3X_HD void c_body(const Args& a, float* slot, const CollideShared& sh, int k, i
         COL(kc, KLD) = 1.0f / (1.0f + h * y[YLD]);
         COL(kc, KAD) = 1.0f / (1.0f + h * y[YAD]);
     } else {
-        COL(bc, BMI) = 0.0f;
-        stm(bc, BII, m3_zero());
+        COL(kb, BMI) = 0.0f;
+        stm(kb, BII, m3_zero());
     }
     for (int f = 0; f < NPF; f++) COL(pc, f) = y[f];
 }
@@ -342,8 +343,8 @@ B3X_HD void c_joint(const Args& a, float* slot, CollideShared& sh, int q, int l)
         return;
     }
     sti(jo, JOK, 1);
-    const float* bca = item(slot + a.SP.body, ja, NBF) + l;
-    const float* bcb = item(slot + a.SP.body, jb, NBF) + l;
+    const float* bca = item(slot + a.SP.bodyk, ja, NBC) + l;
+    const float* bcb = item(slot + a.SP.bodyk, jb, NBC) + l;
     const float* ia_img = item(slot + a.SP.pose, ja, NPF) + l;
     const float* ib_img = item(slot + a.SP.pose, jb, NPF) + l;
     const float ma = COL(bca, BMI), mb = COL(bcb, BMI);
@@ -474,8 +475,8 @@ B3X_HD void c_broadphase(const Args& a, float* slot, CollideShared& sh, int npw,
             continue;
         const int bi = ldi(si, SBODY), bj = ldi(sj, SBODY);
         if (bi == bj) continue;
-        const float* bc = slot + a.SP.body + l;
-        if (ldi(item(bc, bi, NBF), BTYPE) == B3_STATIC && ldi(item(bc, bj, NBF), BTYPE) == B3_STATIC) continue;
+        const float* kb = slot + a.SP.bodyk + l;
+        if (ldi(item(kb, bi, NBC), BTYPE) == B3_STATIC && ldi(item(kb, bj, NBC), BTYPE) == B3_STATIC) continue;
         const uint64_t cat_i = (uint64_t)b3x_f2u(COL(si, SCAT)) | ((uint64_t)b3x_f2u(COL(si, SCAT + 1)) << 32);
         const uint64_t msk_i = (uint64_t)b3x_f2u(COL(si, SMASK)) | ((uint64_t)b3x_f2u(COL(si, SMASK + 1)) << 32);
         const uint64_t cat_j = (uint64_t)b3x_f2u(COL(sj, SCAT)) | ((uint64_t)b3x_f2u(COL(sj, SCAT + 1)) << 32);
@@ -550,8 +551,8 @@ B3X_HD void c_compact_move(const Args& a, float* slot, CollideShared& sh, int m,
     const int l = t & 31, q = t >> 5;
     if (m >= sh.nmoves[l]) return;
     const uint32_t mv = sh.u.moves[m][l];
-    const float* __restrict__ src = item(slot + a.SP.cont, (int)(mv & 0xffffu), kCW) + l;
-    float* __restrict__ dst = item(slot + a.SP.cont, (int)(mv >> 16), kCW) + l;
+    const float* __restrict__ src = item(slot + a.SP.cont, (int)(mv & 0xffffu), kCI) + l;
+    float* __restrict__ dst = item(slot + a.SP.cont, (int)(mv >> 16), kCI) + l;
     constexpr int kPart = (kCW + kCtaWarps - 1) / kCtaWarps;
     float v[kPart];
 #pragma unroll
@@ -627,6 +628,8 @@ B3X_HD void c_contacts(const Args& a, float* slot, CollideShared& sh, int t) {
         const int bi = ldi(si, SBODY), bj = ldi(sj, SBODY);
         const float* ba = item(slot + a.SP.body, bi, NBF) + l;
         const float* bb = item(slot + a.SP.body, bj, NBF) + l;
+        const float* kba = item(slot + a.SP.bodyk, bi, NBC) + l;
+        const float* kbb = item(slot + a.SP.bodyk, bj, NBC) + l;
         const B3Vec3 ca = ld3(item(slot + a.SP.pose, bi, NPF) + l, PCEN);
         const B3Vec3 cb = ld3(item(slot + a.SP.pose, bj, NPF) + l, PCEN);
         const int cnt = m.count;
@@ -635,7 +638,7 @@ B3X_HD void c_contacts(const Args& a, float* slot, CollideShared& sh, int t) {
         const B3Vec3 t1 = b3_perp(nrm);
         const B3Vec3 t2 = b3_cross(t1, nrm);
         const float rest_i = COL(si, SREST), rest_j = COL(sj, SREST);
-        const int stat = ldi(ba, BTYPE) != B3_DYNAMIC || ldi(bb, BTYPE) != B3_DYNAMIC;
+        const int stat = ldi(kba, BTYPE) != B3_DYNAMIC || ldi(kbb, BTYPE) != B3_DYNAMIC;
 
         // warm-start carry by (shape_a, shape_b) and feature id
         float ni[B3_MAX_MANIFOLD];
@@ -667,10 +670,10 @@ B3X_HD void c_contacts(const Args& a, float* slot, CollideShared& sh, int t) {
         }
 
         // prepare
-        const float ma = COL(ba, BMI), mb = COL(bb, BMI);
-        const B3Mat3 ia = ldm(ba, BII), ib = ldm(bb, BII);
+        const float ma = COL(kba, BMI), mb = COL(kbb, BMI);
+        const B3Mat3 ia = ldm(kba, BII), ib = ldm(kbb, BII);
         const B3Vec3 va = ld3(ba, BV), wa = ld3(ba, BW), vb = ld3(bb, BV), wb = ld3(bb, BW);
-        float* co = item(slot + a.SP.cont, p, kCW) + l;
+        float* co = item(slot + a.SP.cont, p, kCI) + l;
         const float inv_tau = 1.0f / B3_SPECULATIVE;
         B3Vec3 center_a = b3_v(0.0f, 0.0f, 0.0f), center_b = b3_v(0.0f, 0.0f, 0.0f);
         float wsum = 0.0f;
@@ -884,11 +887,12 @@ B3X_HD void o_body_gather(const Args& a, int tile, OutShared& sh, int k0, int K,
 // bytes, so the write-back stores whole rows.
 B3X_HD void o_body(const Args& a, float* slot, int k, int l, float* y) {
     const float* bc = item(slot + a.SP.body, k, NBF) + l;
+    const float* kb = item(slot + a.SP.bodyk, k, NBC) + l;
     auto get3 = [&](int f) { return b3_v(y[f], y[f + 1], y[f + 2]); };
     auto put3 = [&](int f, B3Vec3 v) { y[f] = v.x; y[f + 1] = v.y; y[f + 2] = v.z; };
     auto put4 = [&](int f, B3Quat q) { y[f] = q.v.x; y[f + 1] = q.v.y; y[f + 2] = q.v.z; y[f + 3] = q.s; };
-    const int type = ldi(bc, BTYPE);
-    const bool dyn_flag = (b3x_f2u(COL(bc, BFLAGS)) & B3_FLAG_DYNAMIC) != 0;
+    const int type = ldi(kb, BTYPE);
+    const bool dyn_flag = (b3x_f2u(COL(kb, BFLAGS)) & B3_FLAG_DYNAMIC) != 0;
     if (type != B3_STATIC || dyn_flag) {
         put3(YLV, ld3(bc, BV));
         put3(YAV, ld3(bc, BW));
@@ -947,8 +951,8 @@ B3X_HD void o_stage(const float* src, OutShared& sh, int K, int words, int RS, i
 // (08_contacts.inl:234-245) computes them.
 B3X_HD void o_contact_fill(const Args& a, float* slot, int l, float* row) {
     const int ba = b3x_f2i(row[WBA]), bb = b3x_f2i(row[WBB]);
-    const float* ca = item(slot + a.SP.body, ba, NBF) + l;
-    const float* cb = item(slot + a.SP.body, bb, NBF) + l;
+    const float* ca = item(slot + a.SP.bodyk, ba, NBC) + l;
+    const float* cb = item(slot + a.SP.bodyk, bb, NBC) + l;
     const B3Mat3 ia = ldm(ca, BII), ib = ldm(cb, BII);
     const B3Mat3 rm = m3_inv(m3_add(ia, ib));
     auto put3 = [&](int f, B3Vec3 v) { row[f] = v.x; row[f + 1] = v.y; row[f + 2] = v.z; };
@@ -1070,7 +1074,9 @@ B3X_HD void out_tile(X& x, const Args& a, int bt, OutShared& sh) {
         const int K = out_items(sh.maxn, NCW);
         for (int k0 = 0; k0 < sh.maxn; k0 += K) {
             const int Kr = sh.maxn - k0 < K ? sh.maxn - k0 : K;
-            x.each([&](int t) { o_stage(item(slot + a.SP.cont, k0, kCW), sh, Kr, kCW, NCW, t); });
+            // whole items: their separation words land on row words the
+            // fill below overwrites
+            x.each([&](int t) { o_stage(item(slot + a.SP.cont, k0, kCI), sh, Kr, kCI, NCW, t); });
             x.each([&](int t) { o_contacts(a, slot, sh, k0, Kr, t); });
             x.each([&](int t) { o_contact_write(a, tile, sh, k0, Kr, t); });
         }

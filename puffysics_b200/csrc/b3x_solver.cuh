@@ -19,6 +19,7 @@
 // sweeps read the workspace in place).
 #pragma once
 #include <cstdint>
+#include <type_traits>
 
 #include "b3x_layout.cuh"
 
@@ -29,26 +30,17 @@ namespace b3x {
 #endif
 constexpr int kStages = B3X_STAGES;   // streamed items in flight + in use
 
-B3X_HDI bool body_dynamic_flag(const float* __restrict__ bc, int k) {
-    return (b3x_f2u(COL(bc, BI(k, BFLAGS))) & B3_FLAG_DYNAMIC) != 0;
+B3X_HDI bool body_dynamic_flag(const float* __restrict__ bk, int k) {
+    return (b3x_f2u(COL(bk, BK(k, BFLAGS))) & B3_FLAG_DYNAMIC) != 0;
 }
 
 // Body velocity write-back gated by the dynamic flag (the reference writes a
 // solved body only when flags has B3_FLAG_DYNAMIC, 08_contacts.inl:405-412).
-B3X_HDI void put_vel(float* __restrict__ bc, int k, B3Vec3 v, B3Vec3 w) {
-    if (body_dynamic_flag(bc, k)) {
+B3X_HDI void put_vel(float* __restrict__ bc, const float* __restrict__ bk, int k, B3Vec3 v, B3Vec3 w) {
+    if (body_dynamic_flag(bk, k)) {
         st3(bc, BI(k, BV), v);
         st3(bc, BI(k, BW), w);
     }
-}
-
-// 08_contacts.inl:184-192
-B3X_HDI void apply_impulse(float* __restrict__ bc, int k, float m, const B3Mat3& i, B3Vec3 r, B3Vec3 p, int sign) {
-    if (!body_dynamic_flag(bc, k)) return;
-    float s = sign > 0 ? 1.0f : -1.0f;
-    B3Vec3 v = ld3(bc, BI(k, BV)), w = ld3(bc, BI(k, BW));
-    st3(bc, BI(k, BV), b3_madd(v, s * m, p));
-    st3(bc, BI(k, BW), b3_add(w, b3_mv(i, b3_mul(b3_cross(r, p), s))));
 }
 
 // ---- warp collectives and the streaming pipeline ---------------------------------
@@ -173,12 +165,12 @@ B3X_HDI bool stream_items(Pipe& P, const float* g, int words, int copy_words, in
 // Warm start one contact (08_contacts.inl:194-232, 293-313), with the two
 // bodies' velocities kept in registers across the contact's impulses (each
 // body's updates in the reference's order).
-B3X_HDI void warm_contact(float* __restrict__ bc, const float* __restrict__ src) {
+B3X_HDI void warm_contact(float* __restrict__ bc, const float* __restrict__ bk, const float* __restrict__ src) {
     int ba = ldi(src, WBA), bb = ldi(src, WBB);
     int cnt = ldi(src, WCNT);
-    float ma = COL(bc, BI(ba, BMI)), mb = COL(bc, BI(bb, BMI));
-    B3Mat3 ia = ldm(bc, BI(ba, BII)), ib = ldm(bc, BI(bb, BII));
-    const bool da = body_dynamic_flag(bc, ba), db = body_dynamic_flag(bc, bb);
+    float ma = COL(bk, BK(ba, BMI)), mb = COL(bk, BK(bb, BMI));
+    B3Mat3 ia = ldm(bk, BK(ba, BII)), ib = ldm(bk, BK(bb, BII));
+    const bool da = body_dynamic_flag(bk, ba), db = body_dynamic_flag(bk, bb);
     B3Vec3 va = ld3(bc, BI(ba, BV)), wa = ld3(bc, BI(ba, BW));
     B3Vec3 vb = ld3(bc, BI(bb, BV)), wb = ld3(bc, BI(bb, BW));
     auto impulse = [](B3Vec3& v, B3Vec3& w, float m, const B3Mat3& i, B3Vec3 r, B3Vec3 p, float s) {
@@ -206,27 +198,45 @@ B3X_HDI void warm_contact(float* __restrict__ bc, const float* __restrict__ src)
     }
 }
 
+// Sweeps over the contacts: the bias sweep of the first substep, the bias
+// sweeps of later substeps (separations from the preceding relax sweep) and
+// the relax sweeps (which store the separations).
+enum : int { kBiasFresh = 0, kBiasCached = 1, kRelax = 2 };
+
 // One contact of a sweep (08_contacts.inl:315-413, rolling 07_packed.inl:24-45).
 // Reads contact k from src (shared-memory copy or workspace), writes the
 // solver-owned fields to dst (workspace).
-B3X_HD void solve_contact(float* __restrict__ bc, const float* __restrict__ src, float* __restrict__ dst,
-        float inv_h, float speed, int use_bias, B3Soft cs, B3Soft ss) {
+template <int kPass>
+B3X_HD void solve_contact(float* __restrict__ bc, const float* __restrict__ bk, const float* __restrict__ src,
+        float* __restrict__ dst, float inv_h, float speed, B3Soft cs, B3Soft ss) {
+    constexpr bool use_bias = kPass != kRelax;
     int ba = ldi(src, WBA), bb = ldi(src, WBB);
     int cnt = ldi(src, WCNT);
     B3Soft soft = ldi(src, WSTAT) ? ss : cs;
-    float ma = COL(bc, BI(ba, BMI)), mb = COL(bc, BI(bb, BMI));
-    B3Mat3 ia = ldm(bc, BI(ba, BII)), ib = ldm(bc, BI(bb, BII));
+    float ma = COL(bk, BK(ba, BMI)), mb = COL(bk, BK(bb, BMI));
+    B3Mat3 ia = ldm(bk, BK(ba, BII)), ib = ldm(bk, BK(bb, BII));
     B3Vec3 va = ld3(bc, BI(ba, BV)), wa = ld3(bc, BI(ba, BW));
     B3Vec3 vb = ld3(bc, BI(bb, BV)), wb = ld3(bc, BI(bb, BW));
-    B3Quat dqa = ldq(bc, BI(ba, BDQ)), dqb = ldq(bc, BI(bb, BDQ));
-    B3Vec3 dp = b3_sub(ld3(bc, BI(bb, BDP)), ld3(bc, BI(ba, BDP)));
+    B3Quat dqa, dqb;
+    B3Vec3 dp;
+    if (kPass != kBiasCached) {
+        dqa = ldq(bc, BI(ba, BDQ));
+        dqb = ldq(bc, BI(bb, BDQ));
+        dp = b3_sub(ld3(bc, BI(bb, BDP)), ld3(bc, BI(ba, BDP)));
+    }
     B3Vec3 n = ld3(src, WN);
     float total_n = 0.0f, twist_lim = 0.0f;
     for (int p = 0; p < B3_MAX_MANIFOLD; p++) {
         if (p >= cnt) break;
         B3Vec3 ra = ld3(src, PW(p, QRA)), rb = ld3(src, PW(p, QRB));
-        B3Vec3 ds = b3_add(dp, b3_sub(b3_rotate(dqb, rb), b3_rotate(dqa, ra)));
-        float sep = b3_dot(ds, n) + COL(src, PW(p, QBSEP));
+        float sep;
+        if (kPass == kBiasCached) {
+            sep = COL(src, WSEP + p);
+        } else {
+            B3Vec3 ds = b3_add(dp, b3_sub(b3_rotate(dqb, rb), b3_rotate(dqa, ra)));
+            sep = b3_dot(ds, n) + COL(src, PW(p, QBSEP));
+            if (kPass == kRelax) COL(dst, WSEP + p) = sep;
+        }
         float vbias = 0.0f, mscale = 1.0f, iscale = 0.0f;
         if (sep > 0.0f) {
             vbias = sep * inv_h;
@@ -318,19 +328,19 @@ B3X_HD void solve_contact(float* __restrict__ bc, const float* __restrict__ src,
             wb = b3_add(wb, b3_mv(ib, delta));
         }
     }
-    put_vel(bc, ba, va, wa);
-    put_vel(bc, bb, vb, wb);
+    put_vel(bc, bk, ba, va, wa);
+    put_vel(bc, bk, bb, vb, wb);
 }
 
 // Restitution of one contact (08_contacts.inl:439-480).
-B3X_HD void restitute_contact(float* __restrict__ bc, const float* __restrict__ src, float* __restrict__ dst,
+B3X_HD void restitute_contact(float* __restrict__ bc, const float* __restrict__ bk, const float* __restrict__ src, float* __restrict__ dst,
         float threshold) {
     float rest = COL(src, WREST);
     if (rest == 0.0f) return;
     int ba = ldi(src, WBA), bb = ldi(src, WBB);
     int cnt = ldi(src, WCNT);
-    float ma = COL(bc, BI(ba, BMI)), mb = COL(bc, BI(bb, BMI));
-    B3Mat3 ia = ldm(bc, BI(ba, BII)), ib = ldm(bc, BI(bb, BII));
+    float ma = COL(bk, BK(ba, BMI)), mb = COL(bk, BK(bb, BMI));
+    B3Mat3 ia = ldm(bk, BK(ba, BII)), ib = ldm(bk, BK(bb, BII));
     B3Vec3 va = ld3(bc, BI(ba, BV)), wa = ld3(bc, BI(ba, BW));
     B3Vec3 vb = ld3(bc, BI(bb, BV)), wb = ld3(bc, BI(bb, BW));
     B3Vec3 nrm = ld3(src, WN);
@@ -352,8 +362,8 @@ B3X_HD void restitute_contact(float* __restrict__ bc, const float* __restrict__ 
         vb = b3_madd(vb, mb, P);
         wb = b3_add(wb, b3_mv(ib, b3_cross(rb, P)));
     }
-    put_vel(bc, ba, va, wa);
-    put_vel(bc, bb, vb, wb);
+    put_vel(bc, bk, ba, va, wa);
+    put_vel(bc, bk, bb, vb, wb);
 }
 
 // ---- joints (06_joints.inl:204-642) -------------------------------------------
@@ -373,11 +383,11 @@ B3X_HDI B3Mat3 point_k(float ma, float mb, const B3Mat3& ia, const B3Mat3& ib, B
 }
 
 // Warm start one joint (06_joints.inl:204-239).
-B3X_HDI void warm_joint(float* __restrict__ bc, const float* __restrict__ src) {
+B3X_HDI void warm_joint(float* __restrict__ bc, const float* __restrict__ bk, const float* __restrict__ src) {
     int type = ldi(src, JTYPE);
     int ja = ldi(src, JBA), jb = ldi(src, JBB);
-    float ma = COL(bc, BI(ja, BMI)), mb = COL(bc, BI(jb, BMI));
-    B3Mat3 ia = ldm(bc, BI(ja, BII)), ib = ldm(bc, BI(jb, BII));
+    float ma = COL(bk, BK(ja, BMI)), mb = COL(bk, BK(jb, BMI));
+    B3Mat3 ia = ldm(bk, BK(ja, BII)), ib = ldm(bk, BK(jb, BII));
     B3Vec3 ra = b3_rotate(ldq(bc, BI(ja, BDQ)), ld3(src, JFPA));
     B3Vec3 rb = b3_rotate(ldq(bc, BI(jb, BDQ)), ld3(src, JFPB));
     B3Vec3 li = ld3(src, JLI);
@@ -389,11 +399,11 @@ B3X_HDI void warm_joint(float* __restrict__ bc, const float* __restrict__ src) {
     } else {
         ang = ld3(src, JAI);
     }
-    if (body_dynamic_flag(bc, ja)) {
+    if (body_dynamic_flag(bk, ja)) {
         st3(bc, BI(ja, BV), b3_msub(ld3(bc, BI(ja, BV)), ma, li));
         st3(bc, BI(ja, BW), b3_sub(ld3(bc, BI(ja, BW)), b3_mv(ia, b3_add(b3_cross(ra, li), ang))));
     }
-    if (body_dynamic_flag(bc, jb)) {
+    if (body_dynamic_flag(bk, jb)) {
         st3(bc, BI(jb, BV), b3_madd(ld3(bc, BI(jb, BV)), mb, li));
         st3(bc, BI(jb, BW), b3_add(ld3(bc, BI(jb, BW)), b3_mv(ib, b3_add(b3_cross(rb, li), ang))));
     }
@@ -442,12 +452,12 @@ B3X_HDI float limit_impulse(float c, float cdot, float inv_h, int use_bias, B3So
 
 // One joint, either type (dispatch 07_packed.inl:66-79; weld 06_joints.inl:285-332;
 // revolute 06_joints.inl:436-642, default uncached path).
-B3X_HD void solve_joint(float* __restrict__ bc, const float* __restrict__ src, float* __restrict__ dst, float h,
+B3X_HD void solve_joint(float* __restrict__ bc, const float* __restrict__ bk, const float* __restrict__ src, float* __restrict__ dst, float h,
         float inv_h, int use_bias) {
     int type = ldi(src, JTYPE);
     int ja = ldi(src, JBA), jb = ldi(src, JBB);
-    float ma = COL(bc, BI(ja, BMI)), mb = COL(bc, BI(jb, BMI));
-    B3Mat3 ia = ldm(bc, BI(ja, BII)), ib = ldm(bc, BI(jb, BII));
+    float ma = COL(bk, BK(ja, BMI)), mb = COL(bk, BK(jb, BMI));
+    B3Mat3 ia = ldm(bk, BK(ja, BII)), ib = ldm(bk, BK(jb, BII));
     B3Vec3 va = ld3(bc, BI(ja, BV)), wa = ld3(bc, BI(ja, BW));
     B3Vec3 vb = ld3(bc, BI(jb, BV)), wb = ld3(bc, BI(jb, BW));
     int fixed = ldi(src, JFIX);
@@ -479,8 +489,8 @@ B3X_HD void solve_joint(float* __restrict__ bc, const float* __restrict__ src, f
         }
         int lin_bias = use_bias || COL(src, JLH) > 0.0f;
         solve_point(bc, src, dst, ja, jb, ma, mb, ia, ib, va, wa, vb, wb, lds(src, JLS), lin_bias);
-        put_vel(bc, ja, va, wa);
-        put_vel(bc, jb, vb, wb);
+        put_vel(bc, bk, ja, va, wa);
+        put_vel(bc, bk, jb, vb, wb);
         return;
     }
     B3Vec3 axis = ld3(src, JAX);
@@ -589,15 +599,17 @@ B3X_HD void solve_joint(float* __restrict__ bc, const float* __restrict__ src, f
         wb = b3_add(wb, b3_mv(ib, ang));
     }
     solve_point(bc, src, dst, ja, jb, ma, mb, ia, ib, va, wa, vb, wb, soft, use_bias);
-    put_vel(bc, ja, va, wa);
-    put_vel(bc, jb, vb, wb);
+    put_vel(bc, bk, ja, va, wa);
+    put_vel(bc, bk, jb, vb, wb);
 }
 
 // ---- one warp of worlds, the solver part of one step ------------------------------
-// slot: the tile's workspace slot; lane: this world's lane; bc: body columns
-// (lane-offset; shared memory or the slot's body region).  Returns false
-// when the pipeline failed.  Follows 09_step.inl:158-181.
-B3X_HD bool solve_world(const Args& a, float* slot, int lane, float* __restrict__ bc, Pipe& P) {
+// slot: the tile's workspace slot; lane: this world's lane; bc / bk: the body
+// state and body constant columns (lane-offset; shared memory or the slot's
+// body / bodyk regions).  Returns false when the pipeline failed.  Follows
+// 09_step.inl:158-181.
+B3X_HD bool solve_world(const Args& a, float* slot, int lane, float* __restrict__ bc,
+        const float* __restrict__ bk, Pipe& P) {
     const float* rec = slot + a.SP.rec + lane;
     const int nb = ldi(rec, RNB);
     const int n = ldi(rec, RN);
@@ -626,27 +638,28 @@ B3X_HD bool solve_world(const Args& a, float* slot, int lane, float* __restrict_
     (void)kStageBytesEach;
     bool any_rest = false;
     // -- warm start contacts, then joints (09_step.inl:160-163)
-    if (!stream_items(P, cc, kCW, kContactStream, wn, [&](int k, const float* src) {
+    if (!stream_items(P, cc, kCI, kContactStream, wn, [&](int k, const float* src) {
             if (k < n) {
-                warm_contact(bc, src);
+                warm_contact(bc, bk, src);
                 any_rest |= COL(src, WREST) != 0.0f;
             }
         }))
         return false;
     any_rest = warp_any(any_rest);
     if (!stream_items(P, jc, NJF, kJointStream, wj, [&](int q, const float* src) {
-            if (q < nj && ldi(src, JOK)) warm_joint(bc, src);
+            if (q < nj && ldi(src, JOK)) warm_joint(bc, bk, src);
         }))
         return false;
 
-    auto contact_pass = [&](int use_bias) {
-        return stream_items(P, cc, kCW, kContactStream, wn, [&](int k, const float* src) {
-            if (k < n) solve_contact(bc, src, item(cc, k, kCW), inv_h, contact_speed, use_bias, cs, ss);
+    auto contact_pass = [&](auto pass) {
+        constexpr int kPass = decltype(pass)::value;
+        return stream_items(P, cc, kCI, kContactStream, wn, [&](int k, const float* src) {
+            if (k < n) solve_contact<kPass>(bc, bk, src, item(cc, k, kCI), inv_h, contact_speed, cs, ss);
         });
     };
     auto joint_pass = [&](int use_bias) {
         return stream_items(P, jc, NJF, kJointStream, wj, [&](int q, const float* src) {
-            if (q < nj && ldi(src, JOK)) solve_joint(bc, src, item(jc, q, NJF), h, inv_h, use_bias);
+            if (q < nj && ldi(src, JOK)) solve_joint(bc, bk, src, item(jc, q, NJF), h, inv_h, use_bias);
         });
     };
     for (int s = 0; s < subs; s++) {
@@ -660,18 +673,21 @@ B3X_HD bool solve_world(const Args& a, float* slot, int lane, float* __restrict_
         }
 #endif
         for (int k = 0; k < nb; k++) {
-            if (ldi(bc, BI(k, BTYPE)) != B3_DYNAMIC) continue;
+            if (ldi(bk, BK(k, BTYPE)) != B3_DYNAMIC) continue;
             const float* kk = item(kcs, k, NKF);
             st3(bc, BI(k, BV), b3_madd(ld3(kk, KDV), COL(kk, KLD), ld3(bc, BI(k, BV))));
             st3(bc, BI(k, BW), b3_madd(ld3(kk, KDW), COL(kk, KAD), ld3(bc, BI(k, BW))));
         }
-        if (!contact_pass(1)) return false;
+        const bool first = s == 0;
+        if (first ? !contact_pass(std::integral_constant<int, kBiasFresh>{})
+                  : !contact_pass(std::integral_constant<int, kBiasCached>{}))
+            return false;
         for (int it = 0; it < a.joint_iters; it++)
             if (!joint_pass(1)) return false;
         // integrate positions (09_step.inl:55-107)
         for (int k = 0; k < nb; k++) {
-            if (ldi(bc, BI(k, BTYPE)) == B3_STATIC) continue;
-            uint32_t flags = b3x_f2u(COL(bc, BI(k, BFLAGS)));
+            if (ldi(bk, BK(k, BTYPE)) == B3_STATIC) continue;
+            uint32_t flags = b3x_f2u(COL(bk, BK(k, BFLAGS)));
             B3Vec3 v = ld3(bc, BI(k, BV)), av = ld3(bc, BI(k, BW));
             if (flags & B3_LOCK_LIN_X) v.x = 0.0f;
             if (flags & B3_LOCK_LIN_Y) v.y = 0.0f;
@@ -688,14 +704,14 @@ B3X_HD bool solve_world(const Args& a, float* slot, int lane, float* __restrict_
             st3(bc, BI(k, BDP), b3_madd(ld3(bc, BI(k, BDP)), h, v));
             stq(bc, BI(k, BDQ), q_integrate(ldq(bc, BI(k, BDQ)), b3_mul(av, h)));
         }
-        if (!contact_pass(0)) return false;
+        if (!contact_pass(std::integral_constant<int, kRelax>{})) return false;
         for (int it = 0; it < a.relax_iters; it++)
             if (!joint_pass(0)) return false;
         // restitution (08_contacts.inl:439-480): skipped when no contact of
         // the warp's worlds has a nonzero coefficient
         if (any_rest) {
-            if (!stream_items(P, cc, kCW, kContactStream, wn, [&](int k, const float* src) {
-                    if (k < n) restitute_contact(bc, src, item(cc, k, kCW), restitution_threshold);
+            if (!stream_items(P, cc, kCI, kContactStream, wn, [&](int k, const float* src) {
+                    if (k < n) restitute_contact(bc, bk, src, item(cc, k, kCI), restitution_threshold);
                 }))
                 return false;
         }

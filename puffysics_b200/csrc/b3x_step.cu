@@ -62,15 +62,17 @@ struct DevExec {
 
 // Shared memory of a step block: the collide and write-back phases use it
 // as their block state; the solve phase as the streaming stages, their
-// mbarriers, then the body columns when they live on chip.
+// mbarriers, then the body columns that live on chip: the body state and the
+// body constants (kBodyAll), the body state alone (kBodyState; the constants
+// are then read from the workspace through L1), or neither (kBodyNone).
 constexpr size_t kStageBytes = (size_t)kStages * kStreamWords * kLanes * sizeof(float);
 constexpr size_t kBarBytes = 64;
-constexpr int kSolvedBodyFields = BDQ + 4;   // velocities and pose deltas go back
+enum BodyPlace : int { kBodyNone = 0, kBodyState = 1, kBodyAll = 2 };
 
 // Warp 0's part of the step: warm start and substeps of the tile's 32 worlds.
 // Returns false when a pipeline wait gave up (nothing of the tile is then
 // written back: the step is abandoned for these worlds).
-template <bool kBodySmem>
+template <int kBody>
 __device__ bool solve_tile(const Args& a, unsigned char* smem_raw) {
     const int lane = threadIdx.x & 31;
     float* slot = slot_of(a, blockIdx.x);
@@ -79,17 +81,20 @@ __device__ bool solve_tile(const Args& a, unsigned char* smem_raw) {
     P.bar = reinterpret_cast<uint64_t*>(smem_raw + kStageBytes);
     pipe_init(P);
     float* gb = slot + a.SP.body;
+    const float* gk = slot + a.SP.bodyk;
     float* sb = reinterpret_cast<float*>(smem_raw + kStageBytes + kBarBytes);
+    float* sk = sb + (size_t)a.L.B * NBF * kLanes;
     const int nb = warp_max(ldi(slot + a.SP.rec + lane, RNB));
-    if (kBodySmem) {
-        // each lane copies its own column
+    // each lane copies its own columns
+    if (kBody != kBodyNone)
         for (int idx = lane; idx < nb * NBF * kLanes; idx += kLanes) sb[idx] = gb[idx];
-    }
-    float* bc = (kBodySmem ? sb : gb) + lane;
-    const bool ok = solve_world(a, slot, lane, bc, P);
-    if (ok && kBodySmem) {
-        for (int k = 0; k < nb; k++)
-            for (int f = 0; f < kSolvedBodyFields; f++) COL(gb + lane, BI(k, f)) = COL(sb + lane, BI(k, f));
+    if (kBody == kBodyAll)
+        for (int idx = lane; idx < nb * NBC * kLanes; idx += kLanes) sk[idx] = gk[idx];
+    float* bc = (kBody != kBodyNone ? sb : gb) + lane;
+    const float* bk = (kBody == kBodyAll ? sk : gk) + lane;
+    const bool ok = solve_world(a, slot, lane, bc, bk, P);
+    if (ok && kBody != kBodyNone) {
+        for (int idx = lane; idx < nb * NBF * kLanes; idx += kLanes) gb[idx] = sb[idx];
     }
     __syncwarp();
     if (lane == 0) {
@@ -103,7 +108,7 @@ __device__ bool solve_tile(const Args& a, unsigned char* smem_raw) {
 
 // One block per tile: collide (all warps), solve (warp 0), write-back (all
 // warps).
-template <bool kBodySmem>
+template <int kBody>
 __global__ void __launch_bounds__(kCta, 4) step_kernel(Args a) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     __shared__ int solved;
@@ -115,7 +120,7 @@ __global__ void __launch_bounds__(kCta, 4) step_kernel(Args a) {
     asm volatile("fence.proxy.async;" ::: "memory");
     __syncthreads();
     if (threadIdx.x < kLanes) {
-        const bool ok = solve_tile<kBodySmem>(a, smem_raw);
+        const bool ok = solve_tile<kBody>(a, smem_raw);
         if (threadIdx.x == 0) solved = ok;
     }
     __syncthreads();
@@ -185,7 +190,7 @@ __global__ void observe_kernel(const unsigned char* data, unsigned long long str
 
 // ---- host side --------------------------------------------------------------
 struct Plan {
-    bool body_smem;
+    int body;                // BodyPlace of the solve
     Space SP;
     size_t smem_bytes;       // dynamic shared memory of a step block
     size_t tile_bytes;       // one tile's workspace slot
@@ -197,9 +202,8 @@ static std::mutex g_mutex;
 static std::map<std::pair<int, unsigned long long>, Plan> g_plans;
 static std::map<std::tuple<int, void*, unsigned long long>, std::pair<void*, size_t>> g_workspaces;
 
-// Body columns live in shared memory while they fit comfortably.
-static constexpr size_t kBodySmemLimit = 64 * 1024;
-// Resident blocks per SM the default chunk is sized for.
+// Resident blocks per SM the default chunk and the shared memory budget are
+// sized for.
 static constexpr int kChunkBlocksPerSM = 4;
 
 static cudaError_t make_plan(int dev, unsigned long long sig, const Layout& L, Plan* out) {
@@ -211,15 +215,13 @@ static cudaError_t make_plan(int dev, unsigned long long sig, const Layout& L, P
     }
     Plan p;
     p.SP = space_from_layout(L);
-    size_t body_bytes = (size_t)L.B * NBF * kLanes * sizeof(float);
-    p.body_smem = body_bytes <= kBodySmemLimit;
-    size_t solve_smem = kStageBytes + kBarBytes + (p.body_smem ? body_bytes : 0);
-    p.smem_bytes = solve_smem;
-    if (p.smem_bytes < sizeof(CollideShared)) p.smem_bytes = sizeof(CollideShared);
-    if (p.smem_bytes < sizeof(OutShared)) p.smem_bytes = sizeof(OutShared);
     p.tile_bytes = (size_t)p.SP.tile_words * sizeof(float);
-    int sms = 0;
+    int sms = 0, per_sm = 0, reserved = 0;
     cudaError_t e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
+    e = cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+    if (e != cudaSuccess) return e;
+    e = cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev);
     if (e != cudaSuccess) return e;
     // The dynamic shared memory cap is a property of the kernel function, not
     // of a plan: raise it once to the device's opt-in maximum so plans of
@@ -229,14 +231,25 @@ static cudaError_t make_plan(int dev, unsigned long long sig, const Layout& L, P
     if (e != cudaSuccess) return e;
     // (the cap excludes the kernel's static shared memory)
     cudaFuncAttributes fa;
-    e = cudaFuncGetAttributes(&fa, step_kernel<true>);
+    e = cudaFuncGetAttributes(&fa, step_kernel<kBodyAll>);
     if (e != cudaSuccess) return e;
     const int cap = optin - (int)fa.sharedSizeBytes;
+    // Body columns go on chip as far as kChunkBlocksPerSM blocks still fit
+    // on an SM: all of them, else the state the solver writes, else none.
+    const size_t budget = (size_t)(per_sm / kChunkBlocksPerSM - reserved) - fa.sharedSizeBytes;
+    const size_t state_bytes = (size_t)L.B * NBF * kLanes * sizeof(float);
+    const size_t const_bytes = (size_t)L.B * NBC * kLanes * sizeof(float);
+    const size_t base = kStageBytes + kBarBytes;
+    p.body = base + state_bytes + const_bytes <= budget ? kBodyAll
+           : base + state_bytes <= budget ? kBodyState : kBodyNone;
+    p.smem_bytes = base + (p.body != kBodyNone ? state_bytes : 0) + (p.body == kBodyAll ? const_bytes : 0);
+    if (p.smem_bytes < sizeof(CollideShared)) p.smem_bytes = sizeof(CollideShared);
+    if (p.smem_bytes < sizeof(OutShared)) p.smem_bytes = sizeof(OutShared);
     if (p.smem_bytes > (size_t)cap) return cudaErrorInvalidValue;
-    e = cudaFuncSetAttribute(step_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, cap);
-    if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(step_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, cap);
-    if (e != cudaSuccess) return e;
+    for (auto fn : {step_kernel<kBodyNone>, step_kernel<kBodyState>, step_kernel<kBodyAll>}) {
+        e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, cap);
+        if (e != cudaSuccess) return e;
+    }
     p.chunk_tiles = sms * kChunkBlocksPerSM;
     p.ws_bytes = (size_t)p.chunk_tiles * p.tile_bytes;
     g_plans[{dev, sig}] = p;
@@ -275,8 +288,9 @@ static cudaError_t launch_step(const B3Batch& batch, float dt, int substeps, con
     for (int t0 = 0; t0 < ntiles; t0 += chunk) {
         const int nt = ntiles - t0 < chunk ? ntiles - t0 : chunk;
         a.tile0 = t0;
-        if (p.body_smem) step_kernel<true><<<nt, kCta, p.smem_bytes, stream>>>(a);
-        else step_kernel<false><<<nt, kCta, p.smem_bytes, stream>>>(a);
+        if (p.body == kBodyAll) step_kernel<kBodyAll><<<nt, kCta, p.smem_bytes, stream>>>(a);
+        else if (p.body == kBodyState) step_kernel<kBodyState><<<nt, kCta, p.smem_bytes, stream>>>(a);
+        else step_kernel<kBodyNone><<<nt, kCta, p.smem_bytes, stream>>>(a);
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     }
