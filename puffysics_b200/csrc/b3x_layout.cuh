@@ -80,9 +80,11 @@ enum : int {
     RLIVE = 0, RNB = 1, RNS = 2, ROLDN = 3, RNJ = 4, RN = 5, ROVF = 6, RDROP = 7, RSPEED = 8, RRT = 9,
     RMAXLIN = 10, RCS = 11, RSS = 14, NRF = 17
 };
-// body solver state (region body): velocities and pose deltas, the fields
-// the solver writes
-enum : int { BV = 0, BW = 3, BDP = 6, BDQ = 9, NBF = 13 };
+// body velocities (region body): the fields every contact and joint row
+// updates
+enum : int { BV = 0, BW = 3, NBF = 6 };
+// body pose deltas (region bodyp), advanced once per substep
+enum : int { BDP = 0, BDQ = 3, NBP = 7 };
 // body constants of the step (region bodyk): inverse mass and world inverse
 // inertia gated by type, flags, type
 enum : int { BMI = 0, BII = 1, BFLAGS = 10, BTYPE = 11, NBC = 12 };
@@ -113,6 +115,10 @@ constexpr int kStreamWords = kContactStream > kJointStream ? kContactStream : kJ
 // Candidate pairs are tested in windows of kPairWindow consecutive pair
 // indices (lexicographic (i, j) order, the reference's loop order).
 constexpr int kPairWindow = 64;
+// A manifold of the narrowphase, parked between the narrowphase and the
+// contact build of a window (region mani, one item per window candidate):
+// point count, normal, then per point p_a, p_b, separation, feature id.
+enum : int { MCNT = 0, MN = 1, MPA = 4, MPB = 16, MSEP = 28, MFEAT = 32, NMW = 36 };
 
 // World header (the first 68 bytes of B3World).
 struct Header {
@@ -146,12 +152,11 @@ static inline bool layout_from_signature(unsigned long long sig, Layout* L) {
 
 // Word offsets of the regions of one tile's workspace slot.
 // Besides the solver columns, the prepared B3Joint rows (jimg) travel from the
-// collide phase to the write-back, which then writes whole rows.  The contact
-// region holds kPairWindow items beyond the capacity: a pair window first
-// writes each new contact at a provisional slot (the contacts before the
-// window plus its candidate index), then compacts.
+// collide phase to the write-back, which then writes whole rows.  The
+// manifolds of a pair window wait in region mani until their contact slots
+// are known.
 struct Space {
-    unsigned long long rec, body, bodyk, konst, pose, shape, old, cont, joint, jimg, tile_words;
+    unsigned long long rec, body, bodyp, bodyk, konst, pose, shape, old, cont, mani, joint, jimg, tile_words;
 };
 
 static inline Space space_from_layout(const Layout& L) {
@@ -164,12 +169,14 @@ static inline Space space_from_layout(const Layout& L) {
     };
     s.rec = take(1, NRF);
     s.body = take(L.B, NBF);
+    s.bodyp = take(L.B, NBP);
     s.bodyk = take(L.B, NBC);
     s.konst = take(L.B, NKF);
     s.pose = take(L.B, NPF);
     s.shape = take(L.S, NSF);
     s.old = take(L.C, NOF);
-    s.cont = take((unsigned long long)L.C + kPairWindow, kCI);
+    s.cont = take(L.C, kCI);
+    s.mani = take(kPairWindow, NMW);
     s.joint = take(L.J, NJF);
     s.jimg = take(L.J, NVW);
     s.tile_words = (w + 63) & ~63ull;   // 256-byte aligned slots
@@ -229,6 +236,8 @@ B3X_HDI const float* item(const float* base, int k, int nf) { return base + (siz
 B3X_HDI int PW(int p, int f) { return WP + p * NQW + f; }
 // body column field of body k (body columns are [body][field][lane])
 B3X_HDI int BI(int k, int f) { return k * NBF + f; }
+// pose-delta field f of body k (bodyp columns are [body][field][lane])
+B3X_HDI int BP(int k, int f) { return k * NBP + f; }
 // constant field f of body k (bodyk columns are [body][field][lane])
 B3X_HDI int BK(int k, int f) { return k * NBC + f; }
 

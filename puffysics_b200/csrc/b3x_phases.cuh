@@ -43,7 +43,11 @@ struct CollideShared {
     uint32_t cmask[kLanes][kPairWindow / 32];    // broadphase survivors of world l
     uint32_t nmask[kLanes][kPairWindow / 32];    // candidates of world l with a manifold
     int ccount[kLanes];
-    uint32_t wmask[kPairWindow];                 // worlds with more than ci candidates
+    int icount[kLanes];                          // item counts (sequential executor)
+    int nbase[kLanes];                           // contacts of world l before the window
+    // (item index, world) enumeration of the window's candidates, then of its
+    // new contacts: wmask[r] = worlds with more than r items, off = prefix
+    uint32_t wmask[kPairWindow];
     int off[kPairWindow + 1];
     int maxc, total;
     union {
@@ -51,9 +55,7 @@ struct CollideShared {
         float flat[kStageFloats];                // gathered struct rows of a group of worlds
         float jstage[kLanes][NVW];               // one joint of every world (115: odd)
         float clip[48 * kCta];                   // narrowphase clip polygons
-        uint32_t moves[kPairWindow][kLanes];     // compaction: p | k << 16 of move m of world l
     } u;
-    int nmoves[kLanes], maxmoves;
 };
 
 struct OutShared {
@@ -193,13 +195,14 @@ B3X_HD void c_body(const Args& a, float* slot, const CollideShared& sh, int k, i
     const float h = a.dt / (float)a.substeps;
     float* bc = item(slot + a.SP.body, k, NBF) + l;
     float* kb = item(slot + a.SP.bodyk, k, NBC) + l;
+    float* pb = item(slot + a.SP.bodyp, k, NBP) + l;
     float* pc = item(slot + a.SP.pose, k, NPF) + l;
     const int type = b3x_f2i(y[YTYPE]);
     auto v3 = [&](int f) { return b3_v(y[f], y[f + 1], y[f + 2]); };
     st3(bc, BV, v3(YLV));
     st3(bc, BW, v3(YAV));
-    st3(bc, BDP, v3(YDP));
-    stq(bc, BDQ, b3_q(y[YDQ], y[YDQ + 1], y[YDQ + 2], y[YDQ + 3]));
+    st3(pb, BDP, v3(YDP));
+    stq(pb, BDQ, b3_q(y[YDQ], y[YDQ + 1], y[YDQ + 2], y[YDQ + 3]));
     COL(kb, BFLAGS) = y[YFLAGS];
     COL(kb, BTYPE) = y[YTYPE];
     if (type == B3_DYNAMIC) {
@@ -442,17 +445,12 @@ B3X_HDI int pair_of(int p, int ns) {
 B3X_HD void c_window_setup(CollideShared& sh, int p0, int npairs, int t) {
     if (t < kPairWindow) {
         sh.ptab[t] = p0 + t < npairs ? pair_of(p0 + t, sh.maxns) : -1;
-        sh.wmask[t] = 0;
     }
     if (t < kLanes) {
         for (int c = 0; c < kPairWindow / 32; c++) {
             sh.cmask[t][c] = 0;
             sh.nmask[t][c] = 0;
         }
-    }
-    if (t == 0) {
-        sh.maxc = 0;
-        sh.maxmoves = 0;
     }
 }
 
@@ -494,19 +492,51 @@ B3X_HD void c_broadphase(const Args& a, float* slot, CollideShared& sh, int npw,
     }
 }
 
-// Candidates of world l, and its bit in wmask[ci] for every ci it has.
+// Per-world item counts -> the (item, world) enumeration (wmask, off, maxc,
+// total).  Run by the 32 threads of warp 0, lane = world.
+B3X_HD void enumerate(CollideShared& sh, int c, int l) {
+#if defined(__CUDA_ARCH__)
+    const int maxc = __reduce_max_sync(0xffffffffu, c);
+    int off = 0;
+    for (int ci = 0; ci < maxc; ci++) {
+        const uint32_t b = __ballot_sync(0xffffffffu, c > ci);
+        if (l == 0) {
+            sh.wmask[ci] = b;
+            sh.off[ci] = off;
+        }
+        off += __popc(b);
+    }
+    if (l == 0) {
+        sh.off[maxc] = off;
+        sh.maxc = maxc;
+        sh.total = off;
+    }
+#else
+    // sequential executor: the last world's call sees every count
+    sh.icount[l] = c;
+    if (l != kLanes - 1) return;
+    int maxc = 0, off = 0;
+    for (int w = 0; w < kLanes; w++) maxc = sh.icount[w] > maxc ? sh.icount[w] : maxc;
+    for (int ci = 0; ci < maxc; ci++) {
+        uint32_t b = 0;
+        for (int w = 0; w < kLanes; w++)
+            if (sh.icount[w] > ci) b |= 1u << w;
+        sh.wmask[ci] = b;
+        sh.off[ci] = off;
+        off += popc32(b);
+    }
+    sh.off[maxc] = off;
+    sh.maxc = maxc;
+    sh.total = off;
+#endif
+}
+
+// Candidates of world l (warp 0, lane = world).
 B3X_HD void c_count(CollideShared& sh, int l) {
     int c = 0;
     for (int w = 0; w < kPairWindow / 32; w++) c += popc32(sh.cmask[l][w]);
     sh.ccount[l] = c;
-    shared_max(&sh.maxc, c);
-    for (int ci = 0; ci < c; ci++) shared_or(&sh.wmask[ci], 1u << l);
-}
-
-B3X_HD void c_prefix(CollideShared& sh) {
-    sh.off[0] = 0;
-    for (int ci = 0; ci < sh.maxc; ci++) sh.off[ci + 1] = sh.off[ci] + popc32(sh.wmask[ci]);
-    sh.total = sh.off[sh.maxc];
+    enumerate(sh, c, l);
 }
 
 // Enumeration index -> (candidate index ci, world l).
@@ -521,46 +551,24 @@ B3X_HDI void decode(const CollideShared& sh, int idx, int& ci, int& l) {
     l = nth_bit32(sh.wmask[ci], idx - sh.off[ci]);
 }
 
-// Contact slots of world l's candidates in this window (08_contacts.inl:120-134):
+// Contact slots of world l's manifolds in this window (08_contacts.inl:120-134):
 // in candidate order, slots are handed out while the capacity lasts, then
-// overflow is counted.  The contacts were written at their provisional slots
-// (contacts before the window + candidate index); those that land lower are
-// listed as moves p -> k, in increasing order.
-B3X_HD void c_compact_plan(const Args& a, CollideShared& sh, int l) {
+// overflow is counted -- so the r-th manifold of the window takes slot
+// nbase + r.  Then the (contact, world) enumeration of the contact build.
+// Warp 0, lane = world.
+B3X_HD void c_plan(const Args& a, CollideShared& sh, int l) {
+    int m = 0;
+    for (int w = 0; w < kPairWindow / 32; w++) m += popc32(sh.nmask[l][w]);
     const int base = sh.n[l];
-    int n = base, m = 0;
-    for (int ci = 0; ci < sh.ccount[l]; ci++) {
-        if (!((sh.nmask[l][ci >> 5] >> (ci & 31)) & 1u)) continue;
-        if (n >= a.L.C) {
-            sh.ovf[l] = 1;
-            sh.drop[l]++;
-            continue;
-        }
-        const int k = n++, p = base + ci;
-        if (k != p) sh.u.moves[m++][l] = (uint32_t)p | ((uint32_t)k << 16);
+    const int room = a.L.C - base > 0 ? a.L.C - base : 0;
+    const int kept = m < room ? m : room;
+    if (m > kept) {
+        sh.ovf[l] = 1;
+        sh.drop[l] += m - kept;
     }
-    sh.n[l] = n;
-    sh.nmoves[l] = m;
-    shared_max(&sh.maxmoves, m);
-}
-
-// Move m of every world (thread: world t % 32, a quarter of the words).  A
-// move's destination is below its own source and above every earlier
-// source but may be an earlier move's source, so rounds go in increasing m.
-B3X_HD void c_compact_move(const Args& a, float* slot, CollideShared& sh, int m, int t) {
-    const int l = t & 31, q = t >> 5;
-    if (m >= sh.nmoves[l]) return;
-    const uint32_t mv = sh.u.moves[m][l];
-    const float* __restrict__ src = item(slot + a.SP.cont, (int)(mv & 0xffffu), kCI) + l;
-    float* __restrict__ dst = item(slot + a.SP.cont, (int)(mv >> 16), kCI) + l;
-    constexpr int kPart = (kCW + kCtaWarps - 1) / kCtaWarps;
-    float v[kPart];
-#pragma unroll
-    for (int f = 0; f < kPart; f++)
-        if (q * kPart + f < kCW) v[f] = COL(src, q * kPart + f);
-#pragma unroll
-    for (int f = 0; f < kPart; f++)
-        if (q * kPart + f < kCW) COL(dst, q * kPart + f) = v[f];
+    sh.nbase[l] = base;
+    sh.n[l] = base + kept;
+    enumerate(sh, kept, l);
 }
 
 // Warm-cache entries to match for the key (i, j) (08_contacts.inl:136-153):
@@ -598,12 +606,9 @@ B3X_HDI void warm_range(const float* oc, int on, int sorted, int i, int j, int g
 }
 
 // Every candidate of the window (spread over (candidate, world)): the
-// narrowphase (05_collision.inl), and for a manifold the contact built from
-// it -- b3_contact_from_mani (08_contacts.inl:5-39), the warm-start carry
-// (08_contacts.inl:136-171) and b3_prepare_one_contact
-// (08_contacts.inl:234-291) -- written at the provisional slot
-// n + ci (words [0, kCW); point slots past the point count are not written).
-B3X_HD void c_contacts(const Args& a, float* slot, CollideShared& sh, int t) {
+// narrowphase (05_collision.inl); a manifold is parked in region mani at the
+// candidate's index and marked in nmask.
+B3X_HD void c_narrow(const Args& a, float* slot, CollideShared& sh, int t) {
     const float* sc = slot + a.SP.shape;
     Poly P;
     P.base = sh.u.clip + t;
@@ -624,6 +629,48 @@ B3X_HD void c_contacts(const Args& a, float* slot, CollideShared& sh, int t) {
         collide(m, ga, gb, P);
         if (m.count == 0) continue;
         shared_or(&sh.nmask[l][ci >> 5], 1u << (ci & 31));
+        float* mo = item(slot + a.SP.mani, ci, NMW) + l;
+        sti(mo, MCNT, m.count);
+        st3(mo, MN, m.normal);
+#pragma unroll
+        for (int q = 0; q < B3_MAX_MANIFOLD; q++) {
+            if (q >= m.count) continue;
+            st3(mo, MPA + 3 * q, m.pa[q]);
+            st3(mo, MPB + 3 * q, m.pb[q]);
+            COL(mo, MSEP + q) = m.sep[q];
+            sti(mo, MFEAT + q, (int)m.feat[q]);
+        }
+    }
+}
+
+// Every new contact of the window that fits the capacity (spread over
+// (contact, world)): the r-th manifold of world l becomes contact slot
+// nbase + r -- b3_contact_from_mani (08_contacts.inl:5-39), the warm-start
+// carry (08_contacts.inl:136-171) and b3_prepare_one_contact
+// (08_contacts.inl:234-291); words [0, kCW), point slots past the point
+// count are not written.
+B3X_HD void c_build(const Args& a, float* slot, CollideShared& sh, int t) {
+    const float* sc = slot + a.SP.shape;
+    for (int idx = t; idx < sh.total; idx += kCta) {
+        int r, l;
+        decode(sh, idx, r, l);
+        const int ci = nth_bit64(sh.nmask[l], r);
+        const int pr = sh.ptab[nth_bit64(sh.cmask[l], ci)];
+        const int i = pr & 0xffff, j = pr >> 16;
+        const float* si = item(sc, i, NSF) + l;
+        const float* sj = item(sc, j, NSF) + l;
+        const float* mo = item(slot + a.SP.mani, ci, NMW) + l;
+        Mani m;
+        m.count = clampi(ldi(mo, MCNT), 0, B3_MAX_MANIFOLD);
+        m.normal = ld3(mo, MN);
+#pragma unroll
+        for (int q = 0; q < B3_MAX_MANIFOLD; q++) {
+            if (q >= m.count) continue;
+            m.pa[q] = ld3(mo, MPA + 3 * q);
+            m.pb[q] = ld3(mo, MPB + 3 * q);
+            m.sep[q] = COL(mo, MSEP + q);
+            m.feat[q] = (uint32_t)ldi(mo, MFEAT + q);
+        }
 
         const int bi = ldi(si, SBODY), bj = ldi(sj, SBODY);
         const float* ba = item(slot + a.SP.body, bi, NBF) + l;
@@ -633,7 +680,7 @@ B3X_HD void c_contacts(const Args& a, float* slot, CollideShared& sh, int t) {
         const B3Vec3 ca = ld3(item(slot + a.SP.pose, bi, NPF) + l, PCEN);
         const B3Vec3 cb = ld3(item(slot + a.SP.pose, bj, NPF) + l, PCEN);
         const int cnt = m.count;
-        const int p = sh.n[l] + ci;
+        const int p = sh.nbase[l] + r;
         const B3Vec3 nrm = m.normal;
         const B3Vec3 t1 = b3_perp(nrm);
         const B3Vec3 t2 = b3_cross(t1, nrm);
@@ -827,11 +874,11 @@ B3X_HD void collide_tile(X& x, const Args& a, int bt, CollideShared& sh) {
         const int npw = npairs - p0 < kPairWindow ? npairs - p0 : kPairWindow;
         x.each([&](int t) { c_broadphase(a, slot, sh, npw, t); });
         x.each([&](int t) { if (t < kLanes) c_count(sh, t); });
-        x.each([&](int t) { if (t == 0) c_prefix(sh); });
         if (sh.total == 0) continue;
-        x.each([&](int t) { c_contacts(a, slot, sh, t); });
-        x.each([&](int t) { if (t < kLanes) c_compact_plan(a, sh, t); });
-        for (int m = 0; m < sh.maxmoves; m++) x.each([&](int t) { c_compact_move(a, slot, sh, m, t); });
+        x.each([&](int t) { c_narrow(a, slot, sh, t); });
+        x.each([&](int t) { if (t < kLanes) c_plan(a, sh, t); });
+        if (sh.total == 0) continue;
+        x.each([&](int t) { c_build(a, slot, sh, t); });
     }
     x.each([&](int t) { if (t < kLanes) c_finish(a, slot, sh, t); });
 }
@@ -888,6 +935,7 @@ B3X_HD void o_body_gather(const Args& a, int tile, OutShared& sh, int k0, int K,
 B3X_HD void o_body(const Args& a, float* slot, int k, int l, float* y) {
     const float* bc = item(slot + a.SP.body, k, NBF) + l;
     const float* kb = item(slot + a.SP.bodyk, k, NBC) + l;
+    const float* pb = item(slot + a.SP.bodyp, k, NBP) + l;
     auto get3 = [&](int f) { return b3_v(y[f], y[f + 1], y[f + 2]); };
     auto put3 = [&](int f, B3Vec3 v) { y[f] = v.x; y[f + 1] = v.y; y[f + 2] = v.z; };
     auto put4 = [&](int f, B3Quat q) { y[f] = q.v.x; y[f + 1] = q.v.y; y[f + 2] = q.v.z; y[f + 3] = q.s; };
@@ -898,8 +946,8 @@ B3X_HD void o_body(const Args& a, float* slot, int k, int l, float* y) {
         put3(YAV, ld3(bc, BW));
     }
     if (type != B3_STATIC) {
-        const B3Vec3 center = b3_add(get3(YCEN), ld3(bc, BDP));
-        const B3Quat rot = b3_qnorm(b3_qmul(ldq(bc, BDQ), b3_q(y[YROT], y[YROT + 1], y[YROT + 2], y[YROT + 3])));
+        const B3Vec3 center = b3_add(get3(YCEN), ld3(pb, BDP));
+        const B3Quat rot = b3_qnorm(b3_qmul(ldq(pb, BDQ), b3_q(y[YROT], y[YROT + 1], y[YROT + 2], y[YROT + 3])));
         put3(YCEN, center);
         put4(YROT, rot);
         put3(YPOS, b3_sub(center, b3_rotate(rot, get3(YLC))));

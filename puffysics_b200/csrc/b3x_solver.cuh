@@ -207,8 +207,8 @@ enum : int { kBiasFresh = 0, kBiasCached = 1, kRelax = 2 };
 // Reads contact k from src (shared-memory copy or workspace), writes the
 // solver-owned fields to dst (workspace).
 template <int kPass>
-B3X_HD void solve_contact(float* __restrict__ bc, const float* __restrict__ bk, const float* __restrict__ src,
-        float* __restrict__ dst, float inv_h, float speed, B3Soft cs, B3Soft ss) {
+B3X_HD void solve_contact(float* __restrict__ bc, const float* __restrict__ bp, const float* __restrict__ bk,
+        const float* __restrict__ src, float* __restrict__ dst, float inv_h, float speed, B3Soft cs, B3Soft ss) {
     constexpr bool use_bias = kPass != kRelax;
     int ba = ldi(src, WBA), bb = ldi(src, WBB);
     int cnt = ldi(src, WCNT);
@@ -220,9 +220,9 @@ B3X_HD void solve_contact(float* __restrict__ bc, const float* __restrict__ bk, 
     B3Quat dqa, dqb;
     B3Vec3 dp;
     if (kPass != kBiasCached) {
-        dqa = ldq(bc, BI(ba, BDQ));
-        dqb = ldq(bc, BI(bb, BDQ));
-        dp = b3_sub(ld3(bc, BI(bb, BDP)), ld3(bc, BI(ba, BDP)));
+        dqa = ldq(bp, BP(ba, BDQ));
+        dqb = ldq(bp, BP(bb, BDQ));
+        dp = b3_sub(ld3(bp, BP(bb, BDP)), ld3(bp, BP(ba, BDP)));
     }
     B3Vec3 n = ld3(src, WN);
     float total_n = 0.0f, twist_lim = 0.0f;
@@ -383,13 +383,14 @@ B3X_HDI B3Mat3 point_k(float ma, float mb, const B3Mat3& ia, const B3Mat3& ib, B
 }
 
 // Warm start one joint (06_joints.inl:204-239).
-B3X_HDI void warm_joint(float* __restrict__ bc, const float* __restrict__ bk, const float* __restrict__ src) {
+B3X_HDI void warm_joint(float* __restrict__ bc, const float* __restrict__ bp, const float* __restrict__ bk,
+        const float* __restrict__ src) {
     int type = ldi(src, JTYPE);
     int ja = ldi(src, JBA), jb = ldi(src, JBB);
     float ma = COL(bk, BK(ja, BMI)), mb = COL(bk, BK(jb, BMI));
     B3Mat3 ia = ldm(bk, BK(ja, BII)), ib = ldm(bk, BK(jb, BII));
-    B3Vec3 ra = b3_rotate(ldq(bc, BI(ja, BDQ)), ld3(src, JFPA));
-    B3Vec3 rb = b3_rotate(ldq(bc, BI(jb, BDQ)), ld3(src, JFPB));
+    B3Vec3 ra = b3_rotate(ldq(bp, BP(ja, BDQ)), ld3(src, JFPA));
+    B3Vec3 rb = b3_rotate(ldq(bp, BP(jb, BDQ)), ld3(src, JFPB));
     B3Vec3 li = ld3(src, JLI);
     B3Vec3 ang;
     if (type == B3_JOINT_REVOLUTE) {
@@ -410,16 +411,16 @@ B3X_HDI void warm_joint(float* __restrict__ bc, const float* __restrict__ bk, co
 }
 
 // 06_joints.inl:257-282
-B3X_HDI void solve_point(const float* __restrict__ bc, const float* __restrict__ src, float* __restrict__ dst,
+B3X_HDI void solve_point(const float* __restrict__ bp, const float* __restrict__ src, float* __restrict__ dst,
         int ja, int jb, float ma, float mb, const B3Mat3& ia, const B3Mat3& ib, B3Vec3& va, B3Vec3& wa, B3Vec3& vb,
         B3Vec3& wb, B3Soft soft, int use_bias) {
-    B3Vec3 ra = b3_rotate(ldq(bc, BI(ja, BDQ)), ld3(src, JFPA));
-    B3Vec3 rb = b3_rotate(ldq(bc, BI(jb, BDQ)), ld3(src, JFPB));
+    B3Vec3 ra = b3_rotate(ldq(bp, BP(ja, BDQ)), ld3(src, JFPA));
+    B3Vec3 rb = b3_rotate(ldq(bp, BP(jb, BDQ)), ld3(src, JFPB));
     B3Vec3 cdot = b3_sub(b3_add(vb, b3_cross(wb, rb)), b3_add(va, b3_cross(wa, ra)));
     B3Vec3 bias = b3_v(0.0f, 0.0f, 0.0f);
     float mscale = 1.0f, iscale = 0.0f;
     if (use_bias) {
-        B3Vec3 sep = b3_add(b3_add(b3_sub(ld3(bc, BI(jb, BDP)), ld3(bc, BI(ja, BDP))), b3_sub(rb, ra)),
+        B3Vec3 sep = b3_add(b3_add(b3_sub(ld3(bp, BP(jb, BDP)), ld3(bp, BP(ja, BDP))), b3_sub(rb, ra)),
             ld3(src, JDC));
         bias = b3_mul(sep, soft.bias_rate);
         mscale = soft.mass_scale;
@@ -452,7 +453,8 @@ B3X_HDI float limit_impulse(float c, float cdot, float inv_h, int use_bias, B3So
 
 // One joint, either type (dispatch 07_packed.inl:66-79; weld 06_joints.inl:285-332;
 // revolute 06_joints.inl:436-642, default uncached path).
-B3X_HD void solve_joint(float* __restrict__ bc, const float* __restrict__ bk, const float* __restrict__ src, float* __restrict__ dst, float h,
+B3X_HD void solve_joint(float* __restrict__ bc, const float* __restrict__ bp, const float* __restrict__ bk,
+        const float* __restrict__ src, float* __restrict__ dst, float h,
         float inv_h, int use_bias) {
     int type = ldi(src, JTYPE);
     int ja = ldi(src, JBA), jb = ldi(src, JBB);
@@ -461,8 +463,8 @@ B3X_HD void solve_joint(float* __restrict__ bc, const float* __restrict__ bk, co
     B3Vec3 va = ld3(bc, BI(ja, BV)), wa = ld3(bc, BI(ja, BW));
     B3Vec3 vb = ld3(bc, BI(jb, BV)), wb = ld3(bc, BI(jb, BW));
     int fixed = ldi(src, JFIX);
-    B3Quat qa = b3_qmul(ldq(bc, BI(ja, BDQ)), ldq(src, JFQA));
-    B3Quat qb = b3_qmul(ldq(bc, BI(jb, BDQ)), ldq(src, JFQB));
+    B3Quat qa = b3_qmul(ldq(bp, BP(ja, BDQ)), ldq(src, JFQA));
+    B3Quat qb = b3_qmul(ldq(bp, BP(jb, BDQ)), ldq(src, JFQB));
     if (b3_qdot(qa, qb) < 0.0f) qb = b3_qneg(qb);
     B3Quat rel = b3_qinv_mul(qa, qb);
     if (type == B3_JOINT_WELD) {
@@ -488,7 +490,7 @@ B3X_HD void solve_joint(float* __restrict__ bc, const float* __restrict__ bk, co
             wb = b3_add(wb, b3_mv(ib, impulse));
         }
         int lin_bias = use_bias || COL(src, JLH) > 0.0f;
-        solve_point(bc, src, dst, ja, jb, ma, mb, ia, ib, va, wa, vb, wb, lds(src, JLS), lin_bias);
+        solve_point(bp, src, dst, ja, jb, ma, mb, ia, ib, va, wa, vb, wb, lds(src, JLS), lin_bias);
         put_vel(bc, bk, ja, va, wa);
         put_vel(bc, bk, jb, vb, wb);
         return;
@@ -598,17 +600,17 @@ B3X_HD void solve_joint(float* __restrict__ bc, const float* __restrict__ bk, co
         wa = b3_sub(wa, b3_mv(ia, ang));
         wb = b3_add(wb, b3_mv(ib, ang));
     }
-    solve_point(bc, src, dst, ja, jb, ma, mb, ia, ib, va, wa, vb, wb, soft, use_bias);
+    solve_point(bp, src, dst, ja, jb, ma, mb, ia, ib, va, wa, vb, wb, soft, use_bias);
     put_vel(bc, bk, ja, va, wa);
     put_vel(bc, bk, jb, vb, wb);
 }
 
 // ---- one warp of worlds, the solver part of one step ------------------------------
-// slot: the tile's workspace slot; lane: this world's lane; bc / bk: the body
-// state and body constant columns (lane-offset; shared memory or the slot's
-// body / bodyk regions).  Returns false when the pipeline failed.  Follows
+// slot: the tile's workspace slot; lane: this world's lane; bc / bp / bk: the
+// body velocity, pose-delta and constant columns (lane-offset; shared memory or
+// the slot's body / bodyp / bodyk regions).  Returns false when the pipeline failed.  Follows
 // 09_step.inl:158-181.
-B3X_HD bool solve_world(const Args& a, float* slot, int lane, float* __restrict__ bc,
+B3X_HD bool solve_world(const Args& a, float* slot, int lane, float* __restrict__ bc, float* __restrict__ bp,
         const float* __restrict__ bk, Pipe& P) {
     const float* rec = slot + a.SP.rec + lane;
     const int nb = ldi(rec, RNB);
@@ -647,19 +649,19 @@ B3X_HD bool solve_world(const Args& a, float* slot, int lane, float* __restrict_
         return false;
     any_rest = warp_any(any_rest);
     if (!stream_items(P, jc, NJF, kJointStream, wj, [&](int q, const float* src) {
-            if (q < nj && ldi(src, JOK)) warm_joint(bc, bk, src);
+            if (q < nj && ldi(src, JOK)) warm_joint(bc, bp, bk, src);
         }))
         return false;
 
     auto contact_pass = [&](auto pass) {
         constexpr int kPass = decltype(pass)::value;
         return stream_items(P, cc, kCI, kContactStream, wn, [&](int k, const float* src) {
-            if (k < n) solve_contact<kPass>(bc, bk, src, item(cc, k, kCI), inv_h, contact_speed, cs, ss);
+            if (k < n) solve_contact<kPass>(bc, bp, bk, src, item(cc, k, kCI), inv_h, contact_speed, cs, ss);
         });
     };
     auto joint_pass = [&](int use_bias) {
         return stream_items(P, jc, NJF, kJointStream, wj, [&](int q, const float* src) {
-            if (q < nj && ldi(src, JOK)) solve_joint(bc, bk, src, item(jc, q, NJF), h, inv_h, use_bias);
+            if (q < nj && ldi(src, JOK)) solve_joint(bc, bp, bk, src, item(jc, q, NJF), h, inv_h, use_bias);
         });
     };
     for (int s = 0; s < subs; s++) {
@@ -701,8 +703,8 @@ B3X_HD bool solve_world(const Args& a, float* slot, int lane, float* __restrict_
             if (w2 > max_ang2 && w2 > 0.0f) av = b3_mul(av, max_ang / sqrtf(w2));
             st3(bc, BI(k, BV), v);
             st3(bc, BI(k, BW), av);
-            st3(bc, BI(k, BDP), b3_madd(ld3(bc, BI(k, BDP)), h, v));
-            stq(bc, BI(k, BDQ), q_integrate(ldq(bc, BI(k, BDQ)), b3_mul(av, h)));
+            st3(bp, BP(k, BDP), b3_madd(ld3(bp, BP(k, BDP)), h, v));
+            stq(bp, BP(k, BDQ), q_integrate(ldq(bp, BP(k, BDQ)), b3_mul(av, h)));
         }
         if (!contact_pass(std::integral_constant<int, kRelax>{})) return false;
         for (int it = 0; it < a.relax_iters; it++)

@@ -62,12 +62,13 @@ struct DevExec {
 
 // Shared memory of a step block: the collide and write-back phases use it
 // as their block state; the solve phase as the streaming stages, their
-// mbarriers, then the body columns that live on chip: the body state and the
-// body constants (kBodyAll), the body state alone (kBodyState; the constants
-// are then read from the workspace through L1), or neither (kBodyNone).
+// mbarriers, then the body columns that live on chip, most-used first: the
+// velocities (every contact and joint row reads and writes them), the pose
+// deltas, the constants.  What stays off chip is read from the workspace
+// (through L1 for the constants, which the solve does not write).
 constexpr size_t kStageBytes = (size_t)kStages * kStreamWords * kLanes * sizeof(float);
 constexpr size_t kBarBytes = 64;
-enum BodyPlace : int { kBodyNone = 0, kBodyState = 1, kBodyAll = 2 };
+enum BodyPlace : int { kBodyNone = 0, kBodyVel = 1, kBodyState = 2, kBodyAll = 3 };
 
 // Warp 0's part of the step: warm start and substeps of the tile's 32 worlds.
 // Returns false when a pipeline wait gave up (nothing of the tile is then
@@ -80,22 +81,28 @@ __device__ bool solve_tile(const Args& a, unsigned char* smem_raw) {
     P.buf = reinterpret_cast<float*>(smem_raw);
     P.bar = reinterpret_cast<uint64_t*>(smem_raw + kStageBytes);
     pipe_init(P);
-    float* gb = slot + a.SP.body;
+    float* gv = slot + a.SP.body;
+    float* gp = slot + a.SP.bodyp;
     const float* gk = slot + a.SP.bodyk;
-    float* sb = reinterpret_cast<float*>(smem_raw + kStageBytes + kBarBytes);
-    float* sk = sb + (size_t)a.L.B * NBF * kLanes;
+    float* sv = reinterpret_cast<float*>(smem_raw + kStageBytes + kBarBytes);
+    float* sp = sv + (size_t)a.L.B * NBF * kLanes;
+    float* sk = sp + (size_t)a.L.B * NBP * kLanes;
     const int nb = warp_max(ldi(slot + a.SP.rec + lane, RNB));
     // each lane copies its own columns
-    if (kBody != kBodyNone)
-        for (int idx = lane; idx < nb * NBF * kLanes; idx += kLanes) sb[idx] = gb[idx];
+    if (kBody >= kBodyVel)
+        for (int idx = lane; idx < nb * NBF * kLanes; idx += kLanes) sv[idx] = gv[idx];
+    if (kBody >= kBodyState)
+        for (int idx = lane; idx < nb * NBP * kLanes; idx += kLanes) sp[idx] = gp[idx];
     if (kBody == kBodyAll)
         for (int idx = lane; idx < nb * NBC * kLanes; idx += kLanes) sk[idx] = gk[idx];
-    float* bc = (kBody != kBodyNone ? sb : gb) + lane;
+    float* bc = (kBody >= kBodyVel ? sv : gv) + lane;
+    float* bp = (kBody >= kBodyState ? sp : gp) + lane;
     const float* bk = (kBody == kBodyAll ? sk : gk) + lane;
-    const bool ok = solve_world(a, slot, lane, bc, bk, P);
-    if (ok && kBody != kBodyNone) {
-        for (int idx = lane; idx < nb * NBF * kLanes; idx += kLanes) gb[idx] = sb[idx];
-    }
+    const bool ok = solve_world(a, slot, lane, bc, bp, bk, P);
+    if (ok && kBody >= kBodyVel)
+        for (int idx = lane; idx < nb * NBF * kLanes; idx += kLanes) gv[idx] = sv[idx];
+    if (ok && kBody >= kBodyState)
+        for (int idx = lane; idx < nb * NBP * kLanes; idx += kLanes) gp[idx] = sp[idx];
     __syncwarp();
     if (lane == 0) {
         // the barriers' memory is reused by the write-back
@@ -235,18 +242,22 @@ static cudaError_t make_plan(int dev, unsigned long long sig, const Layout& L, P
     if (e != cudaSuccess) return e;
     const int cap = optin - (int)fa.sharedSizeBytes;
     // Body columns go on chip as far as kChunkBlocksPerSM blocks still fit
-    // on an SM: all of them, else the state the solver writes, else none.
+    // on an SM: velocities, then pose deltas, then constants.
     const size_t budget = (size_t)(per_sm / kChunkBlocksPerSM - reserved) - fa.sharedSizeBytes;
-    const size_t state_bytes = (size_t)L.B * NBF * kLanes * sizeof(float);
-    const size_t const_bytes = (size_t)L.B * NBC * kLanes * sizeof(float);
+    const size_t col = (size_t)L.B * kLanes * sizeof(float);
     const size_t base = kStageBytes + kBarBytes;
-    p.body = base + state_bytes + const_bytes <= budget ? kBodyAll
-           : base + state_bytes <= budget ? kBodyState : kBodyNone;
-    p.smem_bytes = base + (p.body != kBodyNone ? state_bytes : 0) + (p.body == kBodyAll ? const_bytes : 0);
+    const size_t upto[4] = {base, base + NBF * col, base + (NBF + NBP) * col, base + (NBF + NBP + NBC) * col};
+    p.body = kBodyNone;
+    for (int m = kBodyAll; m > kBodyNone; m--)
+        if (upto[m] <= budget) {
+            p.body = m;
+            break;
+        }
+    p.smem_bytes = upto[p.body];
     if (p.smem_bytes < sizeof(CollideShared)) p.smem_bytes = sizeof(CollideShared);
     if (p.smem_bytes < sizeof(OutShared)) p.smem_bytes = sizeof(OutShared);
     if (p.smem_bytes > (size_t)cap) return cudaErrorInvalidValue;
-    for (auto fn : {step_kernel<kBodyNone>, step_kernel<kBodyState>, step_kernel<kBodyAll>}) {
+    for (auto fn : {step_kernel<kBodyNone>, step_kernel<kBodyVel>, step_kernel<kBodyState>, step_kernel<kBodyAll>}) {
         e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, cap);
         if (e != cudaSuccess) return e;
     }
@@ -290,6 +301,7 @@ static cudaError_t launch_step(const B3Batch& batch, float dt, int substeps, con
         a.tile0 = t0;
         if (p.body == kBodyAll) step_kernel<kBodyAll><<<nt, kCta, p.smem_bytes, stream>>>(a);
         else if (p.body == kBodyState) step_kernel<kBodyState><<<nt, kCta, p.smem_bytes, stream>>>(a);
+        else if (p.body == kBodyVel) step_kernel<kBodyVel><<<nt, kCta, p.smem_bytes, stream>>>(a);
         else step_kernel<kBodyNone><<<nt, kCta, p.smem_bytes, stream>>>(a);
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return e;
