@@ -129,7 +129,7 @@ def cpu_reference_run(cfg, steps, warmup, budget_s):
                       "partitions, one pthread per host thread, %.2f s" % (worlds, steps, warmup, cpu_model(), secs)}
 
 
-def reference_gpu_run(cfg, steps, warmup, budget_s=20.0):
+def reference_gpu_run(cfg, steps, warmup, budget_s=60.0):
     """Time the reference's own GPU batch step (b3_batch_step_gpu: one thread
     per AoS world, oracle/_ref/libb3refgpu_<cfg>.so built from the reference
     sources with its stock nvcc flags) on this GPU: the scene's actions
@@ -173,7 +173,10 @@ def reference_gpu_run(cfg, steps, warmup, budget_s=20.0):
         assert L.refgpu_apply(worlds.data_ptr(), wb, 0, n, cfg.scene, SEED, 0, step_no[0], sp) == 0
         assert L.refgpu_batch_step(worlds.data_ptr(), wb, 0, n, cfg.dt, cfg.substeps, None, sp) == 0
 
-    for _ in range(max(warmup, 3)):
+    # the same warm-up and timed steps as this arm's own step, so both time
+    # the same stretch of the scene (a settling pile gains contacts); the
+    # last warm-up step sizes a cap for very slow cases
+    for _ in range(max(warmup, 3) - 1):
         one()
     torch.cuda.synchronize(dev)
     t0 = time.time()

@@ -842,7 +842,9 @@ B3X_API size_t b3x_workspace_bytes(unsigned long long config_signature, int devi
 
 /* No counterpart in the reference.  Number of kernel launches one
  * b3x_batch_step_gpu call of `count` worlds makes on `device` with its own
- * workspace (one per chunk of resident tiles); 0 if the configuration is
+ * workspace (one per chunk of resident tiles; one for configurations small
+ * enough to be stepped whole in shared memory, at most 8 bodies, 8 shapes
+ * and 8 contacts, which use no workspace); 0 if the configuration is
  * invalid.  For launch accounting by callers and benchmarks. */
 B3X_API int b3x_step_launches(unsigned long long config_signature, int count, int device);
 

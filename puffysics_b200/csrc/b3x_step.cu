@@ -19,6 +19,12 @@
 // Every loop is bounded by the world's capacities; the solver's pipeline
 // waits are bounded and report through b3x_fault_flags().
 //
+// Small worlds (a few bodies, shapes and contacts: the hover task) have too
+// little work per world for the tile phases to pay for their barriers; their
+// step is small_step_kernel: 32 worlds per block staged whole into shared
+// memory with asynchronous copies, one thread stepping one world there with
+// the per-world step of b3x_world_step.cuh, then copied back.
+//
 // Arithmetic.  The per-world work follows the reference's default
 // b3_step (src/puffysics/09_step.inl:183-258) operation by operation; the
 // library is compiled with -fmad=false and IEEE division / square root so
@@ -39,6 +45,7 @@
 #include "b3x_layout.cuh"
 #include "b3x_solver.cuh"
 #include "b3x_phases.cuh"
+#include "b3x_world_step.cuh"
 
 namespace b3x {
 
@@ -135,6 +142,78 @@ __global__ void __launch_bounds__(kCta, 4) step_kernel(Args a) {
     out_tile(x, a, blockIdx.x, *reinterpret_cast<OutShared*>(smem_raw));
 }
 
+// ---- small worlds -----------------------------------------------------------------
+// Capacity bounds of the small-world step (its per-world scratch is sized by
+// them) and the shared memory its 32 staged worlds may take.
+constexpr int kSmallB = 8, kSmallS = 8, kSmallC = 8;
+constexpr size_t kSmallSmemMax = 112 * 1024;
+#ifndef SMALL_WORLDS_PER_BLOCK
+#define SMALL_WORLDS_PER_BLOCK 8
+#endif
+using SmallView = one::WorldView<kSmallB, kSmallS, kSmallC>;
+
+// 8-byte words between staged worlds: the world rounded up so that
+// consecutive threads' worlds start in different bank pairs (the word stride
+// is 2 x odd, the least conflict an 8-byte aligned stride allows).
+static inline unsigned small_stride_words(const Layout& L) {
+    unsigned w = L.size / 8;
+    if (w % 2 == 0) w++;
+    return w;
+}
+
+__device__ __forceinline__ void async_copy8(void* dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+
+// One block of 32 threads per group of kSmallWorlds worlds: stage the
+// group's selected worlds, step each on its own thread, write them back
+// (unselected worlds are neither read nor written).  Groups smaller than a
+// warp spread the worlds over more SMs and let several warps of one SM share
+// the instruction fetches of this long per-world program.
+constexpr int kSmallWorlds = SMALL_WORLDS_PER_BLOCK;
+__global__ void __launch_bounds__(kLanes) small_step_kernel(Args a, unsigned stride_words) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    uint64_t* sw = reinterpret_cast<uint64_t*>(smem_raw);
+    const int lane = threadIdx.x;
+    const long long first = (long long)blockIdx.x * kSmallWorlds;
+    const unsigned words = a.L.size / 8;
+    const long long wi = first + lane;
+    const bool live = lane < kSmallWorlds && wi < a.count && (!a.active || a.active[wi]);
+    const unsigned live_mask = __ballot_sync(0xffffffffu, live);
+    auto world_ptr = [&](int l) {
+        return reinterpret_cast<uint64_t*>(a.data + (size_t)(first + l) * a.stride + a.offset);
+    };
+    for (int l = 0; l < kSmallWorlds; l++) {
+        if (!((live_mask >> l) & 1u)) continue;
+        const uint64_t* src = world_ptr(l);
+        uint64_t* dst = sw + (size_t)l * stride_words;
+        for (unsigned idx = lane; idx < words; idx += kLanes) async_copy8(dst + idx, src + idx);
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    __syncwarp();
+    if (live) {
+        unsigned char* base = smem_raw + (size_t)lane * stride_words * 8;
+        SmallView v;
+        v.h = reinterpret_cast<B3World*>(base);
+        v.bodies = reinterpret_cast<B3Body*>(base + B3X_WORLD_HEADER_BYTES);
+        v.shapes = reinterpret_cast<B3Shape*>(base + a.L.shape_off);
+        v.contacts = reinterpret_cast<B3Contact*>(base + a.L.contact_off);
+        v.joints = reinterpret_cast<B3Joint*>(base + a.L.joint_off);
+        v.cap_b = a.L.B;
+        v.cap_s = a.L.S;
+        v.cap_c = a.L.C;
+        v.cap_j = a.L.J;
+        one::step_view(v, a.dt, a.substeps, a.joint_iters, a.relax_iters);
+    }
+    __syncwarp();
+    for (int l = 0; l < kSmallWorlds; l++) {
+        if (!((live_mask >> l) & 1u)) continue;
+        uint64_t* dst = world_ptr(l);
+        const uint64_t* src = sw + (size_t)l * stride_words;
+        for (unsigned idx = lane; idx < words; idx += kLanes) dst[idx] = src[idx];
+    }
+}
+
 // ---- restore, actions --------------------------------------------------------
 // One warp per world, 8-byte words, coalesced on both sides.
 __global__ void restore_kernel(unsigned char* data, unsigned long long stride, unsigned long long offset, int count,
@@ -197,6 +276,9 @@ __global__ void observe_kernel(const unsigned char* data, unsigned long long str
 
 // ---- host side --------------------------------------------------------------
 struct Plan {
+    bool small;              // the small-world step (no workspace)
+    size_t small_smem;       // its dynamic shared memory per block
+    unsigned small_stride;   // its staged world stride (8-byte words)
     int body;                // BodyPlace of the solve
     Space SP;
     size_t smem_bytes;       // dynamic shared memory of a step block
@@ -263,6 +345,14 @@ static cudaError_t make_plan(int dev, unsigned long long sig, const Layout& L, P
     }
     p.chunk_tiles = sms * kChunkBlocksPerSM;
     p.ws_bytes = (size_t)p.chunk_tiles * p.tile_bytes;
+    p.small_stride = small_stride_words(L);
+    p.small_smem = (size_t)kSmallWorlds * p.small_stride * 8;
+    p.small = L.B <= kSmallB && L.S <= kSmallS && L.C <= kSmallC && p.small_smem <= kSmallSmemMax
+              && p.small_smem <= (size_t)optin;
+    if (p.small) {
+        e = cudaFuncSetAttribute(small_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.small_smem);
+        if (e != cudaSuccess) return e;
+    }
     g_plans[{dev, sig}] = p;
     *out = p;
     return cudaSuccess;
@@ -336,6 +426,7 @@ B3X_API int b3x_step_launches(unsigned long long sig, int count, int device) {
     Plan p;
     if (make_plan(device, sig, L, &p) != cudaSuccess) return 0;
     const int ntiles = (count + kLanes - 1) / kLanes;
+    if (p.small) return ntiles > 0 ? 1 : 0;
     return (ntiles + p.chunk_tiles - 1) / p.chunk_tiles;
 }
 
@@ -353,6 +444,26 @@ static int step_common(B3Batch batch, float dt, int substeps, const unsigned cha
     Plan p;
     e = make_plan(dev, sig, L, &p);
     if (e != cudaSuccess) return e;
+    if (p.small) {
+        // no workspace: the worlds are stepped in shared memory
+        Args a;
+        a.data = (unsigned char*)batch.data;
+        a.stride = batch.stride;
+        a.offset = batch.world_offset;
+        a.count = batch.count;
+        a.active = active;
+        a.dt = dt;
+        a.substeps = substeps;
+        a.joint_iters = ji;
+        a.relax_iters = ri;
+        a.L = L;
+        a.SP = p.SP;
+        a.ws = nullptr;
+        a.tile0 = 0;
+        const unsigned groups = (unsigned)((batch.count + kSmallWorlds - 1) / kSmallWorlds);
+        small_step_kernel<<<groups, kLanes, p.small_smem, (cudaStream_t)stream>>>(a, p.small_stride);
+        return (int)cudaGetLastError();
+    }
     if (own_ws) {
         std::lock_guard<std::mutex> lock(g_mutex);
         auto key = std::make_tuple(dev, stream, sig);

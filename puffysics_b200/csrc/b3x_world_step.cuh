@@ -115,24 +115,64 @@ __device__ __forceinline__ void store_vel(B3Body& b, B3Vec3 v, B3Vec3 w) {
     }
 }
 
+// One world's arrays.  The element structs do not depend on the capacities,
+// only the array lengths (and so the offsets of shapes, contacts and joints)
+// do: a view addresses a world image of any capacity configuration through
+// its header and four array bases.  kB / kS / kC bound the per-world scratch
+// and must be at least the capacities.
+template <int MB, int MS, int MC>
+struct WorldView {
+    static constexpr int kB = MB, kS = MS, kC = MC;
+    B3World* h;            // header fields only (their offsets are fixed)
+    B3Body* bodies;
+    B3Shape* shapes;
+    B3Contact* contacts;
+    B3Joint* joints;
+    int cap_b, cap_s, cap_c, cap_j;
+};
+
+// The view of a B3World of this translation unit's capacities.
+__device__ __forceinline__ WorldView<B3_MAX_BODIES, B3_MAX_SHAPES, B3_MAX_CONTACTS> view_of(B3World* w) {
+    WorldView<B3_MAX_BODIES, B3_MAX_SHAPES, B3_MAX_CONTACTS> v;
+    v.h = w;
+    v.bodies = w->bodies;
+    v.shapes = w->shapes;
+    v.contacts = w->contacts;
+    v.joints = w->joints;
+    v.cap_b = B3_MAX_BODIES;
+    v.cap_s = B3_MAX_SHAPES;
+    v.cap_c = B3_MAX_CONTACTS;
+    v.cap_j = B3_MAX_JOINTS;
+    return v;
+}
+
+__device__ __forceinline__ int clamp_count(int n, int cap) { return n < 0 ? 0 : (n > cap ? cap : n); }
+
 // The per-world step.  Scratch (the previous step's warm cache, the padded
 // shape boxes and the joint-connection bitset) lives in the thread's local
-// memory, as in the reference.
+// memory, as in the reference.  Counts beyond the capacities are clamped and
+// shapes or joints that name a body outside the world are inert (the
+// reference would index past its arrays), so a corrupt world cannot fault.
+template <class V>
 struct Stepper {
-    B3World& w;
+    V v;
+    int nb, ns, nj;
     float h, inv_h, inv_dt;
     B3Soft cs, ss;
     int joint_iters, relax_iters;
 
+    __device__ bool body_ok(int b) const { return b >= 0 && b < nb; }
+
     // ---- contacts: generation with warm carry (08_contacts.inl:5-39, 45-173)
     __device__ void find_contacts() {
-        Carry old[B3_MAX_CONTACTS];
-        B3AABB box[B3_MAX_SHAPES];
-        uint64_t conn[B3_MAX_BODIES][B3_CONNECT_WORDS];
-        const int old_n = w.contact_count;
+        Carry old[V::kC];
+        B3AABB box[V::kS];
+        constexpr int kWords = (V::kB + 63) / 64;
+        uint64_t conn[V::kB][kWords];
+        const int old_n = clamp_count(v.h->contact_count, v.cap_c);
         bool sorted = true;   // strictly increasing (shape_a, shape_b): unique pairs
         for (int k = 0; k < old_n; k++) {
-            const B3Contact& c = w.contacts[k];
+            const B3Contact& c = v.contacts[k];
             Carry& o = old[k];
             o.sa = c.shape_a;
             o.sb = c.shape_b;
@@ -148,28 +188,31 @@ struct Stepper {
             }
             if (k > 0 && !pair_less(old[k - 1].sa, old[k - 1].sb, o.sa, o.sb)) sorted = false;
         }
-        w.contact_count = 0;
-        for (int i = 0; i < w.body_count; i++)
-            for (int k = 0; k < B3_CONNECT_WORDS; k++) conn[i][k] = 0ull;
-        for (int i = 0; i < w.joint_count; i++) {
-            const B3Joint& j = w.joints[i];
-            if (j.collide_connected) continue;
+        v.h->contact_count = 0;
+        for (int i = 0; i < nb; i++)
+            for (int k = 0; k < kWords; k++) conn[i][k] = 0ull;
+        for (int i = 0; i < nj; i++) {
+            const B3Joint& j = v.joints[i];
+            if (j.collide_connected || !body_ok(j.body_a) || !body_ok(j.body_b)) continue;
             conn[j.body_a][j.body_b >> 6] |= 1ull << (j.body_b & 63);
             conn[j.body_b][j.body_a >> 6] |= 1ull << (j.body_a & 63);
         }
-        for (int i = 0; i < w.shape_count; i++) box[i] = padded_box(shape_geo(w.bodies[w.shapes[i].body], w.shapes[i]));
+        for (int i = 0; i < ns; i++)
+            if (body_ok(v.shapes[i].body)) box[i] = padded_box(shape_geo(v.bodies[v.shapes[i].body], v.shapes[i]));
 
         float clip[48];   // narrowphase polygon scratch (two 8-vertex polygons)
         Poly P;
         P.base = clip;
         P.stride = 1;
         int cursor = 0;   // merge cursor into the sorted old list
-        for (int i = 0; i < w.shape_count; i++) {
-            const B3Shape& sa = w.shapes[i];
-            const B3Body& ba = w.bodies[sa.body];
-            for (int j = i + 1; j < w.shape_count; j++) {
-                const B3Shape& sb = w.shapes[j];
-                const B3Body& bb = w.bodies[sb.body];
+        for (int i = 0; i < ns; i++) {
+            const B3Shape& sa = v.shapes[i];
+            if (!body_ok(sa.body)) continue;
+            const B3Body& ba = v.bodies[sa.body];
+            for (int j = i + 1; j < ns; j++) {
+                const B3Shape& sb = v.shapes[j];
+                if (!body_ok(sb.body)) continue;
+                const B3Body& bb = v.bodies[sb.body];
                 if (sa.body == sb.body || (conn[sa.body][sb.body >> 6] >> (sb.body & 63) & 1ull)
                         || (ba.type == B3_STATIC && bb.type == B3_STATIC)
                         || (sa.category & sb.mask) == 0 || (sb.category & sa.mask) == 0 || !overlap(box[i], box[j]))
@@ -178,12 +221,12 @@ struct Stepper {
                 m_clear(m);
                 collide(m, shape_geo(ba, sa), shape_geo(bb, sb), P);
                 if (m.count == 0) continue;
-                if (w.contact_count >= B3_MAX_CONTACTS) {
-                    w.contact_overflow = 1;
-                    w.contacts_dropped++;
+                if (v.h->contact_count >= v.cap_c) {
+                    v.h->contact_overflow = 1;
+                    v.h->contacts_dropped++;
                     continue;
                 }
-                B3Contact& c = w.contacts[w.contact_count++];
+                B3Contact& c = v.contacts[v.h->contact_count++];
                 c.shape_a = i;
                 c.shape_b = j;
                 c.body_a = sa.body;
@@ -239,8 +282,8 @@ struct Stepper {
 
     // 08_contacts.inl:234-291
     __device__ void prepare_contact(B3Contact& c) {
-        const B3Body& ba = w.bodies[c.body_a];
-        const B3Body& bb = w.bodies[c.body_b];
+        const B3Body& ba = v.bodies[c.body_a];
+        const B3Body& bb = v.bodies[c.body_b];
         bool da = ba.type == B3_DYNAMIC, db = bb.type == B3_DYNAMIC;
         float ma = da ? ba.inv_mass : 0.0f, mb = db ? bb.inv_mass : 0.0f;
         B3Mat3 ia = da ? ba.inv_i_world : m3_zero(), ib = db ? bb.inv_i_world : m3_zero();
@@ -286,8 +329,8 @@ struct Stepper {
 
     // 08_contacts.inl:293-313
     __device__ void warm_contact(const B3Contact& c) {
-        B3Body& ba = w.bodies[c.body_a];
-        B3Body& bb = w.bodies[c.body_b];
+        B3Body& ba = v.bodies[c.body_a];
+        B3Body& bb = v.bodies[c.body_b];
         const B3Vec3 n = c.normal;
         for (int p = 0; p < c.point_count; p++) {
             B3Vec3 P = b3_mul(n, c.points[p].normal_impulse);
@@ -306,13 +349,13 @@ struct Stepper {
     // friction and rolling resistance (08_contacts.inl:315-413,
     // 07_packed.inl:24-45).
     __device__ void solve_contact(B3Contact& c, bool use_bias) {
-        B3Body& ba = w.bodies[c.body_a];
-        B3Body& bb = w.bodies[c.body_b];
+        B3Body& ba = v.bodies[c.body_a];
+        B3Body& bb = v.bodies[c.body_b];
         B3Vec3 va = ba.lin_vel, wa = ba.ang_vel, vb = bb.lin_vel, wb = bb.ang_vel;
         const B3Quat dqa = ba.delta_rot, dqb = bb.delta_rot;
         const B3Vec3 dp = b3_sub(bb.delta_pos, ba.delta_pos);
         const B3Vec3 n = c.normal;
-        const float speed = w.contact_speed;
+        const float speed = v.h->contact_speed;
         float total_n = 0.0f, twist_lim = 0.0f;
         for (int p = 0; p < c.point_count; p++) {
             B3Point& q = c.points[p];
@@ -404,12 +447,12 @@ struct Stepper {
 
     // 08_contacts.inl:439-480
     __device__ void restitution() {
-        const float threshold = w.restitution_threshold;
-        for (int i = 0; i < w.contact_count; i++) {
-            B3Contact& c = w.contacts[i];
+        const float threshold = v.h->restitution_threshold;
+        for (int i = 0; i < v.h->contact_count; i++) {
+            B3Contact& c = v.contacts[i];
             if (c.restitution == 0.0f) continue;
-            B3Body& ba = w.bodies[c.body_a];
-            B3Body& bb = w.bodies[c.body_b];
+            B3Body& ba = v.bodies[c.body_a];
+            B3Body& bb = v.bodies[c.body_b];
             B3Vec3 va = ba.lin_vel, wa = ba.ang_vel, vb = bb.lin_vel, wb = bb.ang_vel;
             const B3Vec3 n = c.normal;
             for (int p = 0; p < c.point_count; p++) {
@@ -435,8 +478,8 @@ struct Stepper {
     // ---- joints (06_joints.inl) ---------------------------------------------
     // 06_joints.inl:161-202
     __device__ void prepare_joint(B3Joint& j) {
-        const B3Body& ba = w.bodies[j.body_a];
-        const B3Body& bb = w.bodies[j.body_b];
+        const B3Body& ba = v.bodies[j.body_a];
+        const B3Body& bb = v.bodies[j.body_b];
         bool da = ba.type == B3_DYNAMIC, db = bb.type == B3_DYNAMIC;
         j.inv_mass_a = da ? ba.inv_mass : 0.0f;
         j.inv_mass_b = db ? bb.inv_mass : 0.0f;
@@ -467,8 +510,8 @@ struct Stepper {
 
     // 06_joints.inl:204-239
     __device__ void warm_joint(const B3Joint& j) {
-        B3Body& ba = w.bodies[j.body_a];
-        B3Body& bb = w.bodies[j.body_b];
+        B3Body& ba = v.bodies[j.body_a];
+        B3Body& bb = v.bodies[j.body_b];
         B3Vec3 ra = b3_rotate(ba.delta_rot, j.frame_p_a);
         B3Vec3 rb = b3_rotate(bb.delta_rot, j.frame_p_b);
         B3Vec3 ang = j.angular_impulse;
@@ -523,8 +566,8 @@ struct Stepper {
 
     // 06_joints.inl:285-332
     __device__ void solve_weld(B3Joint& j, bool use_bias) {
-        B3Body& ba = w.bodies[j.body_a];
-        B3Body& bb = w.bodies[j.body_b];
+        B3Body& ba = v.bodies[j.body_a];
+        B3Body& bb = v.bodies[j.body_b];
         B3Vec3 va = ba.lin_vel, wa = ba.ang_vel, vb = bb.lin_vel, wb = bb.ang_vel;
         B3Quat qa = b3_qmul(ba.delta_rot, j.frame_q_a);
         B3Quat qb = b3_qmul(bb.delta_rot, j.frame_q_b);
@@ -570,8 +613,8 @@ struct Stepper {
 
     // Spring, motor, limits, perpendicular rows, point (06_joints.inl:436-642).
     __device__ void solve_revolute(B3Joint& j, bool use_bias) {
-        B3Body& ba = w.bodies[j.body_a];
-        B3Body& bb = w.bodies[j.body_b];
+        B3Body& ba = v.bodies[j.body_a];
+        B3Body& bb = v.bodies[j.body_b];
         B3Vec3 va = ba.lin_vel, wa = ba.ang_vel, vb = bb.lin_vel, wb = bb.ang_vel;
         B3Quat qa = b3_qmul(ba.delta_rot, j.frame_q_a);
         B3Quat qb = b3_qmul(bb.delta_rot, j.frame_q_b);
@@ -675,39 +718,42 @@ struct Stepper {
     }
 
     // Joint sweeps in joint index order (07_packed.inl:48-81).
+    __device__ bool joint_ok(const B3Joint& j) const { return body_ok(j.body_a) && body_ok(j.body_b); }
+
     __device__ void solve_joints(bool use_bias, int iters) {
         for (int it = 0; it < iters; it++)
-            for (int i = 0; i < w.joint_count; i++) {
-                B3Joint& j = w.joints[i];
+            for (int i = 0; i < nj; i++) {
+                B3Joint& j = v.joints[i];
+                if (!joint_ok(j)) continue;
                 if (j.type == B3_JOINT_WELD) solve_weld(j, use_bias);
                 else solve_revolute(j, use_bias);
             }
     }
 
     __device__ void solve_contacts(bool use_bias) {
-        for (int i = 0; i < w.contact_count; i++) solve_contact(w.contacts[i], use_bias);
+        for (int i = 0; i < v.h->contact_count; i++) solve_contact(v.contacts[i], use_bias);
     }
 
     // ---- integration (09_step.inl:5-130) ---------------------------------------
     __device__ void integrate_velocities() {
-        for (int i = 0; i < w.body_count; i++) {
-            B3Body& b = w.bodies[i];
+        for (int i = 0; i < nb; i++) {
+            B3Body& b = v.bodies[i];
             if (b.type != B3_DYNAMIC) continue;
             float ld = 1.0f / (1.0f + h * b.linear_damping);
             float ad = 1.0f / (1.0f + h * b.angular_damping);
             float gs = b.inv_mass > 0.0f ? b.gravity_scale : 0.0f;
-            B3Vec3 dv = b3_add(b3_mul(b.force, h * b.inv_mass), b3_mul(w.gravity, h * gs));
+            B3Vec3 dv = b3_add(b3_mul(b.force, h * b.inv_mass), b3_mul(v.h->gravity, h * gs));
             b.lin_vel = b3_madd(dv, ld, b.lin_vel);
             b.ang_vel = b3_madd(b3_mul(b3_mv(b.inv_i_world, b.torque), h), ad, b.ang_vel);
         }
     }
 
     __device__ void integrate_positions() {
-        const float max_lin = w.max_linear_speed;
+        const float max_lin = v.h->max_linear_speed;
         const float max_ang = B3_MAX_ROTATION * inv_dt;
         const float max_lin2 = max_lin * max_lin, max_ang2 = max_ang * max_ang;
-        for (int i = 0; i < w.body_count; i++) {
-            B3Body& b = w.bodies[i];
+        for (int i = 0; i < nb; i++) {
+            B3Body& b = v.bodies[i];
             if (b.type == B3_STATIC) continue;
             B3Vec3 v = b.lin_vel, av = b.ang_vel;
             const uint32_t f = b.flags;
@@ -729,8 +775,8 @@ struct Stepper {
     }
 
     __device__ void finalize() {
-        for (int i = 0; i < w.body_count; i++) {
-            B3Body& b = w.bodies[i];
+        for (int i = 0; i < nb; i++) {
+            B3Body& b = v.bodies[i];
             if (b.type == B3_STATIC) continue;
             b.center = b3_add(b.center, b.delta_pos);
             b.rotation = b3_qnorm(b3_qmul(b.delta_rot, b.rotation));
@@ -745,10 +791,12 @@ struct Stepper {
 
     __device__ void run(int subs) {
         find_contacts();
-        for (int i = 0; i < w.contact_count; i++) prepare_contact(w.contacts[i]);
-        for (int i = 0; i < w.joint_count; i++) prepare_joint(w.joints[i]);
-        for (int i = 0; i < w.contact_count; i++) warm_contact(w.contacts[i]);
-        for (int i = 0; i < w.joint_count; i++) warm_joint(w.joints[i]);
+        for (int i = 0; i < v.h->contact_count; i++) prepare_contact(v.contacts[i]);
+        for (int i = 0; i < nj; i++)
+            if (joint_ok(v.joints[i])) prepare_joint(v.joints[i]);
+        for (int i = 0; i < v.h->contact_count; i++) warm_contact(v.contacts[i]);
+        for (int i = 0; i < nj; i++)
+            if (joint_ok(v.joints[i])) warm_joint(v.joints[i]);
         for (int s = 0; s < subs; s++) {
             integrate_velocities();
             solve_contacts(true);
@@ -762,19 +810,32 @@ struct Stepper {
     }
 };
 
-// b3_step_indep (09_step.inl:183-258) with run-time solver iteration counts.
-__device__ inline void step_world(B3World* w, float dt, int substeps, int joint_iters, int relax_iters) {
+// b3_step_indep (09_step.inl:183-258) of the world a view addresses, with
+// run-time solver iteration counts.
+template <class V>
+__device__ inline void step_view(const V& v, float dt, int substeps, int joint_iters, int relax_iters) {
     if (dt <= 0.0f) return;
     const int subs = substeps < 1 ? 1 : substeps;
-    Stepper st{*w, 0.0f, 0.0f, 0.0f, {}, {}, joint_iters, relax_iters};
+    Stepper<V> st;
+    st.v = v;
+    st.nb = clamp_count(v.h->body_count, v.cap_b < V::kB ? v.cap_b : V::kB);
+    st.ns = clamp_count(v.h->shape_count, v.cap_s < V::kS ? v.cap_s : V::kS);
+    st.nj = clamp_count(v.h->joint_count, v.cap_j);
+    st.joint_iters = joint_iters;
+    st.relax_iters = relax_iters;
     // b3_soft_step_params (09_step.inl:148-157)
     st.h = dt / (float)subs;
     st.inv_dt = 1.0f / dt;
     st.inv_h = (float)subs * st.inv_dt;
-    float hertz = b3_minf(w->contact_hertz, 0.25f * st.inv_h);
-    st.cs = make_soft(hertz, w->contact_damping, st.h);
-    st.ss = make_soft(2.0f * hertz, 0.5f * w->contact_damping, st.h);
+    float hertz = b3_minf(v.h->contact_hertz, 0.25f * st.inv_h);
+    st.cs = make_soft(hertz, v.h->contact_damping, st.h);
+    st.ss = make_soft(2.0f * hertz, 0.5f * v.h->contact_damping, st.h);
     st.run(subs);
+}
+
+// b3_step_indep on a B3World of this translation unit's capacities.
+__device__ inline void step_world(B3World* w, float dt, int substeps, int joint_iters, int relax_iters) {
+    step_view(view_of(w), dt, substeps, joint_iters, relax_iters);
 }
 
 }  // namespace one

@@ -185,3 +185,30 @@ def test_corrupt_counts_are_clamped_not_faulting(stack_pair):
     assert step(dev) == 0
     out = layout.view(dev.cpu().numpy(), STACK.caps)
     assert out["contact_count"][1] == 0
+
+
+@pytest.mark.parametrize("n", [1, 33, 997])
+def test_small_world_path_mask_and_embedding(n, oracle_kind, gpu_lib):
+    """Hover worlds take the small-world step (whole worlds staged in shared
+    memory, one thread per world): embedded worlds with a mask and a ragged
+    last tile match the reference; masked-out worlds and the bytes around
+    every world are untouched."""
+    cfg = CONFIGS["hover"]
+    assert engine.step_launches(cfg.caps, n) == 1
+    o = orc.Oracle("hover", oracle_kind)
+    host = o.build(n, cfg.scene, 21)
+    wb = host.shape[1]
+    stride, off = wb + 48, 16
+    rng = np.random.default_rng(n)
+    env = rng.integers(0, 256, size=(n, stride), dtype=np.uint8)
+    env[:, off:off + wb] = host
+    dev = torch.from_numpy(env.copy()).cuda()
+    ref = env.copy()
+    for s in range(1, 8):
+        mask = (rng.random(n) < 0.7).astype(np.uint8)
+        o.batch_step(ref, cfg.dt, cfg.substeps, active=mask, stride=stride, offset=off)
+        rc = engine.batch_step_gpu(dev, cfg.dt, cfg.substeps, active=torch.from_numpy(mask).cuda(), caps=cfg.caps,
+                                   joint_iters=cfg.joint_iters, stride=stride, offset=off)
+        assert rc == 0
+    torch.cuda.synchronize()
+    assert np.array_equal(dev.cpu().numpy(), ref)
