@@ -68,6 +68,8 @@ def parse_args():
     ap.add_argument("--e2e-steps", type=int, default=200)
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-per-thread-path", action="store_true",
+                    help="skip the timing of the per-thread device b3_step after the main measurement")
     return ap.parse_args()
 
 
@@ -499,7 +501,7 @@ def main():
                 "clocks": sampler.summary(),
                 "diagnostics": {"worlds": int(tot[0]), "contacts": int(tot[1]), "overflowed_worlds": int(tot[2]),
                                 "dropped_contacts": int(tot[3])}}
-        if world == 1:
+        if world == 1 and not args.no_per_thread_path:
             line["per_thread_path"] = thread_path_run(cfg, worlds, K, args.warmup, stream)
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_reference_run(cfg, steps=None, warmup=2, budget_s=args.cpu_seconds)
