@@ -186,14 +186,20 @@ def reference_gpu_run(cfg, steps, warmup, budget_s=60.0):
     torch.cuda.synchronize(dev)
     est = max(time.time() - t0, 1e-4)
     k = int(max(3, min(steps or 100, budget_s / est)))
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(k):
+    # the same L2 rule as this arm's own step: flush between timed steps
+    # (outside the events) unless the world array is larger than twice L2
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev) if n * wb < L2_BYTES * 2 else None
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(k)]
+    for e0, e1 in ev:
+        if flush is not None:
+            flush.zero_()
+        e0.record(stream)
         one()
-    e1.record(stream)
+        e1.record(stream)
     torch.cuda.synchronize(dev)
-    ms = e0.elapsed_time(e1)
+    ms = sum(e0.elapsed_time(e1) for e0, e1 in ev)
     return {"value": n * k / (ms / 1e3), "unit": UNIT, "ms_per_step": ms / k, "worlds": n, "steps": k,
+            "l2": "flushed between timed steps" if flush is not None else "world array larger than twice L2",
             "kernel": "reference b3_batch_step_gpu (b3_batch.cuh:63-89), one thread per world, nvcc -O3 sm_100a",
             "note": "the reference's GPU kernel on this GPU, timed like the step (actions + step, events)"}
 

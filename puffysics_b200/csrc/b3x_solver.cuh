@@ -207,7 +207,7 @@ enum : int { kBiasFresh = 0, kBiasCached = 1, kRelax = 2 };
 // Reads contact k from src (shared-memory copy or workspace), writes the
 // solver-owned fields to dst (workspace).
 template <int kPass>
-B3X_HD void solve_contact(float* __restrict__ bc, const float* __restrict__ bp, const float* __restrict__ bk,
+B3X_HDI void solve_contact(float* __restrict__ bc, const float* __restrict__ bp, const float* __restrict__ bk,
         const float* __restrict__ src, float* __restrict__ dst, float inv_h, float speed, B3Soft cs, B3Soft ss) {
     constexpr bool use_bias = kPass != kRelax;
     int ba = ldi(src, WBA), bb = ldi(src, WBB);
@@ -333,7 +333,7 @@ B3X_HD void solve_contact(float* __restrict__ bc, const float* __restrict__ bp, 
 }
 
 // Restitution of one contact (08_contacts.inl:439-480).
-B3X_HD void restitute_contact(float* __restrict__ bc, const float* __restrict__ bk, const float* __restrict__ src, float* __restrict__ dst,
+B3X_HDI void restitute_contact(float* __restrict__ bc, const float* __restrict__ bk, const float* __restrict__ src, float* __restrict__ dst,
         float threshold) {
     float rest = COL(src, WREST);
     if (rest == 0.0f) return;
@@ -453,7 +453,7 @@ B3X_HDI float limit_impulse(float c, float cdot, float inv_h, int use_bias, B3So
 
 // One joint, either type (dispatch 07_packed.inl:66-79; weld 06_joints.inl:285-332;
 // revolute 06_joints.inl:436-642, default uncached path).
-B3X_HD void solve_joint(float* __restrict__ bc, const float* __restrict__ bp, const float* __restrict__ bk,
+B3X_HDI void solve_joint(float* __restrict__ bc, const float* __restrict__ bp, const float* __restrict__ bk,
         const float* __restrict__ src, float* __restrict__ dst, float h,
         float inv_h, int use_bias) {
     int type = ldi(src, JTYPE);
