@@ -204,6 +204,100 @@ def reference_gpu_run(cfg, steps, warmup, budget_s=60.0):
             "note": "the reference's GPU kernel on this GPU, timed like the step (actions + step, events)"}
 
 
+def _timed_steps(one, k, warmup, flush, stream):
+    """k steps of `one` after `warmup`, CUDA events around each step, L2
+    flushed between steps (outside the events) when `flush` is given;
+    returns milliseconds per step."""
+    import torch
+    for _ in range(max(warmup, 3)):
+        one()
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(k)]
+    for e0, e1 in ev:
+        if flush is not None:
+            flush.zero_()
+        e0.record(stream)
+        one()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    return sum(e0.elapsed_time(e1) for e0, e1 in ev) / k
+
+
+HOVER_ENVS = 4096    # puffysics_hover.ini [vec] total_agents
+
+
+def fused_env_run(steps, warmup, stream):
+    """The PufferLib hover environment step fused into one launch
+    (libb3hover.so): action, physics, reward, terminal, log, automatic reset
+    and observation of 4,096 environments per step."""
+    import torch
+    from puffysics_b200 import hover_env
+    n = HOVER_ENVS
+    dev = torch.device("cuda", torch.cuda.current_device())
+    envs = torch.zeros((n, hover_env.env_bytes()), dtype=torch.uint8, device=dev)
+    assert hover_env.init(envs, SEED, stream) == 0
+    obs = torch.zeros((n, 3), dtype=torch.float32, device=dev)
+    rew = torch.zeros(n, dtype=torch.float32, device=dev)
+    term = torch.zeros(n, dtype=torch.float32, device=dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(SEED)
+    acts = torch.randint(0, 3, (16, n), generator=g, device=dev).float()
+    k_no = [0]
+
+    def one():
+        k_no[0] += 1
+        assert hover_env.step(envs, acts[k_no[0] % 16], obs, rew, term, stream) == 0
+
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    ms = _timed_steps(one, steps, warmup, flush, stream)
+    return {"value": n / (ms / 1e3), "unit": UNIT, "ms_per_step": ms, "envs": n, "steps": steps,
+            "kernel": "b3x_hover_step_gpu: environments staged in shared memory, eight per 32-thread block",
+            "l2": "flushed between timed steps"}
+
+
+def reference_gpu_env_run(steps, warmup):
+    """The reference hover adapter's step kernel shape (puffysics_hover.cu:40-43:
+    one thread per environment in place) over the reference's hover_task.h,
+    oracle/_ref/libb3refgpu_hoverenv.so; same environments and actions as
+    fused_env_run."""
+    import ctypes
+    import torch
+    path = os.path.join(ROOT, "oracle", "_ref", "libb3refgpu_hoverenv.so")
+    if not torch.cuda.is_available() or not os.path.exists(path):
+        return None
+    L = ctypes.CDLL(path)
+    vp = ctypes.c_void_p
+    L.refhover_task_bytes.restype = ctypes.c_size_t
+    L.refhover_gpu_init.argtypes = [vp, ctypes.c_int, ctypes.c_float, ctypes.c_float, ctypes.c_float, ctypes.c_int,
+                                    ctypes.c_int, ctypes.c_uint, vp]
+    L.refhover_gpu_step.argtypes = [vp, vp, ctypes.c_int, vp, vp, vp, vp, vp]
+    n = HOVER_ENVS
+    dev = torch.device("cuda", torch.cuda.current_device())
+    stream = torch.cuda.current_stream(dev)
+    sp = ctypes.c_void_p(stream.cuda_stream)
+    tasks = torch.zeros((n, L.refhover_task_bytes()), dtype=torch.uint8, device=dev)
+    logs = torch.zeros((n, 5), dtype=torch.float32, device=dev)
+    assert L.refhover_gpu_init(tasks.data_ptr(), n, 2.0, 10.0, 1.0 / 60.0, 4, 256, SEED, sp) == 0
+    obs = torch.zeros((n, 3), dtype=torch.float32, device=dev)
+    rew = torch.zeros(n, dtype=torch.float32, device=dev)
+    term = torch.zeros(n, dtype=torch.float32, device=dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(SEED)
+    acts = torch.randint(0, 3, (16, n), generator=g, device=dev).float()
+    k_no = [0]
+
+    def one():
+        k_no[0] += 1
+        assert L.refhover_gpu_step(tasks.data_ptr(), logs.data_ptr(), n, acts[k_no[0] % 16].data_ptr(),
+                                   obs.data_ptr(), rew.data_ptr(), term.data_ptr(), sp) == 0
+
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    ms = _timed_steps(one, steps, warmup, flush, stream)
+    return {"value": n / (ms / 1e3), "unit": UNIT, "ms_per_step": ms, "envs": n, "steps": steps,
+            "kernel": "reference hover task (hover_task.h) in the adapter's kernel shape, one thread per "
+                      "environment in place, nvcc -O3 sm_100a", "l2": "flushed between timed steps"}
+
+
 def thread_path_run(cfg, worlds, steps, warmup, stream):
     """Time this library's per-thread device b3_step (include/puffysics.cuh,
     one thread per world, libb3thread_<cfg>.so) on a copy of the worlds: the
@@ -308,6 +402,7 @@ def main():
         if rank == 0:
             ref = cpu_reference_run(cfg, args.steps, args.warmup, budget_s=max(30.0, args.cpu_seconds))
             ref_gpu = reference_gpu_run(cfg, args.steps, args.warmup)
+            ref_env = reference_gpu_env_run(args.steps, args.warmup) if cfg.name == "hover" else None
             print(json.dumps({"impl": "reference", "metric": METRIC, "value": ref["value"], "unit": UNIT,
                               "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
                               "ms_per_step": None, "higher_is_better": True, "scaling": "weak",
@@ -318,7 +413,8 @@ def main():
                               "cpu_baseline": ref,
                               "e2e": {"value": ref["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
                                       "d2h_bytes_per_step": 0},
-                              "reference_gpu": ref_gpu}), flush=True)
+                              "reference_gpu": ref_gpu,
+                              **({"reference_gpu_env": ref_env} if ref_env else {})}), flush=True)
         return
 
     import torch
@@ -509,6 +605,8 @@ def main():
                                 "dropped_contacts": int(tot[3])}}
         if world == 1 and not args.no_per_thread_path:
             line["per_thread_path"] = thread_path_run(cfg, worlds, K, args.warmup, stream)
+            if cfg.name == "hover":
+                line["fused_env"] = fused_env_run(K, args.warmup, stream)
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_reference_run(cfg, steps=None, warmup=2, budget_s=args.cpu_seconds)
         print(json.dumps(line), flush=True)

@@ -124,3 +124,36 @@ class Oracle:
     def run_mt(self, worlds, scene, seed, first, step0, steps, dt, substeps, threads):
         return self._f("run_mt")(_ptr(worlds), worlds.shape[0], scene, seed, first, step0, steps, dt,
                                  substeps, threads)
+
+
+class HoverOracle:
+    """The reference's hover task on the CPU (oracle/_ref/libb3ref_hoverenv.so,
+    hover_task.h compiled from the reference), over (n, task_bytes) uint8
+    arrays; logs are float32 (n, 5)."""
+
+    def __init__(self):
+        path = os.path.join(HERE, "_ref", "libb3ref_hoverenv.so")
+        if not os.path.exists(path):
+            raise FileNotFoundError(path)
+        L = ctypes.CDLL(path)
+        L.refhover_task_bytes.restype = ctypes.c_size_t
+        vp = ctypes.c_void_p
+        L.refhover_init.argtypes = [vp, ctypes.c_int, ctypes.c_float, ctypes.c_float, ctypes.c_float, ctypes.c_int,
+                                    ctypes.c_int, ctypes.c_uint]
+        L.refhover_step.argtypes = [vp, vp, ctypes.c_int, vp, vp, vp, vp]
+        self.L = L
+        self.task_bytes = L.refhover_task_bytes()
+
+    def init(self, n, seed, target_height=2.0, thrust=10.0, dt=1.0 / 60.0, substeps=4, horizon=256):
+        t = np.zeros((n, self.task_bytes), dtype=np.uint8)
+        self.L.refhover_init(_ptr(t), n, target_height, thrust, dt, substeps, horizon, seed)
+        return t, np.zeros((n, 5), dtype=np.float32)
+
+    def step(self, tasks, logs, actions):
+        n = tasks.shape[0]
+        obs = np.zeros((n, 3), dtype=np.float32)
+        rew = np.zeros(n, dtype=np.float32)
+        term = np.zeros(n, dtype=np.float32)
+        a = np.ascontiguousarray(actions, dtype=np.float32)
+        self.L.refhover_step(_ptr(tasks), _ptr(logs), n, _ptr(a), _ptr(obs), _ptr(rew), _ptr(term))
+        return obs, rew, term

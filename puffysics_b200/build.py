@@ -27,6 +27,10 @@ SCENES_SRC = os.path.join(PKG, "scenes", "b3_scenes_host.c")
 THREAD_SRC = os.path.join(PKG, "csrc", "b3x_thread_step.cu")
 THREAD_HEADERS = [os.path.join(ROOT, "include", "puffysics.cuh"),
                   os.path.join(PKG, "csrc", "b3x_world_step.cuh")]
+# the hover environment fused into one launch per step (libb3hover.so)
+HOVER_SRC = os.path.join(PKG, "csrc", "b3x_hover_env.cu")
+HOVER_LIB = os.path.join(LIB_DIR, "libb3hover.so")
+HOVER_HEADERS = THREAD_HEADERS + [os.path.join(ROOT, "include", "b3x_staged.cuh")]
 # capacity configurations the host scene builders are compiled for:
 # name -> (bodies, shapes, contacts, joints)
 SCENE_CONFIGS = {"hover": (2, 2, 4, 1), "stack": (9, 9, 32, 1), "chain": (12, 12, 32, 10),
@@ -66,18 +70,27 @@ def thread_cmd(name):
             + caps + [THREAD_SRC, "-o", thread_lib(name)])
 
 
+def hover_cmd():
+    return ([NVCC] + ARCH + ["-lineinfo", "-O3", "-std=c++17"] + PARITY
+            + ["-Xcompiler", "-fPIC,-fvisibility=hidden", "-shared", "-cudart", "static",
+               "-I" + os.path.join(ROOT, "include"), "-I" + os.path.join(PKG, "csrc"), HOVER_SRC, "-o", HOVER_LIB])
+
+
 def build_thread_libs(force=False):
-    """The per-thread step launchers, one per capacity configuration, compiled
-    concurrently."""
+    """The per-thread step launchers, one per capacity configuration, and the
+    hover environment library, compiled concurrently."""
     deps = [THREAD_SRC, __file__] + HEADERS + THREAD_HEADERS
     todo = [n for n in THREAD_CONFIGS if force or _newer(thread_lib(n), deps)]
-    procs = [(n, subprocess.Popen(thread_cmd(n), stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True))
-             for n in todo]
+    cmds = {n: thread_cmd(n) for n in todo}
+    if force or _newer(HOVER_LIB, [HOVER_SRC, __file__] + HEADERS + HOVER_HEADERS):
+        cmds["hover environment"] = hover_cmd()
+    procs = [(n, subprocess.Popen(c, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True))
+             for n, c in cmds.items()]
     errors = []
     for n, p in procs:
         out, _ = p.communicate()
         if p.returncode != 0:
-            errors.append("per-thread library %s failed:\n%s\n%s" % (n, " ".join(thread_cmd(n)), out))
+            errors.append("library %s failed:\n%s\n%s" % (n, " ".join(cmds[n]), out))
     if errors:
         raise RuntimeError("\n".join(errors))
 
@@ -97,7 +110,8 @@ def up_to_date():
     deps = SOURCES + HEADERS + [__file__]
     thread_deps = [THREAD_SRC, __file__] + HEADERS + THREAD_HEADERS
     return (not _newer(LIB, deps) and not any(_newer(scenes_lib(n), [SCENES_SRC] + HEADERS) for n in SCENE_CONFIGS)
-            and not any(_newer(thread_lib(n), thread_deps) for n in THREAD_CONFIGS))
+            and not any(_newer(thread_lib(n), thread_deps) for n in THREAD_CONFIGS)
+            and not _newer(HOVER_LIB, [HOVER_SRC, __file__] + HEADERS + HOVER_HEADERS))
 
 
 def build_scenes(force=False):
