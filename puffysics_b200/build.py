@@ -35,12 +35,13 @@ HOVER_HEADERS = THREAD_HEADERS + [os.path.join(ROOT, "include", "b3x_staged.cuh"
 # name -> (bodies, shapes, contacts, joints)
 SCENE_CONFIGS = {"hover": (2, 2, 4, 1), "stack": (9, 9, 32, 1), "chain": (12, 12, 32, 10),
                  "pile": (37, 37, 128, 1), "hovertask": (2, 2, 4, 2), "default": (80, 128, 128, 32),
-                 "stacksmall": (9, 9, 4, 1)}
+                 "stacksmall": (9, 9, 4, 1), "bounce": (9, 9, 32, 1)}
 # per-thread step launchers (include/puffysics.cuh's device b3_step): name ->
 # (bodies, shapes, contacts, joints, B3_JOINT_ITERS), the capacities of the
 # benchmark configurations and of the reference's defaults
 THREAD_CONFIGS = {"hover": (2, 2, 4, 1, 8), "stack": (9, 9, 32, 1, 8), "chain": (12, 12, 32, 10, 8),
-                  "pile": (37, 37, 128, 1, 8), "hovertask": (2, 2, 4, 2, 2), "default": (80, 128, 128, 32, 2)}
+                  "pile": (37, 37, 128, 1, 8), "hovertask": (2, 2, 4, 2, 2), "default": (80, 128, 128, 32, 2),
+                  "bounce": (9, 9, 32, 1, 8)}
 CC = os.environ.get("CC", "gcc")
 
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc" if os.path.exists("/usr/local/cuda/bin/nvcc") else "nvcc")

@@ -6,7 +6,7 @@ counts, timestep, substeps and the world count of the configuration.
 """
 from dataclasses import dataclass
 
-SCENE_HOVER, SCENE_STACK, SCENE_CHAIN, SCENE_PILE = 1, 2, 3, 4
+SCENE_HOVER, SCENE_STACK, SCENE_CHAIN, SCENE_PILE, SCENE_BOUNCE = 1, 2, 3, 4, 5
 ACT_NONE, ACT_FORCE, ACT_TORQUE, ACT_LINEAR_IMPULSE, ACT_JOINT_TARGET = -1, 0, 1, 2, 3
 
 
@@ -50,6 +50,8 @@ CONFIGS = {
     # outside shared memory) and a contact capacity the stack overflows
     "default": Config("default", SCENE_PILE, (80, 128, 128, 32), 2, 2, 1.0 / 60.0, 4, 1024,
                       description="pile scene at the reference's default capacities"),
+    "bounce": Config("bounce", SCENE_BOUNCE, (9, 9, 32, 1), 8, 8, 1.0 / 60.0, 4, 1024,
+                     description="spheres and boxes with restitution and rolling resistance (parity coverage)"),
     "stacksmall": Config("stacksmall", SCENE_STACK, (9, 9, 4, 1), 2, 2, 1.0 / 60.0, 4, 1024,
                          description="stack scene with 4 contact slots (overflow path)"),
     "scaleout": Config("stack", SCENE_STACK, (9, 9, 32, 1), 8, 8, 1.0 / 60.0, 4, 1048576,

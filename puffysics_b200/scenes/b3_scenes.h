@@ -28,6 +28,7 @@
 #define B3S_STACK 2
 #define B3S_CHAIN 3
 #define B3S_PILE 4
+#define B3S_BOUNCE 5
 
 /* Action kinds (same numbering as the b3x_batch_apply_gpu C-ABI). */
 #define B3S_ACT_NONE (-1)
@@ -250,12 +251,57 @@ static inline int b3s_build_pile(B3World* w, uint64_t seed, uint64_t index) {
     return b3_world_error(w) ? -1 : 0;
 }
 
+/* Bounce (parity coverage of restitution and rolling resistance, which the
+ * benchmark scenes leave at 0): ground + 4 spheres (r U[0.2, 0.45]) and 4
+ * boxes (half U[0.15, 0.34], random orientation) on a 2 x 2 x 2 lattice of
+ * 1.2 m cells, thrown down with spin; per shape restitution U[0.3, 0.9],
+ * rolling resistance U[0.02, 0.2], friction U[0.2, 1]. */
+static inline int b3s_build_bounce(B3World* w, uint64_t seed, uint64_t index) {
+    b3_world_init(w);
+    w->gravity = b3_v(0.0f, -9.81f, 0.0f);
+    b3s_ground(w);
+    for (int i = 0; i < 8; i++) {
+        int is_box = (i & 1) != 0;
+        uint64_t base = 200u + 32u * (uint64_t)i;
+        B3BodyDef bd = b3_default_body();
+        bd.type = B3_DYNAMIC;
+        bd.position = b3_v((i & 2) ? 0.6f : -0.6f, 1.2f + 1.2f * (float)(i >> 2), (i & 4) ? 0.6f : -0.6f);
+        bd.lin_vel = b3_v(b3s_uniform(seed, index, 0, base + 0, -1.0f, 1.0f),
+            b3s_uniform(seed, index, 0, base + 1, -4.0f, 0.0f), b3s_uniform(seed, index, 0, base + 2, -1.0f, 1.0f));
+        bd.ang_vel = b3_v(b3s_uniform(seed, index, 0, base + 3, -6.0f, 6.0f),
+            b3s_uniform(seed, index, 0, base + 4, -6.0f, 6.0f), b3s_uniform(seed, index, 0, base + 5, -6.0f, 6.0f));
+        if (is_box) {
+            B3Vec3 axis = b3_v(b3s_uniform(seed, index, 0, base + 6, -1.0f, 1.0f),
+                b3s_uniform(seed, index, 0, base + 7, -1.0f, 1.0f),
+                b3s_uniform(seed, index, 0, base + 8, -1.0f, 1.0f));
+            bd.rotation = b3_q_axis_angle(axis, b3s_uniform(seed, index, 0, base + 9, 0.0f, B3_PI));
+        }
+        int b = b3_create_body(w, &bd);
+        B3ShapeDef sd = b3_default_shape();
+        sd.density = b3s_uniform(seed, index, 0, base + 10, 500.0f, 2000.0f);
+        sd.friction = b3s_uniform(seed, index, 0, base + 11, 0.2f, 1.0f);
+        sd.restitution = b3s_uniform(seed, index, 0, base + 12, 0.3f, 0.9f);
+        sd.rolling = b3s_uniform(seed, index, 0, base + 13, 0.02f, 0.2f);
+        if (is_box) {
+            B3Vec3 half = b3_v(b3s_uniform(seed, index, 0, base + 14, 0.15f, 0.34f),
+                b3s_uniform(seed, index, 0, base + 15, 0.15f, 0.34f),
+                b3s_uniform(seed, index, 0, base + 16, 0.15f, 0.34f));
+            b3_create_box(w, b, half, &sd);
+        } else {
+            b3_create_sphere(w, b, b3_v(0.0f, 0.0f, 0.0f), b3s_uniform(seed, index, 0, base + 17, 0.2f, 0.45f), &sd);
+        }
+        b3_finalize_mass(w, b);
+    }
+    return b3_world_error(w) ? -1 : 0;
+}
+
 static inline int b3s_build(B3World* w, int kind, uint64_t seed, uint64_t index) {
     switch (kind) {
     case B3S_HOVER: return b3s_build_hover(w, seed, index);
     case B3S_STACK: return b3s_build_stack(w, seed, index);
     case B3S_CHAIN: return b3s_build_chain(w, seed, index);
     case B3S_PILE: return b3s_build_pile(w, seed, index);
+    case B3S_BOUNCE: return b3s_build_bounce(w, seed, index);
     default: return -1;
     }
 }

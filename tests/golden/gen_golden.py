@@ -29,7 +29,7 @@ from puffysics_b200 import layout  # noqa: E402
 from puffysics_b200.configs import CONFIGS  # noqa: E402
 
 SEED = 20261201
-WORLDS = {"hover": 8, "stack": 8, "chain": 8, "pile": 4}
+WORLDS = {"hover": 8, "stack": 8, "chain": 8, "pile": 4, "bounce": 8}
 
 
 def rollout(name):

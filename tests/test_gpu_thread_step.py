@@ -59,7 +59,7 @@ def built():
     build.build()
 
 
-@pytest.mark.parametrize("name", ["hover", "stack", "chain", "pile", "default"])
+@pytest.mark.parametrize("name", ["hover", "stack", "chain", "pile", "default", "bounce"])
 def test_thread_step_matches_reference(name, oracle_kind, built):
     cfg = CONFIGS[name]
     L = engine.thread_lib(name)
