@@ -17,12 +17,45 @@
 #if defined(__CUDACC__)
 #include "../puffysics_b200/csrc/b3x_world_step.cuh"
 
+/* The reference's step-mode switches of the including translation unit. */
+#if defined(B3_INTERLEAVE_CONTACTS)
+#define B3X_MODE_INTERLEAVE b3x::kStepInterleaveContacts
+#else
+#define B3X_MODE_INTERLEAVE 0
+#endif
+#if defined(B3_SKIP_RESTITUTION)
+#define B3X_MODE_SKIP_RESTITUTION b3x::kStepSkipRestitution
+#else
+#define B3X_MODE_SKIP_RESTITUTION 0
+#endif
+
 __device__ inline void b3_step(B3World* w, float dt, int substeps) {
-    b3x::one::step_world(w, dt, substeps, B3_JOINT_ITERS, B3_RELAX_ITERS);
+    b3x::one::step_world(w, dt, substeps, B3_JOINT_ITERS, B3_RELAX_ITERS,
+                         B3X_MODE_INTERLEAVE | B3X_MODE_SKIP_RESTITUTION);
 }
 
 static __global__ void b3_step_kernel(B3World* worlds, int n, float dt, int substeps) {
     int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) b3_step(&worlds[i], dt, substeps);
 }
+
+#if B3_HAS_USER_FORCES
+/* With a per-substep force hook the batch step runs this translation unit's
+ * per-thread b3_step, which runs the hook (reference b3_batch.cuh:63-89
+ * semantics: same validation, no-ops, mask, stream; no allocation). */
+static __global__ void b3x_user_force_batch_kernel(B3Batch batch, float dt, int substeps,
+        const unsigned char* active) {
+    size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < (size_t)batch.count && (!active || active[i])) b3_step(b3_batch_world(batch, (int)i), dt, substeps);
+}
+
+B3_INL cudaError_t b3_batch_step_gpu(B3Batch batch, float dt, int substeps, const unsigned char* active,
+        cudaStream_t stream) {
+    if (!b3_batch_valid(batch) || !isfinite(dt) || dt < 0 || substeps < 1) return cudaErrorInvalidValue;
+    if (!batch.count || dt == 0) return cudaSuccess;
+    b3x_user_force_batch_kernel<<<((unsigned)batch.count + 31u) / 32u, 32, 0, stream>>>(batch, dt, substeps,
+                                                                                         active);
+    return cudaGetLastError();
+}
+#endif
 #endif

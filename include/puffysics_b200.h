@@ -86,6 +86,17 @@
 #ifndef B3_ART_CONTACTS
 #define B3_ART_CONTACTS 0
 #endif
+/* Optional per-substep force hook (reference 01_config.inl:186-198): code the
+ * including translation unit runs on a B3World* w and substep h before each
+ * velocity integration; its force / torque additions last one substep.  Run
+ * by the device b3_step of puffysics.cuh; with a hook, b3_batch_step_gpu steps
+ * with that per-thread b3_step (a precompiled library cannot run the hook). */
+#ifndef B3_USER_FORCES
+#define B3_USER_FORCES(w, h) ((void)0)
+#define B3_HAS_USER_FORCES 0
+#else
+#define B3_HAS_USER_FORCES 1
+#endif
 #define B3_CONNECT_WORDS ((B3_MAX_BODIES + 63) / 64)
 
 /* 16 bits per capacity, bodies in the low word (reference 01_config.inl:70-74). */
@@ -816,6 +827,19 @@ B3_HD B3_INL B3World* b3_batch_world(B3Batch batch, int index) {
 B3X_API int b3x_batch_step_gpu(B3Batch batch, float dt, int substeps, const unsigned char* active,
     void* stream, unsigned long long config_signature, int joint_iters, int relax_iters);
 
+/* The same step in the reference's alternative step modes, selected there by
+ * compile-time macros of the translation unit (reference 01_config.inl:50-52):
+ *   B3X_STEP_INTERLEAVE_CONTACTS  (B3_INTERLEAVE_CONTACTS) contacts are swept
+ *       at the start of every joint iteration, bias and relax phases, instead
+ *       of once per phase (07_packed.inl:61-65, 09_step.inl:169-177);
+ *   B3X_STEP_SKIP_RESTITUTION     (B3_SKIP_RESTITUTION) no restitution pass
+ *       (09_step.inl:178-180).
+ * Unknown flag bits -> 1 (invalid), nothing launched. */
+#define B3X_STEP_INTERLEAVE_CONTACTS 1
+#define B3X_STEP_SKIP_RESTITUTION 2
+B3X_API int b3x_batch_step_gpu_flags(B3Batch batch, float dt, int substeps, const unsigned char* active,
+    void* stream, unsigned long long config_signature, int joint_iters, int relax_iters, int flags);
+
 /* Same step with a caller-owned device workspace of at least
  * b3x_workspace_bytes(...) bytes (256-byte aligned): never allocates.
  * Work queued on different streams must use different workspaces. */
@@ -897,12 +921,26 @@ B3X_API const char* b3x_version(void);
 
 /* Inline shims with the exact reference signatures (reference
  * b3_batch.cuh:81-99), available wherever the CUDA runtime types are. */
-#if defined(__CUDACC__) || defined(CUDART_VERSION)
+#if (defined(__CUDACC__) || defined(CUDART_VERSION)) && !B3_HAS_USER_FORCES
 B3_INL cudaError_t b3_batch_step_gpu(B3Batch batch, float dt, int substeps,
         const unsigned char* active, cudaStream_t stream) {
+#if defined(B3_INTERLEAVE_CONTACTS) || defined(B3_SKIP_RESTITUTION)
+    int flags = 0;
+#if defined(B3_INTERLEAVE_CONTACTS)
+    flags |= B3X_STEP_INTERLEAVE_CONTACTS;
+#endif
+#if defined(B3_SKIP_RESTITUTION)
+    flags |= B3X_STEP_SKIP_RESTITUTION;
+#endif
+    return (cudaError_t)b3x_batch_step_gpu_flags(batch, dt, substeps, active, (void*)stream,
+        B3_CONFIG_SIGNATURE, B3_JOINT_ITERS, B3_RELAX_ITERS, flags);
+#else
     return (cudaError_t)b3x_batch_step_gpu(batch, dt, substeps, active, (void*)stream,
         B3_CONFIG_SIGNATURE, B3_JOINT_ITERS, B3_RELAX_ITERS);
+#endif
 }
+#endif
+#if defined(__CUDACC__) || defined(CUDART_VERSION)
 B3_INL cudaError_t b3_batch_restore_gpu(B3Batch batch, const B3World* initial,
         const unsigned char* reset, cudaStream_t stream) {
     return (cudaError_t)b3x_batch_restore_gpu(batch, (const void*)initial, reset, (void*)stream,

@@ -1052,9 +1052,15 @@ static void solve_revolute(B3Joint* j, B3Body* ba, B3Body* bb, float h, float in
     if (bb->flags & B3_FLAG_DYNAMIC) { bb->lin_vel = vb; bb->ang_vel = wb; }
 }
 
-/* 07_packed.inl:48-81 */
+static void solve_contacts(B3World* w, float inv_h, int use_bias);
+
+/* 07_packed.inl:48-81; with B3_INTERLEAVE_CONTACTS a contact sweep opens
+ * every iteration (07_packed.inl:63-65) */
 static void solve_joints(B3World* w, float h, float inv_h, int use_bias, int iters) {
     for (int it = 0; it < iters; it++) {
+#ifdef B3_INTERLEAVE_CONTACTS
+        solve_contacts(w, inv_h, use_bias);
+#endif
         for (int i = 0; i < w->joint_count; i++) {
             B3Joint* j = &w->joints[i];
             B3Body* ba = &w->bodies[j->body_a];
@@ -1068,6 +1074,15 @@ static void solve_joints(B3World* w, float h, float inv_h, int use_bias, int ite
 /* -------------------------------------------------------------- step --- */
 /* 09_step.inl:5-18, 41-53 */
 static void integrate_velocities(B3World* w, float h) {
+#ifdef B3_USER_FORCES
+    /* the per-substep hook's contributions last one substep (09_step.inl:20-53) */
+    V saved_f[B3_MAX_BODIES], saved_t[B3_MAX_BODIES];
+    for (int i = 0; i < w->body_count; i++) {
+        saved_f[i] = w->bodies[i].force;
+        saved_t[i] = w->bodies[i].torque;
+    }
+    B3_USER_FORCES(w, h);
+#endif
     for (int i = 0; i < w->body_count; i++) {
         B3Body* b = &w->bodies[i];
         if (b->type != B3_DYNAMIC) continue;
@@ -1079,6 +1094,12 @@ static void integrate_velocities(B3World* w, float h) {
         V dw = pscale(pmv(b->inv_i_world, b->torque), h);
         b->ang_vel = pmadd(dw, ad, b->ang_vel);
     }
+#ifdef B3_USER_FORCES
+    for (int i = 0; i < w->body_count; i++) {
+        w->bodies[i].force = saved_f[i];
+        w->bodies[i].torque = saved_t[i];
+    }
+#endif
 }
 
 /* 09_step.inl:55-107 */
@@ -1122,6 +1143,14 @@ static void finalize(B3World* w) {
     }
 }
 
+/* 08_contacts.inl:424-437 */
+static void solve_contacts(B3World* w, float inv_h, int use_bias) {
+    for (int i = 0; i < w->contact_count; i++) {
+        B3Contact* c = &w->contacts[i];
+        solve_contact(c, &w->bodies[c->body_a], &w->bodies[c->body_b], inv_h, w->contact_speed, use_bias);
+    }
+}
+
 /* b3_step_indep (09_step.inl:148-258) with the default substep (167-181). */
 void b3port_step(B3World* w, float dt, int substeps, int joint_iters, int relax_iters) {
     if (dt <= 0.0f) return;
@@ -1145,18 +1174,18 @@ void b3port_step(B3World* w, float dt, int substeps, int joint_iters, int relax_
     warm_joints(w);
     for (int s = 0; s < subs; s++) {
         integrate_velocities(w, h);
-        for (int i = 0; i < w->contact_count; i++) {
-            B3Contact* c = &w->contacts[i];
-            solve_contact(c, &w->bodies[c->body_a], &w->bodies[c->body_b], inv_h, w->contact_speed, 1);
-        }
+#ifndef B3_INTERLEAVE_CONTACTS
+        solve_contacts(w, inv_h, 1);
+#endif
         solve_joints(w, h, inv_h, 1, joint_iters);
         integrate_positions(w, h, inv_dt, w->max_linear_speed);
-        for (int i = 0; i < w->contact_count; i++) {
-            B3Contact* c = &w->contacts[i];
-            solve_contact(c, &w->bodies[c->body_a], &w->bodies[c->body_b], inv_h, w->contact_speed, 0);
-        }
+#ifndef B3_INTERLEAVE_CONTACTS
+        solve_contacts(w, inv_h, 0);
+#endif
         solve_joints(w, h, inv_h, 0, relax_iters);
+#ifndef B3_SKIP_RESTITUTION
         restitution(w, w->restitution_threshold);
+#endif
     }
     finalize(w);
 }

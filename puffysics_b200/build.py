@@ -31,17 +31,26 @@ THREAD_HEADERS = [os.path.join(ROOT, "include", "puffysics.cuh"),
 HOVER_SRC = os.path.join(PKG, "csrc", "b3x_hover_env.cu")
 HOVER_LIB = os.path.join(LIB_DIR, "libb3hover.so")
 HOVER_HEADERS = THREAD_HEADERS + [os.path.join(ROOT, "include", "b3x_staged.cuh")]
+THREAD_HEADERS = THREAD_HEADERS + [os.path.join(PKG, "scenes", "b3_test_forces.h")]
 # capacity configurations the host scene builders are compiled for:
 # name -> (bodies, shapes, contacts, joints)
 SCENE_CONFIGS = {"hover": (2, 2, 4, 1), "stack": (9, 9, 32, 1), "chain": (12, 12, 32, 10),
                  "pile": (37, 37, 128, 1), "hovertask": (2, 2, 4, 2), "default": (80, 128, 128, 32),
-                 "stacksmall": (9, 9, 4, 1), "bounce": (9, 9, 32, 1)}
+                 "stacksmall": (9, 9, 4, 1), "bounce": (9, 9, 32, 1), "stackil": (9, 9, 32, 1),
+                 "chainil": (12, 12, 32, 10), "bouncenr": (9, 9, 32, 1), "bounceilnr": (9, 9, 32, 1),
+                 "hoveruf": (2, 2, 4, 1)}
 # per-thread step launchers (include/puffysics.cuh's device b3_step): name ->
 # (bodies, shapes, contacts, joints, B3_JOINT_ITERS), the capacities of the
 # benchmark configurations and of the reference's defaults
 THREAD_CONFIGS = {"hover": (2, 2, 4, 1, 8), "stack": (9, 9, 32, 1, 8), "chain": (12, 12, 32, 10, 8),
                   "pile": (37, 37, 128, 1, 8), "hovertask": (2, 2, 4, 2, 2), "default": (80, 128, 128, 32, 2),
-                  "bounce": (9, 9, 32, 1, 8)}
+                  "bounce": (9, 9, 32, 1, 8), "stackil": (9, 9, 32, 1, 8), "chainil": (12, 12, 32, 10, 8),
+                  "bouncenr": (9, 9, 32, 1, 8), "bounceilnr": (9, 9, 32, 1, 8), "hoveruf": (2, 2, 4, 1, 8)}
+# the reference's mode macros of the per-thread configurations
+THREAD_MODES = {"stackil": ["-DB3_INTERLEAVE_CONTACTS"], "chainil": ["-DB3_INTERLEAVE_CONTACTS"],
+                "bouncenr": ["-DB3_SKIP_RESTITUTION"],
+                "bounceilnr": ["-DB3_INTERLEAVE_CONTACTS", "-DB3_SKIP_RESTITUTION"],
+                "hoveruf": ["-include", os.path.join(PKG, "scenes", "b3_test_forces.h")]}
 CC = os.environ.get("CC", "gcc")
 
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc" if os.path.exists("/usr/local/cuda/bin/nvcc") else "nvcc")
@@ -64,7 +73,7 @@ def thread_lib(name):
 def thread_cmd(name):
     b, s, c, j, it = THREAD_CONFIGS[name]
     caps = ["-DB3_MAX_BODIES=%d" % b, "-DB3_MAX_SHAPES=%d" % s, "-DB3_MAX_CONTACTS=%d" % c,
-            "-DB3_MAX_JOINTS=%d" % j, "-DB3_JOINT_ITERS=%d" % it]
+            "-DB3_MAX_JOINTS=%d" % j, "-DB3_JOINT_ITERS=%d" % it] + THREAD_MODES.get(name, [])
     return ([NVCC] + ARCH + ["-lineinfo", "-O3", "-std=c++17"] + PARITY
             + ["-Xcompiler", "-fPIC,-fvisibility=hidden", "-shared", "-cudart", "static",
                "-I" + os.path.join(ROOT, "include"), "-I" + os.path.join(PKG, "csrc")]

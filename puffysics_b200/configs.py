@@ -8,6 +8,7 @@ from dataclasses import dataclass
 
 SCENE_HOVER, SCENE_STACK, SCENE_CHAIN, SCENE_PILE, SCENE_BOUNCE = 1, 2, 3, 4, 5
 ACT_NONE, ACT_FORCE, ACT_TORQUE, ACT_LINEAR_IMPULSE, ACT_JOINT_TARGET = -1, 0, 1, 2, 3
+STEP_INTERLEAVE_CONTACTS, STEP_SKIP_RESTITUTION = 1, 2
 
 
 @dataclass(frozen=True)
@@ -23,6 +24,7 @@ class Config:
     steps: int = 0       # rollout length the configuration is quoted at (0 = open-ended)
     reset_fraction: float = 0.0
     description: str = ""
+    flags: int = 0       # STEP_INTERLEAVE_CONTACTS | STEP_SKIP_RESTITUTION (the reference's mode macros)
 
     @property
     def signature(self):
@@ -52,6 +54,20 @@ CONFIGS = {
                       description="pile scene at the reference's default capacities"),
     "bounce": Config("bounce", SCENE_BOUNCE, (9, 9, 32, 1), 8, 8, 1.0 / 60.0, 4, 1024,
                      description="spheres and boxes with restitution and rolling resistance (parity coverage)"),
+    # the reference's alternative step modes (B3_INTERLEAVE_CONTACTS,
+    # B3_SKIP_RESTITUTION) on the same scenes
+    "stackil": Config("stackil", SCENE_STACK, (9, 9, 32, 1), 8, 8, 1.0 / 60.0, 4, 1024,
+                      flags=STEP_INTERLEAVE_CONTACTS, description="stack, contacts interleaved with 8 iterations"),
+    "chainil": Config("chainil", SCENE_CHAIN, (12, 12, 32, 10), 8, 8, 1.0 / 120.0, 2, 1024,
+                      flags=STEP_INTERLEAVE_CONTACTS, description="chain, contacts interleaved with the joints"),
+    "bouncenr": Config("bouncenr", SCENE_BOUNCE, (9, 9, 32, 1), 8, 8, 1.0 / 60.0, 4, 1024,
+                       flags=STEP_SKIP_RESTITUTION, description="bounce without the restitution pass"),
+    "bounceilnr": Config("bounceilnr", SCENE_BOUNCE, (9, 9, 32, 1), 8, 8, 1.0 / 60.0, 4, 1024,
+                         flags=STEP_INTERLEAVE_CONTACTS | STEP_SKIP_RESTITUTION,
+                         description="bounce, both modes"),
+    "hoveruf": Config("hoveruf", SCENE_HOVER, (2, 2, 4, 1), 8, 8, 1.0 / 60.0, 4, 1024,
+                      description="hover with the per-substep force hook of scenes/b3_test_forces.h "
+                                  "(B3_USER_FORCES; per-thread step only)"),
     "stacksmall": Config("stacksmall", SCENE_STACK, (9, 9, 4, 1), 2, 2, 1.0 / 60.0, 4, 1024,
                          description="stack scene with 4 contact slots (overflow path)"),
     "scaleout": Config("stack", SCENE_STACK, (9, 9, 32, 1), 8, 8, 1.0 / 60.0, 4, 1048576,

@@ -191,6 +191,7 @@ struct Args {
     const unsigned char* active;
     float dt;
     int substeps, joint_iters, relax_iters;
+    int flags;     // kStepInterleaveContacts | kStepSkipRestitution
     Layout L;
     Space SP;
     float* ws;     // workspace slot of the launch's first tile

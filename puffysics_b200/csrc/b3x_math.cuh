@@ -20,6 +20,12 @@
 
 namespace b3x {
 
+// Step modes of the reference's compile-time switches (01_config.inl:50-52,
+// 07_packed.inl:63-65, 09_step.inl:169-181): contacts swept inside every
+// joint iteration instead of once per phase (B3_INTERLEAVE_CONTACTS), and no
+// restitution pass (B3_SKIP_RESTITUTION).
+enum : int { kStepInterleaveContacts = 1, kStepSkipRestitution = 2 };
+
 // Bit casts between 32-bit words (ints and flags share the float columns).
 B3X_HDI int b3x_f2i(float f) {
 #if defined(__CUDA_ARCH__)

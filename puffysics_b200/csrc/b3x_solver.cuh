@@ -198,10 +198,12 @@ B3X_HDI void warm_contact(float* __restrict__ bc, const float* __restrict__ bk, 
     }
 }
 
-// Sweeps over the contacts: the bias sweep of the first substep, the bias
-// sweeps of later substeps (separations from the preceding relax sweep) and
-// the relax sweeps (which store the separations).
-enum : int { kBiasFresh = 0, kBiasCached = 1, kRelax = 2 };
+// Sweeps over the contacts.  Positions change only between a substep's bias
+// and relax sweeps, so a point's separation is computed by the first sweep
+// after a position change (kBiasFresh in the first substep, kRelax) and
+// stored; the sweeps before the next change read it (kBiasCached, and
+// kRelaxCached for the further relax sweeps of the interleaved mode).
+enum : int { kBiasFresh = 0, kBiasCached = 1, kRelax = 2, kRelaxCached = 3 };
 
 // One contact of a sweep (08_contacts.inl:315-413, rolling 07_packed.inl:24-45).
 // Reads contact k from src (shared-memory copy or workspace), writes the
@@ -209,7 +211,8 @@ enum : int { kBiasFresh = 0, kBiasCached = 1, kRelax = 2 };
 template <int kPass>
 B3X_HDI void solve_contact(float* __restrict__ bc, const float* __restrict__ bp, const float* __restrict__ bk,
         const float* __restrict__ src, float* __restrict__ dst, float inv_h, float speed, B3Soft cs, B3Soft ss) {
-    constexpr bool use_bias = kPass != kRelax;
+    constexpr bool use_bias = kPass == kBiasFresh || kPass == kBiasCached;
+    constexpr bool cached = kPass == kBiasCached || kPass == kRelaxCached;
     int ba = ldi(src, WBA), bb = ldi(src, WBB);
     int cnt = ldi(src, WCNT);
     B3Soft soft = ldi(src, WSTAT) ? ss : cs;
@@ -219,7 +222,7 @@ B3X_HDI void solve_contact(float* __restrict__ bc, const float* __restrict__ bp,
     B3Vec3 vb = ld3(bc, BI(bb, BV)), wb = ld3(bc, BI(bb, BW));
     B3Quat dqa, dqb;
     B3Vec3 dp;
-    if (kPass != kBiasCached) {
+    if (!cached) {
         dqa = ldq(bp, BP(ba, BDQ));
         dqb = ldq(bp, BP(bb, BDQ));
         dp = b3_sub(ld3(bp, BP(bb, BDP)), ld3(bp, BP(ba, BDP)));
@@ -230,12 +233,12 @@ B3X_HDI void solve_contact(float* __restrict__ bc, const float* __restrict__ bp,
         if (p >= cnt) break;
         B3Vec3 ra = ld3(src, PW(p, QRA)), rb = ld3(src, PW(p, QRB));
         float sep;
-        if (kPass == kBiasCached) {
+        if (cached) {
             sep = COL(src, WSEP + p);
         } else {
             B3Vec3 ds = b3_add(dp, b3_sub(b3_rotate(dqb, rb), b3_rotate(dqa, ra)));
             sep = b3_dot(ds, n) + COL(src, PW(p, QBSEP));
-            if (kPass == kRelax) COL(dst, WSEP + p) = sep;
+            COL(dst, WSEP + p) = sep;
         }
         float vbias = 0.0f, mscale = 1.0f, iscale = 0.0f;
         if (sep > 0.0f) {
@@ -653,12 +656,22 @@ B3X_HD bool solve_world(const Args& a, float* slot, int lane, float* __restrict_
         }))
         return false;
 
-    auto contact_pass = [&](auto pass) {
+    auto contact_pass_of = [&](auto pass) {
         constexpr int kPass = decltype(pass)::value;
         return stream_items(P, cc, kCI, kContactStream, wn, [&](int k, const float* src) {
             if (k < n) solve_contact<kPass>(bc, bp, bk, src, item(cc, k, kCI), inv_h, contact_speed, cs, ss);
         });
     };
+    // one call site per sweep kind
+    auto contact_pass = [&](int kind) {
+        switch (kind) {
+        case kBiasFresh: return contact_pass_of(std::integral_constant<int, kBiasFresh>{});
+        case kBiasCached: return contact_pass_of(std::integral_constant<int, kBiasCached>{});
+        case kRelax: return contact_pass_of(std::integral_constant<int, kRelax>{});
+        default: return contact_pass_of(std::integral_constant<int, kRelaxCached>{});
+        }
+    };
+    const bool interleave = (a.flags & kStepInterleaveContacts) != 0;
     auto joint_pass = [&](int use_bias) {
         return stream_items(P, jc, NJF, kJointStream, wj, [&](int q, const float* src) {
             if (q < nj && ldi(src, JOK)) solve_joint(bc, bp, bk, src, item(jc, q, NJF), h, inv_h, use_bias);
@@ -680,12 +693,15 @@ B3X_HD bool solve_world(const Args& a, float* slot, int lane, float* __restrict_
             st3(bc, BI(k, BV), b3_madd(ld3(kk, KDV), COL(kk, KLD), ld3(bc, BI(k, BV))));
             st3(bc, BI(k, BW), b3_madd(ld3(kk, KDW), COL(kk, KAD), ld3(bc, BI(k, BW))));
         }
-        const bool first = s == 0;
-        if (first ? !contact_pass(std::integral_constant<int, kBiasFresh>{})
-                  : !contact_pass(std::integral_constant<int, kBiasCached>{}))
-            return false;
-        for (int it = 0; it < a.joint_iters; it++)
-            if (!joint_pass(1)) return false;
+        // bias phase (09_step.inl:170-172): one contact sweep, then the joint
+        // iterations; interleaved, a contact sweep opens every joint iteration
+        // (07_packed.inl:61-65)
+        const int bias_rounds = interleave ? a.joint_iters : 1;
+        for (int it = 0; it < bias_rounds; it++) {
+            if (!contact_pass(it == 0 && s == 0 ? kBiasFresh : kBiasCached)) return false;
+            for (int q = 0; q < (interleave ? 1 : a.joint_iters); q++)
+                if (!joint_pass(1)) return false;
+        }
         // integrate positions (09_step.inl:55-107)
         for (int k = 0; k < nb; k++) {
             if (ldi(bk, BK(k, BTYPE)) == B3_STATIC) continue;
@@ -706,12 +722,17 @@ B3X_HD bool solve_world(const Args& a, float* slot, int lane, float* __restrict_
             st3(bp, BP(k, BDP), b3_madd(ld3(bp, BP(k, BDP)), h, v));
             stq(bp, BP(k, BDQ), q_integrate(ldq(bp, BP(k, BDQ)), b3_mul(av, h)));
         }
-        if (!contact_pass(std::integral_constant<int, kRelax>{})) return false;
-        for (int it = 0; it < a.relax_iters; it++)
-            if (!joint_pass(0)) return false;
+        // relax phase (09_step.inl:173-177), the same way
+        const int relax_rounds = interleave ? a.relax_iters : 1;
+        for (int it = 0; it < relax_rounds; it++) {
+            if (!contact_pass(it == 0 ? kRelax : kRelaxCached)) return false;
+            for (int q = 0; q < (interleave ? 1 : a.relax_iters); q++)
+                if (!joint_pass(0)) return false;
+        }
         // restitution (08_contacts.inl:439-480): skipped when no contact of
-        // the warp's worlds has a nonzero coefficient
-        if (any_rest) {
+        // the warp's worlds has a nonzero coefficient, or in the
+        // B3_SKIP_RESTITUTION mode (09_step.inl:178-180)
+        if (any_rest && !(a.flags & kStepSkipRestitution)) {
             if (!stream_items(P, cc, kCI, kContactStream, wn, [&](int k, const float* src) {
                     if (k < n) restitute_contact(bc, bk, src, item(cc, k, kCI), restitution_threshold);
                 }))

@@ -203,7 +203,7 @@ __global__ void __launch_bounds__(kLanes) small_step_kernel(Args a, unsigned str
         v.cap_s = a.L.S;
         v.cap_c = a.L.C;
         v.cap_j = a.L.J;
-        one::step_view(v, a.dt, a.substeps, a.joint_iters, a.relax_iters);
+        one::step_view(v, a.dt, a.substeps, a.joint_iters, a.relax_iters, a.flags);
     }
     __syncwarp();
     for (int l = 0; l < kSmallWorlds; l++) {
@@ -371,7 +371,7 @@ static bool aligned8(const B3Batch& b) {
 
 // The step over chunks of `chunk` tiles, one step_kernel launch per chunk.
 static cudaError_t launch_step(const B3Batch& batch, float dt, int substeps, const unsigned char* active,
-        cudaStream_t stream, const Layout& L, int ji, int ri, const Plan& p, void* ws, int chunk) {
+        cudaStream_t stream, const Layout& L, int ji, int ri, int flags, const Plan& p, void* ws, int chunk) {
     Args a;
     a.data = (unsigned char*)batch.data;
     a.stride = batch.stride;
@@ -382,6 +382,7 @@ static cudaError_t launch_step(const B3Batch& batch, float dt, int substeps, con
     a.substeps = substeps;
     a.joint_iters = ji;
     a.relax_iters = ri;
+    a.flags = flags;
     a.L = L;
     a.SP = p.SP;
     a.ws = (float*)ws;
@@ -431,10 +432,11 @@ B3X_API int b3x_step_launches(unsigned long long sig, int count, int device) {
 }
 
 static int step_common(B3Batch batch, float dt, int substeps, const unsigned char* active, void* stream,
-        unsigned long long sig, int ji, int ri, void* ws, size_t ws_bytes, bool own_ws) {
+        unsigned long long sig, int ji, int ri, void* ws, size_t ws_bytes, bool own_ws, int flags = 0) {
     Layout L;
     if (!layout_from_signature(sig, &L)) return cudaErrorInvalidValue;
-    if (!batch_ok(batch, L.size) || !std::isfinite(dt) || dt < 0 || substeps < 1 || ji < 1 || ri < 1)
+    if (!batch_ok(batch, L.size) || !std::isfinite(dt) || dt < 0 || substeps < 1 || ji < 1 || ri < 1
+            || (flags & ~(kStepInterleaveContacts | kStepSkipRestitution)) != 0)
         return cudaErrorInvalidValue;
     if (batch.count == 0 || dt == 0) return cudaSuccess;
     if (!aligned8(batch)) return cudaErrorInvalidValue;
@@ -456,6 +458,7 @@ static int step_common(B3Batch batch, float dt, int substeps, const unsigned cha
         a.substeps = substeps;
         a.joint_iters = ji;
         a.relax_iters = ri;
+        a.flags = flags;
         a.L = L;
         a.SP = p.SP;
         a.ws = nullptr;
@@ -484,12 +487,17 @@ static int step_common(B3Batch batch, float dt, int substeps, const unsigned cha
     long long slots = (long long)(ws_bytes / p.tile_bytes);
     if (slots < 1) return cudaErrorInvalidValue;
     int chunk = (int)(slots < p.chunk_tiles ? slots : p.chunk_tiles);
-    return launch_step(batch, dt, substeps, active, (cudaStream_t)stream, L, ji, ri, p, ws, chunk);
+    return launch_step(batch, dt, substeps, active, (cudaStream_t)stream, L, ji, ri, flags, p, ws, chunk);
 }
 
 B3X_API int b3x_batch_step_gpu(B3Batch batch, float dt, int substeps, const unsigned char* active, void* stream,
         unsigned long long sig, int ji, int ri) {
     return step_common(batch, dt, substeps, active, stream, sig, ji, ri, nullptr, 0, true);
+}
+
+B3X_API int b3x_batch_step_gpu_flags(B3Batch batch, float dt, int substeps, const unsigned char* active,
+        void* stream, unsigned long long sig, int ji, int ri, int flags) {
+    return step_common(batch, dt, substeps, active, stream, sig, ji, ri, nullptr, 0, true, flags);
 }
 
 B3X_API int b3x_batch_step_gpu_ws(B3Batch batch, float dt, int substeps, const unsigned char* active, void* stream,

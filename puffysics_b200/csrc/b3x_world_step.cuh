@@ -160,6 +160,7 @@ struct Stepper {
     float h, inv_h, inv_dt;
     B3Soft cs, ss;
     int joint_iters, relax_iters;
+    int flags;     // kStepInterleaveContacts | kStepSkipRestitution
 
     __device__ bool body_ok(int b) const { return b >= 0 && b < nb; }
 
@@ -720,14 +721,16 @@ struct Stepper {
     // Joint sweeps in joint index order (07_packed.inl:48-81).
     __device__ bool joint_ok(const B3Joint& j) const { return body_ok(j.body_a) && body_ok(j.body_b); }
 
-    __device__ void solve_joints(bool use_bias, int iters) {
-        for (int it = 0; it < iters; it++)
+    __device__ void solve_joints(bool use_bias, int iters, bool interleave) {
+        for (int it = 0; it < iters; it++) {
+            if (interleave) solve_contacts(use_bias);
             for (int i = 0; i < nj; i++) {
                 B3Joint& j = v.joints[i];
                 if (!joint_ok(j)) continue;
                 if (j.type == B3_JOINT_WELD) solve_weld(j, use_bias);
                 else solve_revolute(j, use_bias);
             }
+        }
     }
 
     __device__ void solve_contacts(bool use_bias) {
@@ -736,6 +739,16 @@ struct Stepper {
 
     // ---- integration (09_step.inl:5-130) ---------------------------------------
     __device__ void integrate_velocities() {
+#if B3_HAS_USER_FORCES
+        // the per-substep force hook of the including translation unit: its
+        // contributions act for this substep only (09_step.inl:20-53)
+        B3Vec3 saved_f[V::kB], saved_t[V::kB];
+        for (int i = 0; i < nb; i++) {
+            saved_f[i] = v.bodies[i].force;
+            saved_t[i] = v.bodies[i].torque;
+        }
+        B3_USER_FORCES(v.h, h);
+#endif
         for (int i = 0; i < nb; i++) {
             B3Body& b = v.bodies[i];
             if (b.type != B3_DYNAMIC) continue;
@@ -746,6 +759,12 @@ struct Stepper {
             b.lin_vel = b3_madd(dv, ld, b.lin_vel);
             b.ang_vel = b3_madd(b3_mul(b3_mv(b.inv_i_world, b.torque), h), ad, b.ang_vel);
         }
+#if B3_HAS_USER_FORCES
+        for (int i = 0; i < nb; i++) {
+            v.bodies[i].force = saved_f[i];
+            v.bodies[i].torque = saved_t[i];
+        }
+#endif
     }
 
     __device__ void integrate_positions() {
@@ -797,14 +816,17 @@ struct Stepper {
         for (int i = 0; i < v.h->contact_count; i++) warm_contact(v.contacts[i]);
         for (int i = 0; i < nj; i++)
             if (joint_ok(v.joints[i])) warm_joint(v.joints[i]);
+        const bool interleave = (flags & kStepInterleaveContacts) != 0;
         for (int s = 0; s < subs; s++) {
+            // 09_step.inl:167-181; interleaved, a contact sweep opens every
+            // joint iteration (07_packed.inl:61-65)
             integrate_velocities();
-            solve_contacts(true);
-            solve_joints(true, joint_iters);
+            if (!interleave) solve_contacts(true);
+            solve_joints(true, joint_iters, interleave);
             integrate_positions();
-            solve_contacts(false);
-            solve_joints(false, relax_iters);
-            restitution();
+            if (!interleave) solve_contacts(false);
+            solve_joints(false, relax_iters, interleave);
+            if (!(flags & kStepSkipRestitution)) restitution();
         }
         finalize();
     }
@@ -813,7 +835,8 @@ struct Stepper {
 // b3_step_indep (09_step.inl:183-258) of the world a view addresses, with
 // run-time solver iteration counts.
 template <class V>
-__device__ inline void step_view(const V& v, float dt, int substeps, int joint_iters, int relax_iters) {
+__device__ inline void step_view(const V& v, float dt, int substeps, int joint_iters, int relax_iters,
+                                 int flags = 0) {
     if (dt <= 0.0f) return;
     const int subs = substeps < 1 ? 1 : substeps;
     Stepper<V> st;
@@ -823,6 +846,7 @@ __device__ inline void step_view(const V& v, float dt, int substeps, int joint_i
     st.nj = clamp_count(v.h->joint_count, v.cap_j);
     st.joint_iters = joint_iters;
     st.relax_iters = relax_iters;
+    st.flags = flags;
     // b3_soft_step_params (09_step.inl:148-157)
     st.h = dt / (float)subs;
     st.inv_dt = 1.0f / dt;
@@ -834,8 +858,9 @@ __device__ inline void step_view(const V& v, float dt, int substeps, int joint_i
 }
 
 // b3_step_indep on a B3World of this translation unit's capacities.
-__device__ inline void step_world(B3World* w, float dt, int substeps, int joint_iters, int relax_iters) {
-    step_view(view_of(w), dt, substeps, joint_iters, relax_iters);
+__device__ inline void step_world(B3World* w, float dt, int substeps, int joint_iters, int relax_iters,
+                                  int flags = 0) {
+    step_view(view_of(w), dt, substeps, joint_iters, relax_iters, flags);
 }
 
 }  // namespace one

@@ -43,6 +43,9 @@ def lib():
         L.b3x_batch_step_gpu.argtypes = [B3Batch, ctypes.c_float, ctypes.c_int, u8p, vp, ctypes.c_ulonglong,
                                          ctypes.c_int, ctypes.c_int]
         L.b3x_batch_step_gpu.restype = ctypes.c_int
+        L.b3x_batch_step_gpu_flags.argtypes = [B3Batch, ctypes.c_float, ctypes.c_int, u8p, vp, ctypes.c_ulonglong,
+                                               ctypes.c_int, ctypes.c_int, ctypes.c_int]
+        L.b3x_batch_step_gpu_flags.restype = ctypes.c_int
         L.b3x_batch_step_gpu_ws.argtypes = [B3Batch, ctypes.c_float, ctypes.c_int, u8p, vp, ctypes.c_ulonglong,
                                             ctypes.c_int, ctypes.c_int, vp, ctypes.c_size_t]
         L.b3x_batch_step_gpu_ws.restype = ctypes.c_int
@@ -88,11 +91,17 @@ def make_batch(worlds, stride=None, offset=0, count=None):
 
 
 def batch_step_gpu(worlds, dt, substeps, active=None, stream=None, caps=None, joint_iters=2, relax_iters=None,
-                   stride=None, offset=0, count=None, workspace=None):
-    """Step the selected worlds once (b3_batch_step_gpu).  Returns a cudaError_t code."""
+                   stride=None, offset=0, count=None, workspace=None, flags=0):
+    """Step the selected worlds once (b3_batch_step_gpu; `flags` selects the
+    reference's alternative step modes, b3x_batch_step_gpu_flags).  Returns a
+    cudaError_t code."""
     sig = layout.signature(*caps)
     relax_iters = joint_iters if relax_iters is None else relax_iters
     b = make_batch(worlds, stride, offset, count)
+    if flags:
+        assert workspace is None, "the mode entry point uses the library's workspace"
+        return lib().b3x_batch_step_gpu_flags(b, dt, substeps, _ptr(active), _stream(stream), sig, joint_iters,
+                                              relax_iters, flags)
     if workspace is not None:
         return lib().b3x_batch_step_gpu_ws(b, dt, substeps, _ptr(active), _stream(stream), sig, joint_iters,
                                            relax_iters, _ptr(workspace), workspace.numel() * workspace.element_size())

@@ -33,7 +33,7 @@ class Pair:
             assert engine.batch_apply_gpu(self.dev, kind, idx, self.vals, active=act_dev, caps=cfg.caps) == 0
         assert self.o.batch_step(self.host, cfg.dt, cfg.substeps, active=active) == 1
         rc = engine.batch_step_gpu(self.dev, cfg.dt, cfg.substeps, active=act_dev, caps=cfg.caps,
-                                   joint_iters=cfg.joint_iters, relax_iters=cfg.relax_iters)
+                                   joint_iters=cfg.joint_iters, relax_iters=cfg.relax_iters, flags=cfg.flags)
         assert rc == 0
         torch.cuda.synchronize()
 

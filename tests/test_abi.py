@@ -155,3 +155,21 @@ def test_device_b3_step_in_adapter_kernels(tmp_path):
                                        "-I" + os.path.join(ROOT, "include"), str(a), str(b), "-o", str(out)]
     res = subprocess.run(cmd, capture_output=True, text=True)
     assert res.returncode == 0, res.stdout + res.stderr
+
+
+def test_force_hook_adapter_uses_the_per_thread_step(tmp_path):
+    """With B3_USER_FORCES defined, b3_batch_step_gpu compiles to the header's
+    per-thread step (which runs the hook) and needs no library symbol."""
+    src = tmp_path / "hooked.cu"
+    src.write_text('#define B3_MAX_BODIES 2\n#define B3_MAX_SHAPES 2\n#define B3_MAX_CONTACTS 4\n'
+                   '#define B3_MAX_JOINTS 1\n'
+                   '#define B3_USER_FORCES(w, h) ((w)->bodies[0].force.y += 1.0f)\n'
+                   '#include "b3_batch.cuh"\n'
+                   'static_assert(B3_HAS_USER_FORCES, "hook seen");\n'
+                   'int main() { B3Batch b = {nullptr, sizeof(B3World), 0, 0};\n'
+                   '  return (int)b3_batch_step_gpu(b, 1.0f / 60.0f, 4, nullptr, 0); }\n')
+    out = tmp_path / "hooked"
+    cmd = [build.NVCC] + build.ARCH + ["-O1", "-std=c++17", "-I" + os.path.join(ROOT, "include"), str(src),
+                                       "-o", str(out)]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    assert res.returncode == 0, res.stdout + res.stderr

@@ -18,7 +18,7 @@ import pytest
 import oracle as orc
 from gpu_util import TOL_1STEP, TOL_60STEP, Pair, contact_keys, state_close
 from puffysics_b200 import layout
-from puffysics_b200.configs import CONFIGS
+from puffysics_b200.configs import CONFIGS, SCENE_CHAIN
 
 pytestmark = pytest.mark.gpu
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
@@ -27,7 +27,7 @@ EXACT = ["hover", "stack", "pile", "bounce"]
 
 def check_step(name, got, want, step):
     cfg = CONFIGS[name]
-    if name != "chain":
+    if cfg.scene != SCENE_CHAIN:
         if not np.array_equal(got, want):
             bad = np.where((got != want).any(1))[0]
             raise AssertionError("%s: %d worlds differ at step %d (first %d)" % (name, len(bad), step, bad[0]))
@@ -64,6 +64,19 @@ def test_rollout_matches_oracle_every_step(name, oracle_kind, gpu_lib):
     if name == "stacksmall":
         v = layout.view(p.got(), cfg.caps)
         assert (v["contact_overflow"] == 1).any() and v["contacts_dropped"].sum() > 0
+
+
+@pytest.mark.parametrize("name", ["stackil", "chainil", "bouncenr", "bounceilnr"])
+def test_step_modes_match_oracle(name, oracle_kind, gpu_lib):
+    """The reference's B3_INTERLEAVE_CONTACTS / B3_SKIP_RESTITUTION modes
+    (b3x_batch_step_gpu_flags) against the reference built with them."""
+    cfg = CONFIGS[name]
+    o = orc.Oracle(name, oracle_kind)
+    seed = 808
+    p = Pair(cfg, o, o.build(128, cfg.scene, seed), seed)
+    for step in range(1, 41):
+        p.step(step)
+        check_step(name, p.got(), p.host, step)
 
 
 @pytest.mark.parametrize("n", [1, 31, 33, 4097])

@@ -13,7 +13,7 @@ import pytest
 import oracle as orc
 from gpu_util import TOL_1STEP, TOL_60STEP, Pair, contact_keys, state_close
 from puffysics_b200 import engine, layout, synth
-from puffysics_b200.configs import CONFIGS
+from puffysics_b200.configs import CONFIGS, SCENE_CHAIN
 
 pytestmark = pytest.mark.gpu
 
@@ -43,7 +43,7 @@ class ThreadPair(Pair):
 
 def check(name, got, want, step):
     cfg = CONFIGS[name]
-    if name != "chain":
+    if cfg.scene != SCENE_CHAIN:
         if not np.array_equal(got, want):
             bad = np.where((got != want).any(1))[0]
             raise AssertionError("%s: %d worlds differ at step %d (first %d)" % (name, len(bad), step, bad[0]))
@@ -59,7 +59,8 @@ def built():
     build.build()
 
 
-@pytest.mark.parametrize("name", ["hover", "stack", "chain", "pile", "default", "bounce"])
+@pytest.mark.parametrize("name", ["hover", "stack", "chain", "pile", "default", "bounce", "stackil", "chainil",
+                                  "bouncenr", "bounceilnr", "hoveruf"])
 def test_thread_step_matches_reference(name, oracle_kind, built):
     cfg = CONFIGS[name]
     L = engine.thread_lib(name)

@@ -62,8 +62,11 @@ def test_reference_reproduces_golden(name):
     assert np.array_equal(out[1], g["step1"]) and np.array_equal(out[60], g["step60"])
 
 
+MODE_CONFIGS = ["stackil", "chainil", "bouncenr", "bounceilnr", "hoveruf"]
+
+
 @needs_ref
-@pytest.mark.parametrize("name", ROLLOUT_CONFIGS + ["default", "stacksmall"])
+@pytest.mark.parametrize("name", ROLLOUT_CONFIGS + ["default", "stacksmall"] + MODE_CONFIGS)
 def test_port_equals_reference_rollout(name, port_built):
     cfg = CONFIGS[name]
     ref, port = orc.Oracle(name, "ref"), orc.Oracle(name, "port")
@@ -130,3 +133,20 @@ def test_batch_validation_without_mutation(kind, port_built):
     assert o.batch_step(w, 1 / 60, 4, active=mask) == 1
     assert np.array_equal(w[1], before[1]) and np.array_equal(w[3], before[3])
     assert not np.array_equal(w[0], before[0])
+
+
+@needs_ref
+@pytest.mark.parametrize("mode,plain", [("stackil", "stack"), ("bouncenr", "bounce"), ("hoveruf", "hover")])
+def test_step_modes_change_the_trajectory(mode, plain):
+    """The mode builds really run another step: their worlds leave the
+    default mode's after a few steps."""
+    cfg = CONFIGS[mode]
+    a, b = orc.Oracle(mode, "ref"), orc.Oracle(plain, "ref")
+    w = a.build(16, cfg.scene, 5)
+    wa, wb = w.copy(), w.copy()
+    for step in range(1, 6):
+        a.apply(wa, cfg.scene, 5, 0, step)
+        b.apply(wb, cfg.scene, 5, 0, step)
+        a.batch_step(wa, cfg.dt, cfg.substeps)
+        b.batch_step(wb, cfg.dt, cfg.substeps)
+    assert not np.array_equal(wa, wb)
