@@ -32,6 +32,9 @@ HOVER_SRC = os.path.join(PKG, "csrc", "b3x_hover_env.cu")
 HOVER_LIB = os.path.join(LIB_DIR, "libb3hover.so")
 HOVER_HEADERS = THREAD_HEADERS + [os.path.join(ROOT, "include", "b3x_staged.cuh")]
 THREAD_HEADERS = THREAD_HEADERS + [os.path.join(PKG, "scenes", "b3_test_forces.h")]
+# what the per-thread libraries include
+THREAD_DEPS = THREAD_HEADERS + [os.path.join(ROOT, "include", "puffysics_b200.h"),
+                                os.path.join(PKG, "csrc", "b3x_math.cuh"), os.path.join(PKG, "csrc", "b3x_narrow.cuh")]
 # capacity configurations the host scene builders are compiled for:
 # name -> (bodies, shapes, contacts, joints)
 SCENE_CONFIGS = {"hover": (2, 2, 4, 1), "stack": (9, 9, 32, 1), "chain": (12, 12, 32, 10),
@@ -89,10 +92,10 @@ def hover_cmd():
 def build_thread_libs(force=False):
     """The per-thread step launchers, one per capacity configuration, and the
     hover environment library, compiled concurrently."""
-    deps = [THREAD_SRC, __file__] + HEADERS + THREAD_HEADERS
+    deps = [THREAD_SRC, __file__] + THREAD_DEPS
     todo = [n for n in THREAD_CONFIGS if force or _newer(thread_lib(n), deps)]
     cmds = {n: thread_cmd(n) for n in todo}
-    if force or _newer(HOVER_LIB, [HOVER_SRC, __file__] + HEADERS + HOVER_HEADERS):
+    if force or _newer(HOVER_LIB, [HOVER_SRC, __file__] + THREAD_DEPS + HOVER_HEADERS):
         cmds["hover environment"] = hover_cmd()
     procs = [(n, subprocess.Popen(c, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True))
              for n, c in cmds.items()]
@@ -118,10 +121,10 @@ def _newer(out, deps):
 
 def up_to_date():
     deps = SOURCES + HEADERS + [__file__]
-    thread_deps = [THREAD_SRC, __file__] + HEADERS + THREAD_HEADERS
+    thread_deps = [THREAD_SRC, __file__] + THREAD_DEPS
     return (not _newer(LIB, deps) and not any(_newer(scenes_lib(n), [SCENES_SRC] + HEADERS) for n in SCENE_CONFIGS)
             and not any(_newer(thread_lib(n), thread_deps) for n in THREAD_CONFIGS)
-            and not _newer(HOVER_LIB, [HOVER_SRC, __file__] + HEADERS + HOVER_HEADERS))
+            and not _newer(HOVER_LIB, [HOVER_SRC, __file__] + THREAD_DEPS + HOVER_HEADERS))
 
 
 def build_scenes(force=False):

@@ -613,6 +613,9 @@ B3X_HDI void solve_joint(float* __restrict__ bc, const float* __restrict__ bp, c
 // body velocity, pose-delta and constant columns (lane-offset; shared memory or
 // the slot's body / bodyp / bodyk regions).  Returns false when the pipeline failed.  Follows
 // 09_step.inl:158-181.
+// kInterleave: the B3_INTERLEAVE_CONTACTS mode (a separate instantiation, so
+// that the default mode's code is not shaped by the other).
+template <bool kInterleave>
 B3X_HD bool solve_world(const Args& a, float* slot, int lane, float* __restrict__ bc, float* __restrict__ bp,
         const float* __restrict__ bk, Pipe& P) {
     const float* rec = slot + a.SP.rec + lane;
@@ -656,22 +659,16 @@ B3X_HD bool solve_world(const Args& a, float* slot, int lane, float* __restrict_
         }))
         return false;
 
-    auto contact_pass_of = [&](auto pass) {
+    auto contact_pass = [&](auto pass) {
         constexpr int kPass = decltype(pass)::value;
         return stream_items(P, cc, kCI, kContactStream, wn, [&](int k, const float* src) {
             if (k < n) solve_contact<kPass>(bc, bp, bk, src, item(cc, k, kCI), inv_h, contact_speed, cs, ss);
         });
     };
-    // one call site per sweep kind
-    auto contact_pass = [&](int kind) {
-        switch (kind) {
-        case kBiasFresh: return contact_pass_of(std::integral_constant<int, kBiasFresh>{});
-        case kBiasCached: return contact_pass_of(std::integral_constant<int, kBiasCached>{});
-        case kRelax: return contact_pass_of(std::integral_constant<int, kRelax>{});
-        default: return contact_pass_of(std::integral_constant<int, kRelaxCached>{});
-        }
-    };
-    const bool interleave = (a.flags & kStepInterleaveContacts) != 0;
+    using Fresh = std::integral_constant<int, kBiasFresh>;
+    using Cached = std::integral_constant<int, kBiasCached>;
+    using Relax = std::integral_constant<int, kRelax>;
+    using RelaxCached = std::integral_constant<int, kRelaxCached>;
     auto joint_pass = [&](int use_bias) {
         return stream_items(P, jc, NJF, kJointStream, wj, [&](int q, const float* src) {
             if (q < nj && ldi(src, JOK)) solve_joint(bc, bp, bk, src, item(jc, q, NJF), h, inv_h, use_bias);
@@ -696,11 +693,15 @@ B3X_HD bool solve_world(const Args& a, float* slot, int lane, float* __restrict_
         // bias phase (09_step.inl:170-172): one contact sweep, then the joint
         // iterations; interleaved, a contact sweep opens every joint iteration
         // (07_packed.inl:61-65)
-        const int bias_rounds = interleave ? a.joint_iters : 1;
-        for (int it = 0; it < bias_rounds; it++) {
-            if (!contact_pass(it == 0 && s == 0 ? kBiasFresh : kBiasCached)) return false;
-            for (int q = 0; q < (interleave ? 1 : a.joint_iters); q++)
+        if (!kInterleave) {
+            if (s == 0 ? !contact_pass(Fresh{}) : !contact_pass(Cached{})) return false;
+            for (int it = 0; it < a.joint_iters; it++)
                 if (!joint_pass(1)) return false;
+        } else {
+            for (int it = 0; it < a.joint_iters; it++) {
+                if (it == 0 && s == 0 ? !contact_pass(Fresh{}) : !contact_pass(Cached{})) return false;
+                if (!joint_pass(1)) return false;
+            }
         }
         // integrate positions (09_step.inl:55-107)
         for (int k = 0; k < nb; k++) {
@@ -723,11 +724,15 @@ B3X_HD bool solve_world(const Args& a, float* slot, int lane, float* __restrict_
             stq(bp, BP(k, BDQ), q_integrate(ldq(bp, BP(k, BDQ)), b3_mul(av, h)));
         }
         // relax phase (09_step.inl:173-177), the same way
-        const int relax_rounds = interleave ? a.relax_iters : 1;
-        for (int it = 0; it < relax_rounds; it++) {
-            if (!contact_pass(it == 0 ? kRelax : kRelaxCached)) return false;
-            for (int q = 0; q < (interleave ? 1 : a.relax_iters); q++)
+        if (!kInterleave) {
+            if (!contact_pass(Relax{})) return false;
+            for (int it = 0; it < a.relax_iters; it++)
                 if (!joint_pass(0)) return false;
+        } else {
+            for (int it = 0; it < a.relax_iters; it++) {
+                if (it == 0 ? !contact_pass(Relax{}) : !contact_pass(RelaxCached{})) return false;
+                if (!joint_pass(0)) return false;
+            }
         }
         // restitution (08_contacts.inl:439-480): skipped when no contact of
         // the warp's worlds has a nonzero coefficient, or in the

@@ -80,7 +80,7 @@ enum BodyPlace : int { kBodyNone = 0, kBodyVel = 1, kBodyState = 2, kBodyAll = 3
 // Warp 0's part of the step: warm start and substeps of the tile's 32 worlds.
 // Returns false when a pipeline wait gave up (nothing of the tile is then
 // written back: the step is abandoned for these worlds).
-template <int kBody>
+template <int kBody, bool kInterleave>
 __device__ bool solve_tile(const Args& a, unsigned char* smem_raw) {
     const int lane = threadIdx.x & 31;
     float* slot = slot_of(a, blockIdx.x);
@@ -105,7 +105,7 @@ __device__ bool solve_tile(const Args& a, unsigned char* smem_raw) {
     float* bc = (kBody >= kBodyVel ? sv : gv) + lane;
     float* bp = (kBody >= kBodyState ? sp : gp) + lane;
     const float* bk = (kBody == kBodyAll ? sk : gk) + lane;
-    const bool ok = solve_world(a, slot, lane, bc, bp, bk, P);
+    const bool ok = solve_world<kInterleave>(a, slot, lane, bc, bp, bk, P);
     if (ok && kBody >= kBodyVel)
         for (int idx = lane; idx < nb * NBF * kLanes; idx += kLanes) gv[idx] = sv[idx];
     if (ok && kBody >= kBodyState)
@@ -122,7 +122,7 @@ __device__ bool solve_tile(const Args& a, unsigned char* smem_raw) {
 
 // One block per tile: collide (all warps), solve (warp 0), write-back (all
 // warps).
-template <int kBody>
+template <int kBody, bool kInterleave = false>
 __global__ void __launch_bounds__(kCta, 4) step_kernel(Args a) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     __shared__ int solved;
@@ -134,7 +134,7 @@ __global__ void __launch_bounds__(kCta, 4) step_kernel(Args a) {
     asm volatile("fence.proxy.async;" ::: "memory");
     __syncthreads();
     if (threadIdx.x < kLanes) {
-        const bool ok = solve_tile<kBody>(a, smem_raw);
+        const bool ok = solve_tile<kBody, kInterleave>(a, smem_raw);
         if (threadIdx.x == 0) solved = ok;
     }
     __syncthreads();
@@ -339,7 +339,9 @@ static cudaError_t make_plan(int dev, unsigned long long sig, const Layout& L, P
     if (p.smem_bytes < sizeof(CollideShared)) p.smem_bytes = sizeof(CollideShared);
     if (p.smem_bytes < sizeof(OutShared)) p.smem_bytes = sizeof(OutShared);
     if (p.smem_bytes > (size_t)cap) return cudaErrorInvalidValue;
-    for (auto fn : {step_kernel<kBodyNone>, step_kernel<kBodyVel>, step_kernel<kBodyState>, step_kernel<kBodyAll>}) {
+    for (auto fn : {step_kernel<kBodyNone>, step_kernel<kBodyVel>, step_kernel<kBodyState>, step_kernel<kBodyAll>,
+                    step_kernel<kBodyNone, true>, step_kernel<kBodyVel, true>, step_kernel<kBodyState, true>,
+                    step_kernel<kBodyAll, true>}) {
         e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, cap);
         if (e != cudaSuccess) return e;
     }
@@ -390,10 +392,17 @@ static cudaError_t launch_step(const B3Batch& batch, float dt, int substeps, con
     for (int t0 = 0; t0 < ntiles; t0 += chunk) {
         const int nt = ntiles - t0 < chunk ? ntiles - t0 : chunk;
         a.tile0 = t0;
-        if (p.body == kBodyAll) step_kernel<kBodyAll><<<nt, kCta, p.smem_bytes, stream>>>(a);
-        else if (p.body == kBodyState) step_kernel<kBodyState><<<nt, kCta, p.smem_bytes, stream>>>(a);
-        else if (p.body == kBodyVel) step_kernel<kBodyVel><<<nt, kCta, p.smem_bytes, stream>>>(a);
-        else step_kernel<kBodyNone><<<nt, kCta, p.smem_bytes, stream>>>(a);
+        if (flags & kStepInterleaveContacts) {
+            if (p.body == kBodyAll) step_kernel<kBodyAll, true><<<nt, kCta, p.smem_bytes, stream>>>(a);
+            else if (p.body == kBodyState) step_kernel<kBodyState, true><<<nt, kCta, p.smem_bytes, stream>>>(a);
+            else if (p.body == kBodyVel) step_kernel<kBodyVel, true><<<nt, kCta, p.smem_bytes, stream>>>(a);
+            else step_kernel<kBodyNone, true><<<nt, kCta, p.smem_bytes, stream>>>(a);
+        } else {
+            if (p.body == kBodyAll) step_kernel<kBodyAll><<<nt, kCta, p.smem_bytes, stream>>>(a);
+            else if (p.body == kBodyState) step_kernel<kBodyState><<<nt, kCta, p.smem_bytes, stream>>>(a);
+            else if (p.body == kBodyVel) step_kernel<kBodyVel><<<nt, kCta, p.smem_bytes, stream>>>(a);
+            else step_kernel<kBodyNone><<<nt, kCta, p.smem_bytes, stream>>>(a);
+        }
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     }
