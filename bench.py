@@ -54,7 +54,8 @@ TRAFFIC_FILE_FMT = os.path.join(ROOT, "profiles", "step_kernel_%s.md")
 
 WORKLOAD = {"hover": "C1 hover (4,096 worlds/GPU)", "stack": "C2 box stack (16,384 worlds/GPU)",
             "chain": "C3 capsule chain (16,384 worlds/GPU)", "pile": "C4 pile (65,536 worlds/GPU)",
-            "scaleout": "C5 scale-out (1,048,576 C2 worlds in total, 1% reset per step)"}
+            "scaleout": "C5 scale-out (1,048,576 C2 worlds in total, 1% reset per step)",
+            "stackil": "C2 box stack in the B3_INTERLEAVE_CONTACTS mode (16,384 worlds/GPU)"}
 
 
 def parse_args():
@@ -470,7 +471,7 @@ def main():
         if ev is not None:
             ev.record(stream)
         rc = engine.batch_step_gpu(worlds, cfg.dt, cfg.substeps, None, stream, caps, cfg.joint_iters,
-                                   cfg.relax_iters)
+                                   cfg.relax_iters, flags=cfg.flags)
         assert rc == 0, rc
         return launches + step_launches
 
@@ -530,7 +531,7 @@ def main():
             vals.copy_(h_act[:, :nv], non_blocking=True)
             assert engine.batch_apply_gpu(worlds, kind, aidx, vals, None, stream, caps) == 0
         assert engine.batch_step_gpu(worlds, cfg.dt, cfg.substeps, None, stream, caps, cfg.joint_iters,
-                                     cfg.relax_iters) == 0
+                                     cfg.relax_iters, flags=cfg.flags) == 0
         assert engine.batch_observe_gpu(worlds, obs_body, d_obs, stream, caps) == 0
         h_obs.copy_(d_obs, non_blocking=True)
         stream.synchronize()

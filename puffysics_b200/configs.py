@@ -56,7 +56,7 @@ CONFIGS = {
                      description="spheres and boxes with restitution and rolling resistance (parity coverage)"),
     # the reference's alternative step modes (B3_INTERLEAVE_CONTACTS,
     # B3_SKIP_RESTITUTION) on the same scenes
-    "stackil": Config("stackil", SCENE_STACK, (9, 9, 32, 1), 8, 8, 1.0 / 60.0, 4, 1024,
+    "stackil": Config("stackil", SCENE_STACK, (9, 9, 32, 1), 8, 8, 1.0 / 60.0, 4, 16384,
                       flags=STEP_INTERLEAVE_CONTACTS, description="stack, contacts interleaved with 8 iterations"),
     "chainil": Config("chainil", SCENE_CHAIN, (12, 12, 32, 10), 8, 8, 1.0 / 120.0, 2, 1024,
                       flags=STEP_INTERLEAVE_CONTACTS, description="chain, contacts interleaved with the joints"),
