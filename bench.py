@@ -69,6 +69,7 @@ def parse_args():
     ap.add_argument("--e2e-steps", type=int, default=200)
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graph", action="store_true", help="e2e with direct calls instead of a CUDA graph")
     ap.add_argument("--no-per-thread-path", action="store_true",
                     help="skip the timing of the per-thread device b3_step after the main measurement")
     return ap.parse_args()
@@ -521,23 +522,55 @@ def main():
     obs_body = min(obs_body, int(layout.view(worlds[:1].cpu().numpy(), caps)["body_count"][0]) - 1)
     act_src = [torch.from_numpy(scenes.actions(per_gpu, SEED, first, step_no[0] + 1 + i)).contiguous()
                for i in range(min(E, 4))] if nv else []
+
+    def e2e_ops(s):
+        """One environment step through the C-ABI on stream s: the actions
+        from pinned host memory, apply, step, observe, observations back."""
+        if nv:
+            vals.copy_(h_act[:, :nv], non_blocking=True)
+            assert engine.batch_apply_gpu(worlds, kind, aidx, vals, None, s, caps) == 0
+        assert engine.batch_step_gpu(worlds, cfg.dt, cfg.substeps, None, s, caps, cfg.joint_iters,
+                                     cfg.relax_iters, flags=cfg.flags) == 0
+        assert engine.batch_observe_gpu(worlds, obs_body, d_obs, s, caps) == 0
+        h_obs.copy_(d_obs, non_blocking=True)
+
+    # The step's calls are captured once in a CUDA graph and replayed every
+    # step (the host writes that step's actions into the pinned buffer first,
+    # then waits for the observations).  The step's first call on a stream
+    # allocates its workspace, so one call runs on the capture stream before
+    # the capture.  Falls back to direct calls if capture is refused.
+    gstream = torch.cuda.Stream(dev)
+    gstream.wait_stream(stream)
+    graph, e2e_mode = None, "direct calls"
+    with torch.cuda.stream(gstream):
+        e2e_ops(gstream)
+    gstream.synchronize()
+    if not args.no_graph:
+        try:
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=gstream):
+                e2e_ops(gstream)
+            e2e_mode = "one CUDA graph replay"
+        except RuntimeError:
+            graph = None
+            torch.cuda.synchronize(dev)
     barrier()
     torch.cuda.synchronize(dev)
     e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e_start.record(stream)
-    for i in range(E):
-        if nv:
-            h_act[:, :nv].copy_(act_src[i % len(act_src)])
-            vals.copy_(h_act[:, :nv], non_blocking=True)
-            assert engine.batch_apply_gpu(worlds, kind, aidx, vals, None, stream, caps) == 0
-        assert engine.batch_step_gpu(worlds, cfg.dt, cfg.substeps, None, stream, caps, cfg.joint_iters,
-                                     cfg.relax_iters, flags=cfg.flags) == 0
-        assert engine.batch_observe_gpu(worlds, obs_body, d_obs, stream, caps) == 0
-        h_obs.copy_(d_obs, non_blocking=True)
-        stream.synchronize()
-    e_end.record(stream)
+    with torch.cuda.stream(gstream):
+        e_start.record(gstream)
+        for i in range(E):
+            if nv:
+                h_act[:, :nv].copy_(act_src[i % len(act_src)])
+            if graph is not None:
+                graph.replay()
+            else:
+                e2e_ops(gstream)
+            gstream.synchronize()
+        e_end.record(gstream)
     torch.cuda.synchronize(dev)
     e2e_local = e_start.elapsed_time(e_end)
+    del graph
     bi = per_gpu * nv * 4
     bo = per_gpu * 13 * 4
 
@@ -599,7 +632,7 @@ def main():
                 "e2e": {"value": total * E / (e_max / 1e3), "unit": UNIT, "h2d_bytes_per_step": bi,
                         "d2h_bytes_per_step": bo, "steps": E,
                         "path": "pinned H2D actions -> b3x_batch_apply_gpu -> b3x_batch_step_gpu -> "
-                                "b3x_batch_observe_gpu -> D2H, stream synchronised every step"},
+                                "b3x_batch_observe_gpu -> D2H (%s), stream synchronised every step" % e2e_mode},
                 "gpu_launches": launches,
                 "clocks": sampler.summary(),
                 "diagnostics": {"worlds": int(tot[0]), "contacts": int(tot[1]), "overflowed_worlds": int(tot[2]),
