@@ -300,21 +300,23 @@ def reference_gpu_env_run(steps, warmup):
                       "environment in place, nvcc -O3 sm_100a", "l2": "flushed between timed steps"}
 
 
-def thread_path_run(cfg, worlds, steps, warmup, stream):
+def thread_path_run(cfg, n, steps, warmup, stream, budget_s=60.0):
     """Time this library's per-thread device b3_step (include/puffysics.cuh,
-    one thread per world, libb3thread_<cfg>.so) on a copy of the worlds: the
-    scene's actions plus one launch per step, CUDA events on `stream`."""
+    one thread per world, libb3thread_<cfg>.so) over the stretch of the scene
+    the reference GPU kernel is timed on: freshly built worlds, the scene's
+    actions from step 1, the same warm-up, timed steps and L2 rule; CUDA
+    events on `stream` around each step."""
     import torch
     from puffysics_b200 import engine, synth
     try:
         engine.thread_lib(cfg.name)
     except RuntimeError:
         return None
-    w = worlds.clone()
-    n = w.shape[0]
+    dev = torch.device("cuda", torch.cuda.current_device())
+    w = torch.from_numpy(synth.SceneLib(cfg).build(n, SEED)).to(dev)
     kind, aidx, nv = cfg.action
-    vals = torch.zeros((n, max(nv, 1)), dtype=torch.float32, device=w.device)
-    step_no = [10 ** 6]
+    vals = torch.zeros((n, max(nv, 1)), dtype=torch.float32, device=dev)
+    step_no = [0]
 
     def one():
         step_no[0] += 1
@@ -323,22 +325,26 @@ def thread_path_run(cfg, worlds, steps, warmup, stream):
             assert engine.batch_apply_gpu(w, kind, aidx, vals, None, stream, cfg.caps) == 0
         assert engine.thread_step_gpu(cfg.name, w, cfg.dt, cfg.substeps, stream=stream) == 0
 
-    for _ in range(max(warmup, 3)):
+    for _ in range(max(warmup, 3) - 1):
         one()
-    torch.cuda.synchronize(w.device)
+    torch.cuda.synchronize(dev)
     t0 = time.time()
     one()
-    torch.cuda.synchronize(w.device)
-    k = int(max(3, min(steps, 10.0 / max(time.time() - t0, 1e-4))))
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(k):
+    torch.cuda.synchronize(dev)
+    k = int(max(3, min(steps or 100, budget_s / max(time.time() - t0, 1e-4))))
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev) if w.numel() < L2_BYTES * 2 else None
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(k)]
+    for e0, e1 in ev:
+        if flush is not None:
+            flush.zero_()
+        e0.record(stream)
         one()
-    e1.record(stream)
-    torch.cuda.synchronize(w.device)
-    ms = e0.elapsed_time(e1)
+        e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = sum(e0.elapsed_time(e1) for e0, e1 in ev)
     del w
     return {"value": n * k / (ms / 1e3), "unit": UNIT, "ms_per_step": ms / k, "worlds": n, "steps": k,
+            "l2": "flushed between timed steps" if flush is not None else "world array larger than twice L2",
             "kernel": "per-thread device b3_step of include/puffysics.cuh (one thread per world)"}
 
 
@@ -638,7 +644,7 @@ def main():
                 "diagnostics": {"worlds": int(tot[0]), "contacts": int(tot[1]), "overflowed_worlds": int(tot[2]),
                                 "dropped_contacts": int(tot[3])}}
         if world == 1 and not args.no_per_thread_path:
-            line["per_thread_path"] = thread_path_run(cfg, worlds, K, args.warmup, stream)
+            line["per_thread_path"] = thread_path_run(cfg, per_gpu, K, args.warmup, stream)
             if cfg.name == "hover":
                 line["fused_env"] = fused_env_run(K, args.warmup, stream)
         if world == 1 and not args.no_cpu_baseline:

@@ -20,7 +20,7 @@ namespace {
 
 constexpr int kThreads = 32;   // one warp per block, as the reference launches
 
-__global__ void thread_batch_kernel(B3Batch batch, float dt, int substeps, const unsigned char* active) {
+__global__ void B3X_THREAD_BOUNDS thread_batch_kernel(B3Batch batch, float dt, int substeps, const unsigned char* active) {
     size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i < (size_t)batch.count && (!active || active[i])) b3_step(b3_batch_world(batch, (int)i), dt, substeps);
 }
