@@ -53,7 +53,6 @@ struct CollideShared {
     union {
         float hdr[kLanes][NHW];                  // world headers (17: odd)
         float flat[kStageFloats];                // gathered struct rows of a group of worlds
-        float jstage[kLanes][NVW];               // one joint of every world (115: odd)
         float clip[48 * kCta];                   // narrowphase clip polygons
     } u;
 };
@@ -308,13 +307,27 @@ B3X_HD void c_old_row(const Args& a, float* slot, CollideShared& sh, int k, int 
     }
 }
 
-// Joint q of every world into jstage (warp w: worlds w, w+4, ...).
-B3X_HD void c_joint_gather(const Args& a, int tile, CollideShared& sh, int q, int t) {
+// Joints per collide round: as many B3Joint rows of every world as the
+// staging area holds.
+constexpr int kJointRound = kStageFloats / (kLanes * NVW);
+static_assert(kJointRound >= 1, "one joint of every world must fit the staging area");
+
+// Staged row of joint q0 + qq of world l (odd stride NVW: conflict-free
+// columns).
+B3X_HDI float* joint_row(CollideShared& sh, int qq, int l) { return sh.u.flat + (qq * kLanes + l) * NVW; }
+
+// Joints [q0, q0 + Q) of every world, each world's run of rows in one
+// contiguous copy (warp w: worlds w, w+4, ...).
+B3X_HD void c_joint_gather(const Args& a, int tile, CollideShared& sh, int q0, int Q, int t) {
     const int w = t >> 5, i = t & 31;
     for (int l = w; l < kLanes; l += kCtaWarps) {
-        if (q >= sh.nj[l]) continue;
-        const float* src = world_words(a, tile * kLanes + l) + (a.L.joint_off + (size_t)B3X_JOINT_BYTES * q) / 4;
-        for (int c = i; c < NVW; c += 32) async_copy4_world(&sh.u.jstage[l][c], src + c);
+        const int n = (sh.nj[l] < q0 + Q ? sh.nj[l] : q0 + Q) - q0;
+        if (n <= 0) continue;
+        const float* src = world_words(a, tile * kLanes + l) + (a.L.joint_off + (size_t)B3X_JOINT_BYTES * q0) / 4;
+        for (int idx = i; idx < n * NVW; idx += 32) {
+            const int qq = idx / NVW, c = idx - qq * NVW;
+            async_copy4_world(joint_row(sh, qq, l) + c, src + idx);
+        }
     }
     async_wait();
 }
@@ -323,9 +336,8 @@ B3X_HD void c_joint_gather(const Args& a, int tile, CollideShared& sh, int q, in
 // the B3Joint row with the prepared fields in place (jimg) for the write-back.
 // Invalid body indices make the joint inert (the reference would index out
 // of bounds).
-B3X_HD void c_joint(const Args& a, float* slot, CollideShared& sh, int q, int l) {
+B3X_HD void c_joint(const Args& a, float* slot, CollideShared& sh, int q, int l, float* y) {
     if (q >= sh.nj[l]) return;
-    float* y = sh.u.jstage[l];
     auto v3 = [&](int f) { return b3_v(y[f], y[f + 1], y[f + 2]); };
     auto v4 = [&](int f) { return b3_q(y[f], y[f + 1], y[f + 2], y[f + 3]); };
     auto put3 = [&](int f, B3Vec3 v) { y[f] = v.x; y[f + 1] = v.y; y[f + 2] = v.z; };
@@ -863,9 +875,12 @@ B3X_HD void collide_tile(X& x, const Args& a, int bt, CollideShared& sh) {
             }
         }
     }
-    for (int q = 0; q < sh.maxnj; q++) {
-        x.each([&](int t) { c_joint_gather(a, tile, sh, q, t); });
-        x.each([&](int t) { if (t < kLanes) c_joint(a, slot, sh, q, t); });
+    for (int q0 = 0; q0 < sh.maxnj; q0 += kJointRound) {
+        const int Q = sh.maxnj - q0 < kJointRound ? sh.maxnj - q0 : kJointRound;
+        x.each([&](int t) { c_joint_gather(a, tile, sh, q0, Q, t); });
+        x.each([&](int t) {
+            for (int j = t; j < Q * kLanes; j += kCta) c_joint(a, slot, sh, q0 + (j >> 5), j & 31, joint_row(sh, j >> 5, j & 31));
+        });
     }
     const int maxns = sh.maxns;
     const int npairs = maxns * (maxns - 1) / 2;
@@ -1079,9 +1094,10 @@ B3X_HD void o_joint_write(const Args& a, int tile, float* slot, OutShared& sh, i
         const int n = (sh.nj[l] < q0 + K ? sh.nj[l] : q0 + K) - q0;
         if (n <= 0) continue;
         float* dst = world_words_w(a, tile * kLanes + l) + (a.L.joint_off + (size_t)B3X_JOINT_BYTES * q0) / 4;
-        for (int idx = i; idx < n * NVW; idx += 32) {
-            const int kk = idx / NVW, c = idx - kk * NVW;
-            if (ldi(item(slot + a.SP.joint, q0 + kk, NJF) + l, JOK)) store_world(dst + idx, out_row(sh, l, kk, K, NVW)[c]);
+        for (int kk = 0; kk < n; kk++) {
+            if (!ldi(item(slot + a.SP.joint, q0 + kk, NJF) + l, JOK)) continue;
+            const float* row = out_row(sh, l, kk, K, NVW);
+            for (int c = i; c < NVW; c += 32) store_world(dst + kk * NVW + c, row[c]);
         }
     }
 }
