@@ -50,7 +50,7 @@ BYTES_DYN_BODY, BYTES_BODY, BYTES_SHAPE, BYTES_CONTACT, BYTES_JOINT = 196, 44, 8
 # (add/sub/mul/div/sqrt = 1 each, comparisons excluded) on these scenes,
 # measured by oracle/flops; None until counted.
 FLOPS_FILE = os.path.join(ROOT, "profiles", "flops_per_world_step.md")
-TRAFFIC_FILE_FMT = os.path.join(ROOT, "profiles", "step_kernel_%s.md")
+TRAFFIC_FILE_FMT = os.path.join(ROOT, "profiles", "%s_%s.md")      # (kernel, scene)
 
 WORKLOAD = {"hover": "C1 hover (4,096 worlds/GPU)", "stack": "C2 box stack (16,384 worlds/GPU)",
             "chain": "C3 capsule chain (16,384 worlds/GPU)", "pile": "C4 pile (65,536 worlds/GPU)",
@@ -602,8 +602,11 @@ def main():
             pass
         hbm_peak = peaks.get("hbm_gbs") or 6650.0
         achieved = alg_bytes / kern_s / 1e9
-        traffic_scene = cfg.name
-        traffic = read_number(TRAFFIC_FILE_FMT % traffic_scene, "dram_bytes_per_world_step")
+        # worlds small enough to be stepped whole in shared memory take the
+        # small-world kernel: one launch for any batch size
+        small_path = engine.step_launches(caps, 1 << 20, local) == 1
+        kname = "small_step_kernel" if small_path else "step_kernel"
+        traffic = read_number(TRAFFIC_FILE_FMT % (kname, cfg.name), "dram_bytes_per_world_step")
         flops_ws = read_number(FLOPS_FILE, "%s_flops_per_world_step" % cfg.name)
         sm_max = (peaks.get("sm_max_mhz") or 1965.0)
         fp32_peak = 148 * 128 * sm_max * 1e6 / 1e12      # one fp32 add or mul per lane per clock
@@ -611,7 +614,9 @@ def main():
                 "frac": achieved / hbm_peak,
                 "traffic": traffic * per_gpu if traffic else None,
                 "peak_source": "MEASURED_PEAKS.json hbm_gbs" if peaks.get("hbm_gbs") else "fallback 6650 GB/s",
-                "kernel": "b3x::step_kernel (collide, solve and write-back phases; %d launch(es) per step)"
+                "kernel": ("b3x::small_step_kernel (worlds staged whole in shared memory, one thread per "
+                           "world; %d launch per step)" if small_path else
+                           "b3x::step_kernel (collide, solve and write-back phases; %d launch(es) per step)")
                           % step_launches, "kernel_ms": kern_s * 1e3,
                 "algorithmic_bytes_per_launch": alg_bytes,
                 "algorithmic_bytes_per_world_step": bytes_world}
