@@ -1048,11 +1048,11 @@ B3X_HD void o_contact_write(const Args& a, int tile, OutShared& sh, int k0, int 
         const int n = (sh.n[l] < k0 + K ? sh.n[l] : k0 + K) - k0;
         if (n <= 0) continue;
         float* dst = world_words_w(a, tile * kLanes + l) + (a.L.contact_off + (size_t)B3X_CONTACT_BYTES * k0) / 4;
-        for (int idx = i; idx < n * NCW; idx += 32) {
-            const int kk = idx / NCW, c = idx - kk * NCW;
+        for (int kk = 0; kk < n; kk++) {    // row by row: each row's point count is read once
             const float* row = out_row(sh, l, kk, K, NCW);
-            const int cnt = clampi(b3x_f2i(row[WCNT]), 0, B3_MAX_MANIFOLD);
-            if (c < WP + cnt * NQW || c >= WCA) store_world(dst + idx, row[c]);
+            const int hi = WP + clampi(b3x_f2i(row[WCNT]), 0, B3_MAX_MANIFOLD) * NQW;
+            for (int c = i; c < NCW; c += 32)
+                if (c < hi || c >= WCA) store_world(dst + kk * NCW + c, row[c]);
         }
     }
 }

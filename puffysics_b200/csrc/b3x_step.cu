@@ -172,8 +172,8 @@ __device__ __forceinline__ void async_copy8(void* dst, const void* src) {
 // the instruction fetches of this long per-world program.
 constexpr int kSmallWorlds = SMALL_WORLDS_PER_BLOCK;
 __global__ void __launch_bounds__(kLanes) small_step_kernel(Args a, unsigned stride_words) {
-    extern __shared__ __align__(16) unsigned char smem_raw[];
-    uint64_t* sw = reinterpret_cast<uint64_t*>(smem_raw);
+    extern __shared__ __align__(16) unsigned char small_smem[];
+    uint64_t* sw = reinterpret_cast<uint64_t*>(small_smem);
     const int lane = threadIdx.x;
     const long long first = (long long)blockIdx.x * kSmallWorlds;
     const unsigned words = a.L.size / 8;
@@ -192,7 +192,7 @@ __global__ void __launch_bounds__(kLanes) small_step_kernel(Args a, unsigned str
     asm volatile("cp.async.wait_all;" ::: "memory");
     __syncwarp();
     if (live) {
-        unsigned char* base = smem_raw + (size_t)lane * stride_words * 8;
+        unsigned char* base = small_smem + (size_t)lane * stride_words * 8;
         SmallView v;
         v.h = reinterpret_cast<B3World*>(base);
         v.bodies = reinterpret_cast<B3Body*>(base + B3X_WORLD_HEADER_BYTES);
