@@ -18,7 +18,8 @@ e2e      through the C-ABI with host buffers: each step copies that step's
          actions from pinned host memory, applies them, steps, gathers one
          observation per world and copies it back, then synchronises.
 roofline the step kernel alone, its CUDA-event duration against the
-         algorithmic bytes of a world-step (byte model in DESIGN.md).
+         algorithmic bytes of a world-step (the byte model below), plus the
+         fp32 work per world-step against one add or mul per lane per clock.
 """
 import argparse
 import json
@@ -46,9 +47,10 @@ L2_BYTES = 126e6
 # 68 r / 68 w), joint 208 B (constants 112 r, impulses 48 r / 48 w).
 BYTES_DYN_BODY, BYTES_BODY, BYTES_SHAPE, BYTES_CONTACT, BYTES_JOINT = 196, 44, 84, 136, 208
 
-# Counted fp32 operations of one world-step of the reference's default path
-# (add/sub/mul/div/sqrt = 1 each, comparisons excluded) on these scenes,
-# measured by oracle/flops; None until counted.
+# fp32 operations of one world-step per scene (fadd + fmul + 2 x ffma of one
+# step-kernel launch, counted by ncu on the benchmark workloads and committed
+# under profiles/ with the commands that made them); None for scenes not
+# counted.
 FLOPS_FILE = os.path.join(ROOT, "profiles", "flops_per_world_step.md")
 TRAFFIC_FILE_FMT = os.path.join(ROOT, "profiles", "%s_%s.md")      # (kernel, scene)
 
