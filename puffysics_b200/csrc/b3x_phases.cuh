@@ -661,7 +661,16 @@ B3X_HD void c_narrow(const Args& a, float* slot, CollideShared& sh, int t) {
 // carry (08_contacts.inl:136-171) and b3_prepare_one_contact
 // (08_contacts.inl:234-291); words [0, kCW), point slots past the point
 // count are not written.
-B3X_HD void c_build(const Args& a, float* slot, CollideShared& sh, int t) {
+// The tile's warm-start cache into the staging area (same [item][field][lane]
+// layout), so that the contact build's cache lookups read shared memory.
+B3X_HD void c_stage_old(const Args& a, float* slot, CollideShared& sh, int t) {
+    const float* src = slot + a.SP.old;
+    const int n = sh.maxold * NOF * kLanes;
+    for (int idx = t; idx < n; idx += kCta) async_copy4(sh.u.flat + idx, src + idx);
+    async_wait();
+}
+
+B3X_HD void c_build(const Args& a, float* slot, CollideShared& sh, int t, const float* old_base) {
     const float* sc = slot + a.SP.shape;
     for (int idx = t; idx < sh.total; idx += kCta) {
         int r, l;
@@ -708,7 +717,7 @@ B3X_HD void c_build(const Args& a, float* slot, CollideShared& sh, int t) {
         fi.y = 0.0f;
         float twi = 0.0f;
         B3Vec3 ri = b3_v(0.0f, 0.0f, 0.0f);
-        const float* oc = slot + a.SP.old + l;
+        const float* oc = old_base + l;
         int first, end;
         warm_range(oc, sh.oldn[l], sh.sorted[l], i, j, p, first, end);
         for (int kk = first; kk < end; kk++) {
@@ -893,7 +902,10 @@ B3X_HD void collide_tile(X& x, const Args& a, int bt, CollideShared& sh) {
         x.each([&](int t) { c_narrow(a, slot, sh, t); });
         x.each([&](int t) { if (t < kLanes) c_plan(a, sh, t); });
         if (sh.total == 0) continue;
-        x.each([&](int t) { c_build(a, slot, sh, t); });
+        // the staging area is free between the narrowphase and the next window
+        const bool stage_old = sh.maxold > 0 && sh.maxold * NOF * kLanes <= kStageFloats;
+        if (stage_old) x.each([&](int t) { c_stage_old(a, slot, sh, t); });
+        x.each([&](int t) { c_build(a, slot, sh, t, stage_old ? sh.u.flat : slot + a.SP.old); });
     }
     x.each([&](int t) { if (t < kLanes) c_finish(a, slot, sh, t); });
 }
