@@ -821,9 +821,17 @@ B3_HD B3_INL B3World* b3_batch_world(B3Batch batch, int index) {
  * or negative dt, substeps < 1 -> 1, nothing launched or written), same no-op
  * cases (count == 0 or dt == 0 -> 0), same mask meaning (NULL = all worlds,
  * nonzero byte = selected; unselected worlds are not written).  Additionally
- * rejects world addresses or strides that are not 8-byte aligned.  The first
- * call per (device, stream, capacity configuration) allocates a device
- * workspace; make it before any stream capture.  Later calls only enqueue. */
+ * rejects world addresses or strides that are not 8-byte aligned.  Like the
+ * reference (b3_batch.cuh:77-80) it only enqueues on `stream`: no allocation,
+ * no synchronisation.  Its workspace is the one b3x_reserve_workspace made
+ * for `stream` (set-up), else a fixed 128 MiB array inside the library, on
+ * which it runs as many tiles per launch as fit (slower for large batches);
+ * calls on the array from different streams are ordered on the GPU with an
+ * event, except while the stream is being captured into a CUDA graph (reserve
+ * a workspace for capture streams).  A capacity configuration whose tile slot
+ * exceeds the array needs a reservation: 2 (cudaErrorMemoryAllocation)
+ * without one.  The library's kernels load on a device at its first call:
+ * make that call before any stream capture. */
 B3X_API int b3x_batch_step_gpu(B3Batch batch, float dt, int substeps, const unsigned char* active,
     void* stream, unsigned long long config_signature, int joint_iters, int relax_iters);
 
@@ -852,21 +860,47 @@ B3X_API int b3x_batch_step_gpu_ws(B3Batch batch, float dt, int substeps, const u
  * a framework allocator or plugin host that forbids cudaMalloc, real-time
  * loops that cannot risk an allocation's synchronisation): the workspace is a
  * fixed 64 MiB array inside the library, reserved on every device that loads
- * it.  Calls nothing that allocates.  The first call on a device resolves the
- * array's device address (make it before any stream capture).  All calls on a
- * device share the array: calls that overlap on the GPU race.  Capacity
- * configurations needing a workspace slot above 64 MiB return
- * cudaErrorInvalidValue; batch size is not limited. */
+ * it, never a reservation.  Calls nothing that allocates.  Every call looks
+ * up the array's device address on the current device; the first call on a
+ * device loads the library's kernels there (make it before any stream
+ * capture).  All calls on a device share the array: calls that overlap on
+ * the GPU race.  Capacity configurations needing a workspace slot above
+ * 64 MiB return cudaErrorInvalidValue (configurations stepped whole in shared
+ * memory need none); batch size is not limited. */
 B3X_API int b3x_batch_step_gpu_noalloc(B3Batch batch, float dt, int substeps, const unsigned char* active,
     void* stream, unsigned long long config_signature, int joint_iters, int relax_iters);
 
 /* Bytes of workspace a step needs on `device` for this capacity configuration
- * (independent of the batch size); 0 if the configuration is invalid. */
+ * to run one launch per wave of resident tiles (independent of the batch
+ * size; what b3x_reserve_workspace allocates); 0 if the configuration is
+ * invalid. */
 B3X_API size_t b3x_workspace_bytes(unsigned long long config_signature, int device);
 
+/* No counterpart in the reference.  Bytes of one tile's slot of the
+ * workspace (32 worlds); a workspace of k slots runs up to k tiles per
+ * launch.  0 if the configuration is invalid. */
+B3X_API size_t b3x_workspace_slot_bytes(unsigned long long config_signature);
+
+/* No counterpart in the reference (whose per-thread step needs no
+ * workspace).  Set-up call, the library's only device allocation: reserve
+ * b3x_workspace_bytes(...) of device memory for steps of this capacity
+ * configuration on `stream` (current device).  Later b3x_batch_step_gpu /
+ * b3_batch_step_gpu calls on that stream use it.  A reservation that is
+ * large enough is kept; a smaller one is replaced (cudaFree synchronises).
+ * Configurations stepped in shared memory need none (returns 0).  Batches
+ * stepped concurrently on several streams should each have one. */
+B3X_API int b3x_reserve_workspace(void* stream, unsigned long long config_signature);
+
+/* Free every workspace reserved on the current device (synchronises, as
+ * cudaFree does).  Later steps on those streams use the library's array. */
+B3X_API int b3x_release_workspaces(void);
+
+/* Bytes reserved for `stream` on the current device, 0 if none. */
+B3X_API size_t b3x_reserved_bytes(void* stream);
+
 /* No counterpart in the reference.  Number of kernel launches one
- * b3x_batch_step_gpu call of `count` worlds makes on `device` with its own
- * workspace (one per chunk of resident tiles; one for configurations small
+ * b3x_batch_step_gpu call of `count` worlds makes on `device` with a
+ * reserved workspace (one per chunk of resident tiles; one for configurations small
  * enough to be stepped whole in shared memory, at most 8 bodies, 8 shapes
  * and 8 contacts, which use no workspace); 0 if the configuration is
  * invalid.  For launch accounting by callers and benchmarks. */
@@ -910,9 +944,11 @@ B3X_API int b3x_scene_reset_gpu(unsigned char* out, int n, unsigned long long se
     unsigned long long step, void* stream);
 
 /* Nonzero if a step on the current device was abandoned because one of its
- * bounded waits for a bulk copy into shared memory gave up (not expected;
- * the worlds of that launch are then unspecified).  clear != 0 resets it.
- * Synchronises the device; -1 on error. */
+ * bounded waits for a bulk copy into shared memory gave up (not expected).
+ * The 32 worlds of the tile whose wait gave up are then left as they were
+ * before the call (nothing of that tile is written back); the other tiles
+ * are stepped.  clear != 0 resets it.  Synchronises the device; -1 on
+ * error. */
 B3X_API int b3x_fault_flags(int clear);
 
 /* Capacity configuration helpers (host). */

@@ -29,10 +29,13 @@ def lib_path(cfg, kind):
     return os.path.join(HERE, sub, "libb3%s_%s.so" % (kind, cfg))
 
 
-def build_oracles(quiet=True):
-    """Compile the port oracles (and the reference ones when the reference
-    checkout is present).  Returns the make exit status."""
-    out = subprocess.run(["make", "-C", HERE, "-j8"], capture_output=quiet)
+def build_oracles(quiet=True, ref_dir=None):
+    """Compile the port oracles, and the reference ones when a reference
+    checkout is given (`ref_dir`, else the PUFFYSICS_REF environment
+    variable).  Returns the make exit status."""
+    ref_dir = ref_dir or os.environ.get("PUFFYSICS_REF")
+    cmd = ["make", "-C", HERE, "-j8"] + (["REF_DIR=" + ref_dir] if ref_dir else [])
+    out = subprocess.run(cmd, capture_output=quiet)
     return out.returncode
 
 

@@ -39,7 +39,7 @@ THREAD_DEPS = THREAD_HEADERS + [os.path.join(ROOT, "include", "puffysics_b200.h"
 # name -> (bodies, shapes, contacts, joints)
 SCENE_CONFIGS = {"hover": (2, 2, 4, 1), "stack": (9, 9, 32, 1), "chain": (12, 12, 32, 10),
                  "pile": (37, 37, 128, 1), "hovertask": (2, 2, 4, 2), "default": (80, 128, 128, 32),
-                 "stacksmall": (9, 9, 4, 1), "bounce": (9, 9, 32, 1), "stackil": (9, 9, 32, 1),
+                 "stacksmall": (9, 9, 4, 1), "bounce": (9, 9, 32, 1), "capsule": (17, 17, 64, 1), "stackil": (9, 9, 32, 1),
                  "chainil": (12, 12, 32, 10), "bouncenr": (9, 9, 32, 1), "bounceilnr": (9, 9, 32, 1),
                  "hoveruf": (2, 2, 4, 1)}
 # per-thread step launchers (include/puffysics.cuh's device b3_step): name ->
@@ -47,7 +47,8 @@ SCENE_CONFIGS = {"hover": (2, 2, 4, 1), "stack": (9, 9, 32, 1), "chain": (12, 12
 # benchmark configurations and of the reference's defaults
 THREAD_CONFIGS = {"hover": (2, 2, 4, 1, 8), "stack": (9, 9, 32, 1, 8), "chain": (12, 12, 32, 10, 8),
                   "pile": (37, 37, 128, 1, 8), "hovertask": (2, 2, 4, 2, 2), "default": (80, 128, 128, 32, 2),
-                  "bounce": (9, 9, 32, 1, 8), "stackil": (9, 9, 32, 1, 8), "chainil": (12, 12, 32, 10, 8),
+                  "bounce": (9, 9, 32, 1, 8), "capsule": (17, 17, 64, 1, 8), "stackil": (9, 9, 32, 1, 8),
+                  "chainil": (12, 12, 32, 10, 8),
                   "bouncenr": (9, 9, 32, 1, 8), "bounceilnr": (9, 9, 32, 1, 8), "hoveruf": (2, 2, 4, 1, 8)}
 # the reference's mode macros of the per-thread configurations
 THREAD_MODES = {"stackil": ["-DB3_INTERLEAVE_CONTACTS"], "chainil": ["-DB3_INTERLEAVE_CONTACTS"],

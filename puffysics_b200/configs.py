@@ -6,7 +6,7 @@ counts, timestep, substeps and the world count of the configuration.
 """
 from dataclasses import dataclass
 
-SCENE_HOVER, SCENE_STACK, SCENE_CHAIN, SCENE_PILE, SCENE_BOUNCE = 1, 2, 3, 4, 5
+SCENE_HOVER, SCENE_STACK, SCENE_CHAIN, SCENE_PILE, SCENE_BOUNCE, SCENE_CAPSULE = 1, 2, 3, 4, 5, 6
 ACT_NONE, ACT_FORCE, ACT_TORQUE, ACT_LINEAR_IMPULSE, ACT_JOINT_TARGET = -1, 0, 1, 2, 3
 STEP_INTERLEAVE_CONTACTS, STEP_SKIP_RESTITUTION = 1, 2
 
@@ -54,6 +54,9 @@ CONFIGS = {
                       description="pile scene at the reference's default capacities"),
     "bounce": Config("bounce", SCENE_BOUNCE, (9, 9, 32, 1), 8, 8, 1.0 / 60.0, 4, 1024,
                      description="spheres and boxes with restitution and rolling resistance (parity coverage)"),
+    "capsule": Config("capsule", SCENE_CAPSULE, (17, 17, 64, 1), 8, 8, 1.0 / 60.0, 4, 1024,
+                      description="capsules and spheres falling into a walled bin (sphere-capsule and "
+                                  "capsule-capsule manifolds)"),
     # the reference's alternative step modes (B3_INTERLEAVE_CONTACTS,
     # B3_SKIP_RESTITUTION) on the same scenes
     "stackil": Config("stackil", SCENE_STACK, (9, 9, 32, 1), 8, 8, 1.0 / 60.0, 4, 16384,

@@ -289,7 +289,39 @@ struct Plan {
 
 static std::mutex g_mutex;
 static std::map<std::pair<int, unsigned long long>, Plan> g_plans;
-static std::map<std::tuple<int, void*, unsigned long long>, std::pair<void*, size_t>> g_workspaces;
+
+// ---- workspaces ------------------------------------------------------------------
+// A step never allocates.  Its workspace is, in order of preference:
+//  * the caller's (b3x_batch_step_gpu_ws);
+//  * the one reserved for the calling stream by b3x_reserve_workspace, an
+//    explicit set-up call (the only place the library allocates device
+//    memory), freed by b3x_release_workspaces;
+//  * the library's fixed array g_step_scratch, which every device that loads
+//    the library holds until exit.  Steps on it run as many tiles per launch
+//    as its slots hold.  Calls from different streams are ordered on the GPU
+//    through an event, so they cannot overlap on the array; a call made while
+//    its stream is being captured into a CUDA graph is ordered only by that
+//    stream (reserve a workspace for capture streams).
+struct Reserved {
+    void* ptr;
+    size_t bytes;
+};
+static std::mutex g_ws_mutex;
+static std::map<std::pair<int, void*>, Reserved> g_reserved;   // (device, stream)
+
+constexpr size_t kStepScratchBytes = 128ull << 20;
+static __device__ __align__(256) unsigned char g_step_scratch[kStepScratchBytes];
+struct FixedUse {
+    cudaEvent_t done = nullptr;   // recorded after the last launch on the array
+    void* last = nullptr;         // the stream of that launch
+    bool pending = false;         // `done` has been recorded
+};
+static std::mutex g_fixed_mutex;  // held across a call's launches on the array
+static std::map<int, FixedUse> g_fixed;   // per device
+
+// The allocation-free entry's own array (b3x_batch_step_gpu_noalloc).
+constexpr size_t kNoAllocScratchBytes = 64ull << 20;   // 64 MiB per device
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
 // Resident blocks per SM the default chunk and the shared memory budget are
 // sized for.
@@ -430,6 +462,12 @@ B3X_API size_t b3x_workspace_bytes(unsigned long long sig, int device) {
     return p.ws_bytes;
 }
 
+B3X_API size_t b3x_workspace_slot_bytes(unsigned long long sig) {
+    Layout L;
+    if (!layout_from_signature(sig, &L)) return 0;
+    return (size_t)space_from_layout(L).tile_words * sizeof(float);
+}
+
 B3X_API int b3x_step_launches(unsigned long long sig, int count, int device) {
     Layout L;
     if (!layout_from_signature(sig, &L) || count < 0) return 0;
@@ -440,8 +478,48 @@ B3X_API int b3x_step_launches(unsigned long long sig, int count, int device) {
     return (ntiles + p.chunk_tiles - 1) / p.chunk_tiles;
 }
 
+// Where a step's workspace comes from (see "workspaces" above).
+enum class WsFrom { kLibrary, kCaller, kNoAlloc };
+
+// Chunked launches on the library's fixed array, ordered after the previous
+// user of the array when that was another stream.
+static cudaError_t step_on_fixed(int dev, const B3Batch& batch, float dt, int substeps,
+        const unsigned char* active, void* stream, const Layout& L, int ji, int ri, int flags, const Plan& p) {
+    void* ws = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&ws, g_step_scratch);
+    if (e != cudaSuccess) return e;
+    const long long slots = (long long)(kStepScratchBytes / p.tile_bytes);
+    if (slots < 1) return cudaErrorMemoryAllocation;   // a reserved workspace is needed
+    const int chunk = (int)(slots < p.chunk_tiles ? slots : p.chunk_tiles);
+    std::lock_guard<std::mutex> lock(g_fixed_mutex);
+    FixedUse& f = g_fixed[dev];
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing((cudaStream_t)stream, &cs) != cudaSuccess) {
+        (void)cudaGetLastError();
+        cs = cudaStreamCaptureStatusActive;
+    }
+    const bool ordered = cs == cudaStreamCaptureStatusNone;
+    if (ordered) {
+        if (!f.done) {
+            e = cudaEventCreateWithFlags(&f.done, cudaEventDisableTiming);
+            if (e != cudaSuccess) return e;
+        }
+        if (f.pending && f.last != stream) {
+            e = cudaStreamWaitEvent((cudaStream_t)stream, f.done, 0);
+            if (e != cudaSuccess) return e;
+        }
+    }
+    e = launch_step(batch, dt, substeps, active, (cudaStream_t)stream, L, ji, ri, flags, p, ws, chunk);
+    if (e != cudaSuccess || !ordered) return e;
+    e = cudaEventRecord(f.done, (cudaStream_t)stream);
+    if (e != cudaSuccess) return e;
+    f.last = stream;
+    f.pending = true;
+    return cudaSuccess;
+}
+
 static int step_common(B3Batch batch, float dt, int substeps, const unsigned char* active, void* stream,
-        unsigned long long sig, int ji, int ri, void* ws, size_t ws_bytes, bool own_ws, int flags = 0) {
+        unsigned long long sig, int ji, int ri, WsFrom from, void* ws, size_t ws_bytes, int flags = 0) {
     Layout L;
     if (!layout_from_signature(sig, &L)) return cudaErrorInvalidValue;
     if (!batch_ok(batch, L.size) || !std::isfinite(dt) || dt < 0 || substeps < 1 || ji < 1 || ri < 1
@@ -476,20 +554,23 @@ static int step_common(B3Batch batch, float dt, int substeps, const unsigned cha
         small_step_kernel<<<groups, kLanes, p.small_smem, (cudaStream_t)stream>>>(a, p.small_stride);
         return (int)cudaGetLastError();
     }
-    if (own_ws) {
-        std::lock_guard<std::mutex> lock(g_mutex);
-        auto key = std::make_tuple(dev, stream, sig);
-        auto it = g_workspaces.find(key);
-        if (it == g_workspaces.end()) {
-            void* mem = nullptr;
-            e = cudaMalloc(&mem, p.ws_bytes);
-            if (e != cudaSuccess) return e;
-            g_workspaces[key] = {mem, p.ws_bytes};
-            ws = mem;
-        } else {
-            ws = it->second.first;
+    if (from == WsFrom::kLibrary) {
+        {
+            std::lock_guard<std::mutex> lock(g_ws_mutex);
+            auto it = g_reserved.find({dev, stream});
+            if (it != g_reserved.end() && it->second.bytes >= p.tile_bytes) {
+                ws = it->second.ptr;
+                ws_bytes = it->second.bytes;
+            }
         }
-        ws_bytes = p.ws_bytes;
+        if (ws == nullptr)
+            return step_on_fixed(dev, batch, dt, substeps, active, stream, L, ji, ri, flags, p);
+    } else if (from == WsFrom::kNoAlloc) {
+        // looked up on every call: the address is per device and per context
+        e = cudaGetSymbolAddress(&ws, g_noalloc_scratch);
+        if (e != cudaSuccess) return e;
+        ws_bytes = kNoAllocScratchBytes;
+        if (p.tile_bytes > kNoAllocScratchBytes) return cudaErrorInvalidValue;
     }
     if (ws == nullptr || ((uintptr_t)ws % 256) != 0) return cudaErrorInvalidValue;
     // A smaller caller workspace simply runs fewer tiles per launch.
@@ -501,17 +582,76 @@ static int step_common(B3Batch batch, float dt, int substeps, const unsigned cha
 
 B3X_API int b3x_batch_step_gpu(B3Batch batch, float dt, int substeps, const unsigned char* active, void* stream,
         unsigned long long sig, int ji, int ri) {
-    return step_common(batch, dt, substeps, active, stream, sig, ji, ri, nullptr, 0, true);
+    return step_common(batch, dt, substeps, active, stream, sig, ji, ri, WsFrom::kLibrary, nullptr, 0);
 }
 
 B3X_API int b3x_batch_step_gpu_flags(B3Batch batch, float dt, int substeps, const unsigned char* active,
         void* stream, unsigned long long sig, int ji, int ri, int flags) {
-    return step_common(batch, dt, substeps, active, stream, sig, ji, ri, nullptr, 0, true, flags);
+    return step_common(batch, dt, substeps, active, stream, sig, ji, ri, WsFrom::kLibrary, nullptr, 0, flags);
 }
 
 B3X_API int b3x_batch_step_gpu_ws(B3Batch batch, float dt, int substeps, const unsigned char* active, void* stream,
         unsigned long long sig, int ji, int ri, void* ws, size_t ws_bytes) {
-    return step_common(batch, dt, substeps, active, stream, sig, ji, ri, ws, ws_bytes, false);
+    return step_common(batch, dt, substeps, active, stream, sig, ji, ri, WsFrom::kCaller, ws, ws_bytes);
+}
+
+// Set-up call: a workspace for steps of this capacity configuration on
+// `stream` (current device), large enough for one launch per resident wave.
+// Grows an existing reservation of the stream (synchronising, as cudaFree
+// does); a large enough one is kept.
+B3X_API int b3x_reserve_workspace(void* stream, unsigned long long sig) {
+    Layout L;
+    if (!layout_from_signature(sig, &L)) return cudaErrorInvalidValue;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    Plan p;
+    e = make_plan(dev, sig, L, &p);
+    if (e != cudaSuccess) return e;
+    if (p.small) return cudaSuccess;   // stepped in shared memory, no workspace
+    std::lock_guard<std::mutex> lock(g_ws_mutex);
+    auto key = std::make_pair(dev, stream);
+    auto it = g_reserved.find(key);
+    if (it != g_reserved.end()) {
+        if (it->second.bytes >= p.ws_bytes) return cudaSuccess;
+        e = cudaFree(it->second.ptr);
+        g_reserved.erase(it);
+        if (e != cudaSuccess) return e;
+    }
+    void* mem = nullptr;
+    e = cudaMalloc(&mem, p.ws_bytes);
+    if (e != cudaSuccess) return e;
+    g_reserved[key] = {mem, p.ws_bytes};
+    return cudaSuccess;
+}
+
+// Frees every workspace reserved on the current device (synchronising, as
+// cudaFree does); steps on those streams fall back to the library's array.
+B3X_API int b3x_release_workspaces(void) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    cudaError_t first = cudaSuccess;
+    std::lock_guard<std::mutex> lock(g_ws_mutex);
+    for (auto it = g_reserved.begin(); it != g_reserved.end();) {
+        if (it->first.first != dev) {
+            ++it;
+            continue;
+        }
+        e = cudaFree(it->second.ptr);
+        if (e != cudaSuccess && first == cudaSuccess) first = e;
+        it = g_reserved.erase(it);
+    }
+    return first;
+}
+
+// Bytes reserved for `stream` on the current device (0 if none).
+B3X_API size_t b3x_reserved_bytes(void* stream) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+    std::lock_guard<std::mutex> lock(g_ws_mutex);
+    auto it = g_reserved.find({dev, stream});
+    return it == g_reserved.end() ? 0 : it->second.bytes;
 }
 
 B3X_API int b3x_batch_restore_gpu(B3Batch batch, const void* initial, const unsigned char* reset, void* stream,
@@ -575,54 +715,26 @@ B3X_API int b3x_batch_observe_gpu(B3Batch batch, int body, float* out, void* str
 // whose device memory is entirely owned by a framework's caching allocator or
 // a plugin host that forbids raw cudaMalloc, and real-time loops that cannot
 // afford the implicit synchronisation an allocation may bring.  For them,
-// b3x_batch_step_gpu_noalloc takes its workspace from this fixed array,
-// reserved on every device that loads the library until the process exits.
-constexpr size_t kNoAllocScratchBytes = 64ull << 20;   // 64 MiB per device
-static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
-
-static std::mutex g_noalloc_mutex;
-static std::map<int, void*> g_noalloc_ptr;   // device -> address of g_noalloc_scratch there
-
-}  // extern "C"
-
-extern "C" {
-
-// Same step as b3x_batch_step_gpu with the workspace taken from the fixed
-// 64 MiB array above; it calls no cudaMalloc, cudaFree or other allocating
-// routine.  The first call on a device looks up the array's device address
-// (cudaGetSymbolAddress, with that device current) and caches it; make that
-// first call before any stream capture.  Every call on a device shares the
-// array, and its contents are left over from the previous call (the step
-// writes every word of it that it reads, so nothing needs clearing); calls
-// whose launches overlap on the GPU (different streams, no ordering between
-// them) race on it and must not be issued.  A capacity configuration whose
-// per-CTA workspace slot exceeds 64 MiB is rejected with
-// cudaErrorInvalidValue; smaller ones run as many tiles per launch as slots
-// fit (at most the device's resident blocks), so any batch size is accepted.
+// b3x_batch_step_gpu_noalloc takes its workspace from g_noalloc_scratch, a
+// fixed 64 MiB array reserved on every device that loads the library until
+// the process exits.
+//
+// Same step as b3x_batch_step_gpu with that array as the workspace; it calls
+// no cudaMalloc, cudaFree or other allocating routine.  Every call looks up
+// the array's device address on the current device (cudaGetSymbolAddress);
+// the first call on a device also loads the library's kernels there, so make
+// it before any stream capture.  Every call on a device shares the array, and
+// its contents are left over from the previous call (the step writes every
+// word of it that it reads, so nothing needs clearing); calls whose launches
+// overlap on the GPU (different streams, no ordering between them) race on it
+// and must not be issued.  A capacity configuration whose per-CTA workspace
+// slot exceeds 64 MiB is rejected with cudaErrorInvalidValue (configurations
+// small enough to be stepped in shared memory use no workspace and are never
+// rejected); smaller ones run as many tiles per launch as slots fit (at most
+// the device's resident blocks), so any batch size is accepted.
 B3X_API int b3x_batch_step_gpu_noalloc(B3Batch batch, float dt, int substeps, const unsigned char* active,
         void* stream, unsigned long long sig, int ji, int ri) {
-    Layout L;
-    if (!layout_from_signature(sig, &L)) return cudaErrorInvalidValue;
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return e;
-    void* ptr = nullptr;
-    {
-        std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-        auto it = g_noalloc_ptr.find(dev);
-        if (it == g_noalloc_ptr.end()) {
-            e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
-            if (e != cudaSuccess) return e;
-            g_noalloc_ptr[dev] = ptr;
-        } else {
-            ptr = it->second;
-        }
-    }
-    Plan p;
-    e = make_plan(dev, sig, L, &p);
-    if (e != cudaSuccess) return e;
-    if (p.tile_bytes > kNoAllocScratchBytes) return cudaErrorInvalidValue;
-    return step_common(batch, dt, substeps, active, stream, sig, ji, ri, ptr, kNoAllocScratchBytes, false);
+    return step_common(batch, dt, substeps, active, stream, sig, ji, ri, WsFrom::kNoAlloc, nullptr, 0);
 }
 
 }  // extern "C"

@@ -54,6 +54,16 @@ def lib():
         L.b3x_batch_step_gpu_noalloc.restype = ctypes.c_int
         L.b3x_workspace_bytes.argtypes = [ctypes.c_ulonglong, ctypes.c_int]
         L.b3x_workspace_bytes.restype = ctypes.c_size_t
+        L.b3x_workspace_slot_bytes.argtypes = [ctypes.c_ulonglong]
+        L.b3x_workspace_slot_bytes.restype = ctypes.c_size_t
+        L.b3x_reserve_workspace.argtypes = [vp, ctypes.c_ulonglong]
+        L.b3x_reserve_workspace.restype = ctypes.c_int
+        L.b3x_release_workspaces.argtypes = []
+        L.b3x_release_workspaces.restype = ctypes.c_int
+        L.b3x_reserved_bytes.argtypes = [vp]
+        L.b3x_reserved_bytes.restype = ctypes.c_size_t
+        L.b3x_fault_flags.argtypes = [ctypes.c_int]
+        L.b3x_fault_flags.restype = ctypes.c_int
         L.b3x_step_launches.argtypes = [ctypes.c_ulonglong, ctypes.c_int, ctypes.c_int]
         L.b3x_step_launches.restype = ctypes.c_int
         L.b3x_batch_restore_gpu.argtypes = [B3Batch, vp, u8p, vp, ctypes.c_ulonglong]
@@ -128,7 +138,33 @@ def batch_observe_gpu(worlds, body, out, stream=None, caps=None, stride=None, of
 
 
 def workspace_bytes(caps, device=0):
+    """Workspace of one launch per resident wave (what reserve_workspace takes)."""
     return lib().b3x_workspace_bytes(layout.signature(*caps), device)
+
+
+def workspace_slot_bytes(caps):
+    """One tile's (32 worlds') workspace slot."""
+    return lib().b3x_workspace_slot_bytes(layout.signature(*caps))
+
+
+def reserve_workspace(caps, stream=None):
+    """Set-up: reserve the step's workspace for `stream` (the only device
+    allocation the library makes); later steps on that stream use it."""
+    return lib().b3x_reserve_workspace(_stream(stream), layout.signature(*caps))
+
+
+def release_workspaces():
+    """Free every workspace reserved on the current device."""
+    return lib().b3x_release_workspaces()
+
+
+def reserved_bytes(stream=None):
+    return lib().b3x_reserved_bytes(_stream(stream))
+
+
+def fault_flags(clear=False):
+    """Nonzero if a step abandoned a tile because a bounded wait gave up."""
+    return lib().b3x_fault_flags(1 if clear else 0)
 
 
 def step_launches(caps, count, device=0):

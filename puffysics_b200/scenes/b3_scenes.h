@@ -29,6 +29,7 @@
 #define B3S_CHAIN 3
 #define B3S_PILE 4
 #define B3S_BOUNCE 5
+#define B3S_CAPSULE 6
 
 /* Action kinds (same numbering as the b3x_batch_apply_gpu C-ABI). */
 #define B3S_ACT_NONE (-1)
@@ -41,6 +42,7 @@
 #define B3S_STACK_BOXES 8
 #define B3S_PILE_BOXES 16
 #define B3S_PILE_SPHERES 16
+#define B3S_CAPSULE_SHAPES 12
 
 /* splitmix64 finaliser over a combined counter. */
 B3_HD B3_INL uint64_t b3s_mix(uint64_t z) {
@@ -295,6 +297,76 @@ static inline int b3s_build_bounce(B3World* w, uint64_t seed, uint64_t index) {
     return b3_world_error(w) ? -1 : 0;
 }
 
+/* Capsules (parity coverage of the sphere-capsule and capsule-capsule
+ * manifolds, which no benchmark scene makes): ground + 4 walls around x, z in
+ * [-1, 1] + 6 capsules (radius U[0.08, 0.2], half length U[0.15, 0.35],
+ * random orientation) and 6 spheres (r U[0.1, 0.25]), densities
+ * U[500, 2000], placed without overlap (bounding spheres, seeded rejection
+ * sampling) in the 2 x 2 x 4 m region above the ground, so they fall into a
+ * tangle. */
+static inline int b3s_build_capsule(B3World* w, uint64_t seed, uint64_t index) {
+    b3_world_init(w);
+    w->gravity = b3_v(0.0f, -9.81f, 0.0f);
+    b3s_ground(w);
+    B3ShapeDef wsd = b3_default_shape();
+    wsd.friction = 0.5f;
+    for (int k = 0; k < 4; k++) {
+        B3BodyDef wd = b3_default_body();
+        float s = (k & 1) ? 1.0f : -1.0f;
+        wd.position = (k < 2) ? b3_v(1.2f * s, 1.5f, 0.0f) : b3_v(0.0f, 1.5f, 1.2f * s);
+        int b = b3_create_body(w, &wd);
+        b3_create_box(w, b, (k < 2) ? b3_v(0.2f, 1.5f, 1.4f) : b3_v(1.4f, 1.5f, 0.2f), &wsd);
+    }
+    float px[B3S_CAPSULE_SHAPES], py[B3S_CAPSULE_SHAPES], pz[B3S_CAPSULE_SHAPES], pr[B3S_CAPSULE_SHAPES];
+    for (int i = 0; i < B3S_CAPSULE_SHAPES; i++) {
+        int is_capsule = (i & 1) == 0;
+        uint64_t base = 300u + 32u * (uint64_t)i;
+        float rad = is_capsule ? b3s_uniform(seed, index, 0, base + 0, 0.08f, 0.2f)
+                               : b3s_uniform(seed, index, 0, base + 0, 0.1f, 0.25f);
+        float half_len = b3s_uniform(seed, index, 0, base + 1, 0.15f, 0.35f);
+        float bound = is_capsule ? rad + half_len : rad;
+        float x = 0.0f, y = 0.0f, z = 0.0f;
+        int placed = 0;
+        for (int t = 0; t < 48 && !placed; t++) {
+            uint64_t sl = 20000u + 1000u * (uint64_t)i + 3u * (uint64_t)t;
+            x = b3s_uniform(seed, index, 0, sl + 0, -1.0f + bound, 1.0f - bound);
+            y = b3s_uniform(seed, index, 0, sl + 1, bound + 0.05f, 4.0f - bound);
+            z = b3s_uniform(seed, index, 0, sl + 2, -1.0f + bound, 1.0f - bound);
+            placed = 1;
+            for (int k = 0; k < i; k++) {
+                float dx = x - px[k], dy = y - py[k], dz = z - pz[k];
+                float rr = bound + pr[k] + 0.01f;
+                if (dx * dx + dy * dy + dz * dz < rr * rr) { placed = 0; break; }
+            }
+        }
+        if (!placed) {            /* deterministic fallback: a column above the bin */
+            x = -0.5f + 1.0f * (float)(i % 2);
+            z = -0.5f + 1.0f * (float)((i / 2) % 2);
+            y = 5.0f + 0.8f * (float)i;
+        }
+        px[i] = x; py[i] = y; pz[i] = z; pr[i] = bound;
+        B3BodyDef bd = b3_default_body();
+        bd.type = B3_DYNAMIC;
+        bd.position = b3_v(x, y, z);
+        if (is_capsule) {
+            B3Vec3 axis = b3_v(b3s_uniform(seed, index, 0, base + 2, -1.0f, 1.0f),
+                b3s_uniform(seed, index, 0, base + 3, -1.0f, 1.0f),
+                b3s_uniform(seed, index, 0, base + 4, -1.0f, 1.0f));
+            bd.rotation = b3_q_axis_angle(axis, b3s_uniform(seed, index, 0, base + 5, 0.0f, B3_PI));
+        }
+        bd.ang_vel = b3_v(b3s_uniform(seed, index, 0, base + 6, -2.0f, 2.0f),
+            b3s_uniform(seed, index, 0, base + 7, -2.0f, 2.0f), b3s_uniform(seed, index, 0, base + 8, -2.0f, 2.0f));
+        int b = b3_create_body(w, &bd);
+        B3ShapeDef sd = b3_default_shape();
+        sd.density = b3s_uniform(seed, index, 0, base + 9, 500.0f, 2000.0f);
+        sd.friction = b3s_uniform(seed, index, 0, base + 10, 0.3f, 0.9f);
+        if (is_capsule) b3_create_capsule(w, b, half_len, rad, &sd);
+        else b3_create_sphere(w, b, b3_v(0.0f, 0.0f, 0.0f), rad, &sd);
+        b3_finalize_mass(w, b);
+    }
+    return b3_world_error(w) ? -1 : 0;
+}
+
 static inline int b3s_build(B3World* w, int kind, uint64_t seed, uint64_t index) {
     switch (kind) {
     case B3S_HOVER: return b3s_build_hover(w, seed, index);
@@ -302,6 +374,7 @@ static inline int b3s_build(B3World* w, int kind, uint64_t seed, uint64_t index)
     case B3S_CHAIN: return b3s_build_chain(w, seed, index);
     case B3S_PILE: return b3s_build_pile(w, seed, index);
     case B3S_BOUNCE: return b3s_build_bounce(w, seed, index);
+    case B3S_CAPSULE: return b3s_build_capsule(w, seed, index);
     default: return -1;
     }
 }

@@ -1,6 +1,6 @@
 """Generate the golden fixtures of tests/golden/ from the reference itself.
 
-    python tests/golden/gen_golden.py          # needs oracle/_ref (make -C oracle)
+    python tests/golden/gen_golden.py [name ...]   # needs oracle/_ref (make -C oracle REF_DIR=...)
 
 The reference ships no tests or golden vectors for its stepping path, so the
 fixtures are outputs of the reference's own CPU code (b3_batch_step from
@@ -29,7 +29,7 @@ from puffysics_b200 import layout  # noqa: E402
 from puffysics_b200.configs import CONFIGS  # noqa: E402
 
 SEED = 20261201
-WORLDS = {"hover": 8, "stack": 8, "chain": 8, "pile": 4, "bounce": 8}
+WORLDS = {"hover": 8, "stack": 8, "chain": 8, "pile": 4, "bounce": 8, "capsule": 8}
 
 
 def rollout(name):
@@ -124,7 +124,10 @@ def kats():
 
 
 if __name__ == "__main__":
-    for name in WORLDS:
-        rollout(name)
-    c = kats()
-    print("kats:", len(c), "with contact:", int((c > 0).sum()))
+    names = sys.argv[1:] or list(WORLDS) + ["kats"]
+    for name in names:
+        if name == "kats":
+            c = kats()
+            print("kats:", len(c), "with contact:", int((c > 0).sum()))
+        else:
+            rollout(name)

@@ -4,7 +4,7 @@ loader (mjcf.h, compiled from the reference checkout against this library's
 include/), as AoS B3World bytes at the default capacities: the bind pose and
 the "crouch" keyframe.
 
-    python tests/golden/gen_mjcf.py        # needs the reference checkout
+    python tests/golden/gen_mjcf.py     # PUFFYSICS_REF=<checkout> to name it
 """
 import os
 import subprocess
@@ -16,7 +16,11 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
 FIX = os.path.join(ROOT, "tests", "fixtures", "mjcf")
-REF_DIR = os.environ.get("PUFFYSICS_REF", "/root/reference")
+sys.path.insert(0, ROOT)
+import __graft_entry__  # noqa: E402
+
+# the reference checkout: PUFFYSICS_REF, else where the build driver mounts it
+REF_DIR = os.environ.get("PUFFYSICS_REF") or __graft_entry__.REFERENCE_MOUNT
 
 
 def spawn(include_dirs, keys, workdir):
@@ -32,7 +36,7 @@ def spawn(include_dirs, keys, workdir):
 
 
 def main():
-    if not os.path.exists(os.path.join(REF_DIR, "mjcf.h")):
+    if not REF_DIR or not os.path.exists(os.path.join(REF_DIR, "mjcf.h")):
         sys.exit("reference checkout not found at %s" % REF_DIR)
     with tempfile.TemporaryDirectory() as d:
         worlds = spawn([os.path.join(ROOT, "include"), REF_DIR], ["-", "crouch"], d)

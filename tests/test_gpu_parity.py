@@ -22,7 +22,7 @@ from puffysics_b200.configs import CONFIGS, SCENE_CHAIN
 
 pytestmark = pytest.mark.gpu
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
-EXACT = ["hover", "stack", "pile", "bounce"]
+EXACT = ["hover", "stack", "pile", "bounce", "capsule"]
 
 
 def check_step(name, got, want, step):
@@ -37,7 +37,7 @@ def check_step(name, got, want, step):
     assert ok, "state error %.3g at step %d" % (err, step)
 
 
-@pytest.mark.parametrize("name", ["hover", "stack", "chain", "pile", "bounce"])
+@pytest.mark.parametrize("name", ["hover", "stack", "chain", "pile", "bounce", "capsule"])
 def test_golden_fixtures(name, gpu_lib):
     cfg = CONFIGS[name]
     g = np.load(os.path.join(GOLDEN, name + ".npz"))
@@ -51,7 +51,7 @@ def test_golden_fixtures(name, gpu_lib):
             check_step(name, p.got(), g["step60"], 60)
 
 
-@pytest.mark.parametrize("name", ["hover", "stack", "chain", "pile", "default", "stacksmall", "bounce"])
+@pytest.mark.parametrize("name", ["hover", "stack", "chain", "pile", "default", "stacksmall", "bounce", "capsule"])
 def test_rollout_matches_oracle_every_step(name, oracle_kind, gpu_lib):
     cfg = CONFIGS[name]
     o = orc.Oracle(name, oracle_kind)

@@ -14,7 +14,7 @@ from puffysics_b200 import layout
 from puffysics_b200.configs import CONFIGS
 
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
-ROLLOUT_CONFIGS = ["hover", "stack", "chain", "pile", "bounce"]
+ROLLOUT_CONFIGS = ["hover", "stack", "chain", "pile", "bounce", "capsule"]
 have_ref = orc.available("stack", "ref")
 needs_ref = pytest.mark.skipif(not have_ref, reason="reference build (oracle/_ref) not present")
 
