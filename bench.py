@@ -12,9 +12,13 @@ world count per GPU; `scaleout` keeps 1,048,576 worlds in total).  No
 collective runs inside the timed region.  Rank 0 prints one JSON line.
 
 value    device-resident: actions generated on the device, worlds resident in
-         HBM; per-step CUDA events on the launching stream, L2 flushed between
-         timed steps (outside the events) unless the world array is larger
-         than twice L2, max over ranks.
+         HBM -- by default as structure-of-arrays columns across worlds
+         (b3x_engine_*, bound once from the seeded AoS worlds before the
+         timing; --path aos: the drop-in b3x_batch_step_gpu on the caller's
+         AoS worlds, which the line also reports as `aos_path`); per-step
+         CUDA events on the launching stream, L2 flushed between timed steps
+         (outside the events) unless the world array is larger than twice
+         L2, max over ranks.
 e2e      through the C-ABI with host buffers: each step copies that step's
          actions from pinned host memory, applies them, steps, gathers one
          observation per world and copies it back, then synchronises.
@@ -80,6 +84,8 @@ def parse_args():
     ap.add_argument("--no-graph", action="store_true", help="e2e with direct calls instead of a CUDA graph")
     ap.add_argument("--no-per-thread-path", action="store_true",
                     help="skip the timing of the per-thread device b3_step after the main measurement")
+    ap.add_argument("--path", default="aos", choices=["columns", "aos"],
+                    help="world layout of the headline: resident columns (b3x_engine_*) or the AoS drop-in")
     ap.add_argument("--extra-configs", default="pile",
                     help="comma list of configurations measured after the main one on one GPU ('' for none)")
     return ap.parse_args()
@@ -462,11 +468,14 @@ class ClockSampler:
                 "reasons": sorted(self.reasons - {"gpu_idle"}), "samples": len(self.samples)}
 
 
-def run_ours(name, args, rank, world, local, dev, barrier):
+def run_ours(name, args, rank, world, local, dev, barrier, path="columns"):
     """This library's arm on one configuration: the device-resident timed
     steps (the headline's K after W warm-up steps, or a configuration's
     window from its seeded state), then the end-to-end steps through host
-    buffers.  Returns the per-rank timings and the final state's counts."""
+    buffers.  path "columns": the worlds resident as structure-of-arrays
+    columns (b3x_engine_*: bound once from the seeded AoS worlds, outside the
+    timing); "aos": the drop-in b3x_batch_step_gpu on the AoS worlds.
+    Returns the per-rank timings and the final state's counts."""
     import torch
     from puffysics_b200 import engine, layout, shard, synth
     cfg = CONFIGS[name]
@@ -480,6 +489,9 @@ def run_ours(name, args, rank, world, local, dev, barrier):
     worlds = torch.from_numpy(scenes.build(per_gpu, SEED, first=first)).to(dev)
     seeded = worlds.clone() if (cfg.reset_fraction or window) else None
     stream = torch.cuda.current_stream(dev)
+    cols = engine.Columns(caps, per_gpu, device=dev) if path == "columns" else None
+    if cols is not None:
+        assert cols.bind(worlds, stream=stream) == 0
     # set-up: the step's workspace for this stream (the step itself never allocates)
     assert engine.reserve_workspace(caps, stream) == 0
     vals = torch.zeros((per_gpu, max(nv, 1)), dtype=torch.float32, device=dev)
@@ -497,21 +509,33 @@ def run_ours(name, args, rank, world, local, dev, barrier):
         launches = 0
         if cfg.reset_fraction:
             assert synth.reset_gpu(reset, per_gpu, SEED, first, s, stream) == 0
-            assert engine.batch_restore_gpu(worlds, seeded, reset, stream, caps) == 0
+            if cols is not None:
+                assert cols.bind(seeded, select=reset, stream=stream) == 0
+            else:
+                assert engine.batch_restore_gpu(worlds, seeded, reset, stream, caps) == 0
             launches += 2
         if nv:
             assert synth.actions_gpu(vals, per_gpu, cfg.scene, SEED, first, s, stream) == nv
-            assert engine.batch_apply_gpu(worlds, kind, aidx, vals, None, stream, caps) == 0
+            if cols is not None:
+                assert cols.apply(kind, aidx, vals, stream=stream) == 0
+            else:
+                assert engine.batch_apply_gpu(worlds, kind, aidx, vals, None, stream, caps) == 0
             launches += 2
         if ev is not None:
             ev.record(stream)
-        rc = engine.batch_step_gpu(worlds, cfg.dt, cfg.substeps, None, stream, caps, cfg.joint_iters,
-                                   cfg.relax_iters, flags=cfg.flags)
+        if cols is not None:
+            rc = cols.step(cfg.dt, cfg.substeps, None, stream, cfg.joint_iters, cfg.relax_iters, flags=cfg.flags)
+        else:
+            rc = engine.batch_step_gpu(worlds, cfg.dt, cfg.substeps, None, stream, caps, cfg.joint_iters,
+                                       cfg.relax_iters, flags=cfg.flags)
         assert rc == 0, rc
         return launches + step_launches
 
     def restart():
-        worlds.copy_(seeded)
+        if cols is not None:
+            assert cols.bind(seeded, stream=stream) == 0
+        else:
+            worlds.copy_(seeded)
         step_no[0] = 0
 
     for _ in range(max(args.warmup, 3)):
@@ -540,6 +564,8 @@ def run_ours(name, args, rank, world, local, dev, barrier):
     k_local = sum(evk[i].elapsed_time(ev1[i]) for i in range(K))
 
     # diagnostics of the final state (outside the timed region)
+    if cols is not None:
+        assert cols.sync_to_aos(worlds, stream=stream) == 0
     final = worlds.cpu().numpy()
     stats = shard.world_stats(final, caps)
     v = layout.view(final, caps)
@@ -563,10 +589,17 @@ def run_ours(name, args, rank, world, local, dev, barrier):
         from pinned host memory, apply, step, observe, observations back."""
         if nv:
             vals.copy_(h_act[:, :nv], non_blocking=True)
-            assert engine.batch_apply_gpu(worlds, kind, aidx, vals, None, s, caps) == 0
-        assert engine.batch_step_gpu(worlds, cfg.dt, cfg.substeps, None, s, caps, cfg.joint_iters,
-                                     cfg.relax_iters, flags=cfg.flags) == 0
-        assert engine.batch_observe_gpu(worlds, obs_body, d_obs, s, caps) == 0
+            if cols is not None:
+                assert cols.apply(kind, aidx, vals, stream=s) == 0
+            else:
+                assert engine.batch_apply_gpu(worlds, kind, aidx, vals, None, s, caps) == 0
+        if cols is not None:
+            assert cols.step(cfg.dt, cfg.substeps, None, s, cfg.joint_iters, cfg.relax_iters, flags=cfg.flags) == 0
+            assert cols.observe(obs_body, d_obs, stream=s) == 0
+        else:
+            assert engine.batch_step_gpu(worlds, cfg.dt, cfg.substeps, None, s, caps, cfg.joint_iters,
+                                         cfg.relax_iters, flags=cfg.flags) == 0
+            assert engine.batch_observe_gpu(worlds, obs_body, d_obs, s, caps) == 0
         h_obs.copy_(d_obs, non_blocking=True)
 
     # The step's calls are captured once in a CUDA graph and replayed every
@@ -611,7 +644,15 @@ def run_ours(name, args, rank, world, local, dev, barrier):
     e2e_local = e_start.elapsed_time(e_end)
     del graph
     assert engine.release_workspaces() == 0
-    return {"name": name, "cfg": cfg, "per_gpu": per_gpu, "K": K, "E": E, "window": window,
+    if path == "columns":
+        e2e_path = ("pinned H2D actions -> b3x_engine_apply -> b3x_engine_step -> b3x_engine_observe -> D2H "
+                    "(%s), stream synchronised every step" % e2e_mode)
+    else:
+        e2e_path = ("pinned H2D actions -> b3x_batch_apply_gpu -> b3x_batch_step_gpu -> b3x_batch_observe_gpu -> "
+                    "D2H (%s), stream synchronised every step" % e2e_mode)
+    del cols
+    return {"name": name, "cfg": cfg, "per_gpu": per_gpu, "K": K, "E": E, "window": window, "path": path,
+            "e2e_path": e2e_path,
             "t": t_local, "k": k_local, "e2e": e2e_local, "launches": launches, "step_launches": step_launches,
             "stats": stats, "counts": counts, "clocks": sampler.summary(),
             "bi": per_gpu * nv * 4, "bo": per_gpu * 13 * 4, "e2e_mode": e2e_mode}
@@ -718,7 +759,7 @@ def main():
         if world > 1:
             dist.barrier()
 
-    res = run_ours(args.config, args, rank, world, local, dev, barrier)
+    res = run_ours(args.config, args, rank, world, local, dev, barrier, path=args.path)
 
     # reductions (after timing): max time over ranks, summed diagnostics
     t_max, k_max, e_max = res["t"], res["k"], res["e2e"]
@@ -728,49 +769,50 @@ def main():
         t_max, k_max, e_max = tt.tolist()
     tot = shard.reduce_stats(res["stats"], device=dev)
 
+    def measured(r, t, k, e, nranks):
+        """The measurement fields of one run (t, k, e: max-over-ranks ms)."""
+        total = r["per_gpu"] * nranks
+        return {"value": total * r["K"] / (t / 1e3), "unit": UNIT, "steps": r["K"], "warmup": args.warmup,
+                "ms_per_step": t / r["K"], "world_path": r["path"],
+                "roofline": roofline(r, k / r["K"] / 1e3, local),
+                "e2e": {"value": total * r["E"] / (e / 1e3), "unit": UNIT, "h2d_bytes_per_step": r["bi"],
+                        "d2h_bytes_per_step": r["bo"], "steps": r["E"], "path": r["e2e_path"]},
+                "gpu_launches": r["launches"], "clocks": r["clocks"]}
+
+    other = "aos" if args.path == "columns" else "columns"
     if rank == 0:
-        K, E, per_gpu = res["K"], res["E"], res["per_gpu"]
-        total = per_gpu * world
-        line = {"metric": METRIC, "value": total * K / (t_max / 1e3), "unit": UNIT, "n_gpus": world, "steps": K,
-                "warmup": args.warmup, "ms_per_step": t_max / K, "higher_is_better": True,
+        per_gpu = res["per_gpu"]
+        stream = torch.cuda.current_stream(dev)
+        line = {"metric": METRIC, "n_gpus": world,
+                "higher_is_better": True,
                 "scaling": "strong" if args.config == "scaleout" else "weak", "vs_baseline": None, "dtype": "f32",
                 "data": "synthetic: seeded scenes (puffysics_b200/scenes/b3_scenes.h), on-device actions",
-                "config": workload_config(res["cfg"], args.config, per_gpu, world),
-                "roofline": roofline(res, k_max / K / 1e3, local),
-                "e2e": {"value": total * E / (e_max / 1e3), "unit": UNIT, "h2d_bytes_per_step": res["bi"],
-                        "d2h_bytes_per_step": res["bo"], "steps": E,
-                        "path": "pinned H2D actions -> b3x_batch_apply_gpu -> b3x_batch_step_gpu -> "
-                                "b3x_batch_observe_gpu -> D2H (%s), stream synchronised every step"
-                                % res["e2e_mode"]},
-                "gpu_launches": res["launches"],
-                "clocks": res["clocks"],
-                "diagnostics": {"worlds": int(tot[0]), "contacts": int(tot[1]), "overflowed_worlds": int(tot[2]),
-                                "dropped_contacts": int(tot[3]), "mean_contacts": res["counts"]["contact"],
-                                "mean_bodies": res["counts"]["body"]}}
-        stream = torch.cuda.current_stream(dev)
+                "config": workload_config(res["cfg"], args.config, per_gpu, world)}
+        line.update(measured(res, t_max, k_max, e_max, world))
+        line["diagnostics"] = {"worlds": int(tot[0]), "contacts": int(tot[1]), "overflowed_worlds": int(tot[2]),
+                               "dropped_contacts": int(tot[3]), "mean_contacts": res["counts"]["contact"],
+                               "mean_bodies": res["counts"]["body"]}
+        if world == 1:
+            r2 = run_ours(args.config, args, 0, 1, local, dev, barrier, path=other)
+            line[other + "_path"] = measured(r2, r2["t"], r2["k"], r2["e2e"], 1)
         if world == 1 and not args.no_per_thread_path:
-            line["per_thread_path"] = thread_path_run(res["cfg"], per_gpu, K, args.warmup, stream,
+            line["per_thread_path"] = thread_path_run(res["cfg"], per_gpu, res["K"], args.warmup, stream,
                                                       window=res["window"])
             if res["cfg"].name == "hover":
-                line["fused_env"] = fused_env_run(K, args.warmup, stream)
+                line["fused_env"] = fused_env_run(res["K"], args.warmup, stream)
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_reference_run(res["cfg"], steps=None, warmup=2, budget_s=args.cpu_seconds,
                                                      window=res["window"])
         if extras:
             line["configs"] = {}
             for name in extras:
-                r = run_ours(name, args, 0, 1, local, dev, barrier)
-                sub = {"value": r["per_gpu"] * r["K"] / (r["t"] / 1e3), "unit": UNIT, "steps": r["K"],
-                       "warmup": args.warmup, "ms_per_step": r["t"] / r["K"],
-                       "config": workload_config(r["cfg"], name, r["per_gpu"], 1),
-                       "roofline": roofline(r, r["k"] / r["K"] / 1e3, local),
-                       "e2e": {"value": r["per_gpu"] * r["E"] / (r["e2e"] / 1e3), "unit": UNIT,
-                               "h2d_bytes_per_step": r["bi"], "d2h_bytes_per_step": r["bo"], "steps": r["E"],
-                               "path": "as the main line's e2e (%s)" % r["e2e_mode"]},
-                       "gpu_launches": r["launches"], "clocks": r["clocks"],
-                       "diagnostics": {"mean_contacts": r["counts"]["contact"], "mean_bodies": r["counts"]["body"],
-                                       "overflowed_worlds": int(r["stats"][2]),
-                                       "dropped_contacts": int(r["stats"][3])}}
+                r = run_ours(name, args, 0, 1, local, dev, barrier, path=args.path)
+                sub = {"config": workload_config(r["cfg"], name, r["per_gpu"], 1)}
+                sub.update(measured(r, r["t"], r["k"], r["e2e"], 1))
+                sub["diagnostics"] = {"mean_contacts": r["counts"]["contact"], "mean_bodies": r["counts"]["body"],
+                                      "overflowed_worlds": int(r["stats"][2]), "dropped_contacts": int(r["stats"][3])}
+                r2 = run_ours(name, args, 0, 1, local, dev, barrier, path=other)
+                sub[other + "_path"] = measured(r2, r2["t"], r2["k"], r2["e2e"], 1)
                 if not args.no_per_thread_path:
                     sub["per_thread_path"] = thread_path_run(r["cfg"], r["per_gpu"], r["K"], args.warmup, stream,
                                                              window=r["window"])

@@ -934,6 +934,45 @@ B3X_API int b3x_batch_apply_gpu(B3Batch batch, int kind, int index, const float*
 B3X_API int b3x_batch_observe_gpu(B3Batch batch, int body, float* out, void* stream,
     unsigned long long config_signature);
 
+/* ---------------------------------------------------------------------------
+ * Resident world columns.  No counterpart in the reference, whose worlds
+ * always stay in the caller's AoS array (src/puffysics/02_types.inl:306-332,
+ * stepped in place by b3_batch.cuh:63-68).  Here the worlds of a batch can
+ * live in HBM as structure-of-arrays across worlds ("columns"): word w of the
+ * B3World of world i at engine[((i / 32) * W + w) * 32 + i % 32] (4-byte
+ * words, W = sizeof(B3World) / 4), so one word of 32 consecutive worlds is
+ * one 128-byte line.  Steps on the columns read and write only them: no AoS
+ * row gathers or scatters.  The memory is the caller's (device, 16-byte
+ * aligned, b3x_engine_bytes long); world i of the columns is world i of the
+ * batches bound to or synced from them.  Results are the same bytes as
+ * b3x_batch_step_gpu on the AoS worlds.
+ * ------------------------------------------------------------------------- */
+
+/* Bytes of the columns of `count` worlds (whole tiles of 32); 0 if invalid. */
+B3X_API size_t b3x_engine_bytes(unsigned long long config_signature, int count);
+
+/* Copy the selected worlds (NULL = all; nonzero byte = selected) of the AoS
+ * batch into the columns; the batch must hold `count` worlds (stride and
+ * embedding offset as in b3_batch_step_gpu).  Binding the initial snapshots
+ * with a reset mask is the columns' b3_batch_restore_gpu. */
+B3X_API int b3x_engine_bind(void* engine, int count, B3Batch worlds, const unsigned char* select,
+    void* stream, unsigned long long config_signature);
+
+/* Copy the selected worlds of the columns back into the AoS batch. */
+B3X_API int b3x_engine_sync_to_aos(const void* engine, int count, B3Batch worlds, const unsigned char* select,
+    void* stream, unsigned long long config_signature);
+
+/* b3x_batch_step_gpu_flags on the columns: same validation, no-op cases,
+ * mask, modes, workspace (reservation or the library's array) and results. */
+B3X_API int b3x_engine_step(void* engine, int count, float dt, int substeps, const unsigned char* active,
+    void* stream, unsigned long long config_signature, int joint_iters, int relax_iters, int flags);
+
+/* b3x_batch_apply_gpu and b3x_batch_observe_gpu on the columns. */
+B3X_API int b3x_engine_apply(void* engine, int count, int kind, int index, const float* values,
+    int values_per_world, const unsigned char* active, void* stream, unsigned long long config_signature);
+B3X_API int b3x_engine_observe(const void* engine, int count, int body, float* out, void* stream,
+    unsigned long long config_signature);
+
 /* Device generators of the benchmark inputs (seeded scenes of
  * puffysics_b200/scenes/b3_scenes.h): per-step action values of world
  * first+i (returns values per world, 0 when the scene has none, -1 on error)

@@ -196,6 +196,11 @@ struct Args {
     Space SP;
     float* ws;     // workspace slot of the launch's first tile
     int tile0;     // first tile of this launch
+    // Resident world columns (the b3x_engine_* entry points): word w of the
+    // B3World of tile-lane l of tile t at res[(t * resW + w) * 32 + l]; null
+    // when the step reads and writes the caller's AoS worlds.
+    float* res;
+    unsigned long long resW;   // words of one B3World
 };
 
 // ---- column accessors (c points at an item's column of one lane) -----------

@@ -70,6 +70,12 @@ B3X_HDI float* world_words_w(const Args& a, int wi) {
     return reinterpret_cast<float*>(a.data + (size_t)wi * a.stride + a.offset);
 }
 B3X_HDI float* slot_of(const Args& a, int bt) { return a.ws + (size_t)bt * a.SP.tile_words; }
+// Word w of the B3World of lane l of tile `tile` in the resident world
+// columns ([tile][word][lane]: one word of a tile's 32 worlds is one
+// contiguous 128-byte line).
+B3X_HDI float* res_word(const Args& a, int tile, size_t w, int l) {
+    return a.res + ((size_t)tile * a.resW + w) * kLanes + l;
+}
 
 // Index of the n-th set bit of a window mask (two words).
 B3X_HDI int nth_bit64(const uint32_t* m, int n) {
@@ -81,10 +87,17 @@ B3X_HDI int nth_bit64(const uint32_t* m, int n) {
 
 // Header of each world (warp w: worlds w, w+4, ...; lane = header word),
 // copied asynchronously so all of a thread's loads are in flight at once.
+template <bool kRes>
 B3X_HD void c_header(const Args& a, int tile, CollideShared& sh, int t) {
     const int w = t >> 5, i = t & 31;
     if (t == 0) sh.maxnb = sh.maxns = sh.maxold = sh.maxnj = 0;
-    if (i < NHW) {
+    if constexpr (kRes) {
+        // resident columns: consecutive threads read one word of consecutive worlds
+        for (int idx = t; idx < NHW * kLanes; idx += kCta) {
+            const int l = idx & 31, f = idx >> 5;
+            if (tile * kLanes + l < a.count) async_copy4_world(&sh.u.hdr[l][f], res_word(a, tile, f, l));
+        }
+    } else if (i < NHW) {
         for (int l = w; l < kLanes; l += kCtaWarps) {
             int wi = tile * kLanes + l;
             if (wi < a.count) async_copy4_world(&sh.u.hdr[l][i], world_words(a, wi) + i);
@@ -145,10 +158,21 @@ B3X_HD void c_record(const Args& a, int tile, float* slot, CollideShared& sh, in
 // field of consecutive worlds hit distinct banks).  Warps take whole worlds:
 // the items of a world are one contiguous region of the caller's struct
 // array, copied with consecutive words on consecutive lanes.
-template <int PER>
+template <int PER, bool kRes>
 B3X_HD void c_gather_group(const Args& a, int tile, CollideShared& sh, const int* count, int l0, int G, int M,
         int RS, unsigned base, int dst, int t) {
     const int w = t >> 5, i = t & 31;
+    if constexpr (kRes) {
+        // resident columns: consecutive threads take one word of consecutive worlds
+        for (int idx = t; idx < M * PER * G; idx += kCta) {
+            const int g = idx % G, r = idx / G, k = r / PER, c = r - k * PER;
+            const int l = l0 + g;
+            if (k < count[l])
+                async_copy4_world(sh.u.flat + dst + (g * M + k) * RS + c,
+                                  res_word(a, tile, base / 4 + (size_t)k * PER + c, l));
+        }
+        return;
+    }
     for (int g = w; g < G; g += kCtaWarps) {
         const int l = l0 + g;
         const int words = count[l] * PER;
@@ -168,8 +192,19 @@ B3X_HDI int old_word(int i) {
         : i == OTWI ? WTWI : i < OFEAT ? WRI + (i - ORI) : i < ONI ? PW(i - OFEAT, QFEAT) : PW(i - ONI, QNI);
 }
 
+template <bool kRes>
 B3X_HD void c_gather_old(const Args& a, int tile, CollideShared& sh, int l0, int G, int M, int dst, int t) {
     const int w = t >> 5, i = t & 31;
+    if constexpr (kRes) {
+        for (int idx = t; idx < M * NOF * G; idx += kCta) {
+            const int g = idx % G, r = idx / G, k = r / NOF, f = r - k * NOF;
+            const int l = l0 + g;
+            if (k < sh.oldn[l])
+                async_copy4_world(sh.u.flat + dst + (g * M + k) * NOF + f,
+                                  res_word(a, tile, a.L.contact_off / 4 + (size_t)k * NCW + old_word(f), l));
+        }
+        return;
+    }
     if (i >= NOF) return;
     const int word = old_word(i);
     for (int g = w; g < G; g += kCtaWarps) {
@@ -318,8 +353,19 @@ B3X_HDI float* joint_row(CollideShared& sh, int qq, int l) { return sh.u.flat + 
 
 // Joints [q0, q0 + Q) of every world, each world's run of rows in one
 // contiguous copy (warp w: worlds w, w+4, ...).
+template <bool kRes>
 B3X_HD void c_joint_gather(const Args& a, int tile, CollideShared& sh, int q0, int Q, int t) {
     const int w = t >> 5, i = t & 31;
+    if constexpr (kRes) {
+        for (int idx = t; idx < Q * NVW * kLanes; idx += kCta) {
+            const int l = idx & 31, r = idx >> 5, qq = r / NVW, c = r - qq * NVW;
+            if (q0 + qq < sh.nj[l])
+                async_copy4_world(joint_row(sh, qq, l) + c,
+                                  res_word(a, tile, a.L.joint_off / 4 + (size_t)(q0 + qq) * NVW + c, l));
+        }
+        async_wait();
+        return;
+    }
     for (int l = w; l < kLanes; l += kCtaWarps) {
         const int n = (sh.nj[l] < q0 + Q ? sh.nj[l] : q0 + Q) - q0;
         if (n <= 0) continue;
@@ -814,11 +860,11 @@ B3X_HD void c_finish(const Args& a, float* slot, CollideShared& sh, int l) {
 }
 
 // The collide phases of tile `bt` of the launch.
-template <class X>
+template <bool kRes, class X>
 B3X_HD void collide_tile(X& x, const Args& a, int bt, CollideShared& sh) {
     float* slot = slot_of(a, bt);
     const int tile = a.tile0 + bt;
-    x.each([&](int t) { c_header(a, tile, sh, t); });
+    x.each([&](int t) { c_header<kRes>(a, tile, sh, t); });
     x.each([&](int t) { if (t < kLanes) c_record(a, tile, slot, sh, t); });
     {
         // bodies: whole body arrays of G worlds per round
@@ -827,7 +873,7 @@ B3X_HD void collide_tile(X& x, const Args& a, int bt, CollideShared& sh) {
         for (int l0 = 0; l0 < kLanes; l0 += G) {
             const int Gr = kLanes - l0 < G ? kLanes - l0 : G;
             x.each([&](int t) {
-                c_gather_group<NYW>(a, tile, sh, sh.nb, l0, Gr, M, RS, B3X_WORLD_HEADER_BYTES, 0, t);
+                c_gather_group<NYW, kRes>(a, tile, sh, sh.nb, l0, Gr, M, RS, B3X_WORLD_HEADER_BYTES, 0, t);
                 async_wait();
             });
             x.each([&](int t) {
@@ -847,8 +893,8 @@ B3X_HD void collide_tile(X& x, const Args& a, int bt, CollideShared& sh) {
             const int Gr = kLanes - l0 < Gs ? kLanes - l0 : Gs;
             const int odst = Gr * per_s;
             x.each([&](int t) {
-                c_gather_group<NXW>(a, tile, sh, sh.ns, l0, Gr, Ms, NXW + 1, a.L.shape_off, 0, t);
-                if (joint_round) c_gather_old(a, tile, sh, l0, Gr, Mo, odst, t);
+                c_gather_group<NXW, kRes>(a, tile, sh, sh.ns, l0, Gr, Ms, NXW + 1, a.L.shape_off, 0, t);
+                if (joint_round) c_gather_old<kRes>(a, tile, sh, l0, Gr, Mo, odst, t);
                 async_wait();
             });
             x.each([&](int t) {
@@ -870,7 +916,7 @@ B3X_HD void collide_tile(X& x, const Args& a, int bt, CollideShared& sh) {
             for (int l0 = 0; l0 < kLanes; l0 += Go) {
                 const int Gr = kLanes - l0 < Go ? kLanes - l0 : Go;
                 x.each([&](int t) {
-                    c_gather_old(a, tile, sh, l0, Gr, Mo, 0, t);
+                    c_gather_old<kRes>(a, tile, sh, l0, Gr, Mo, 0, t);
                     async_wait();
                 });
                 x.each([&](int t) {
@@ -886,7 +932,7 @@ B3X_HD void collide_tile(X& x, const Args& a, int bt, CollideShared& sh) {
     }
     for (int q0 = 0; q0 < sh.maxnj; q0 += kJointRound) {
         const int Q = sh.maxnj - q0 < kJointRound ? sh.maxnj - q0 : kJointRound;
-        x.each([&](int t) { c_joint_gather(a, tile, sh, q0, Q, t); });
+        x.each([&](int t) { c_joint_gather<kRes>(a, tile, sh, q0, Q, t); });
         x.each([&](int t) {
             for (int j = t; j < Q * kLanes; j += kCta) c_joint(a, slot, sh, q0 + (j >> 5), j & 31, joint_row(sh, j >> 5, j & 31));
         });
@@ -942,8 +988,19 @@ B3X_HDI float* out_row(OutShared& sh, int l, int kk, int K, int RS) {
 
 // Bodies [k0, k0 + K) of every world: each world's run of B3Body rows,
 // gathered from the caller's array (rows stay untouched until written back).
+template <bool kRes>
 B3X_HD void o_body_gather(const Args& a, int tile, OutShared& sh, int k0, int K, int t) {
     const int w = t >> 5, i = t & 31;
+    if constexpr (kRes) {
+        for (int idx = t; idx < K * NYW * kLanes; idx += kCta) {
+            const int l = idx & 31, r = idx >> 5, kk = r / NYW, c = r - kk * NYW;
+            if (k0 + kk < sh.nb[l])
+                async_copy4_world(out_row(sh, l, kk, K, kRow) + c,
+                                  res_word(a, tile, B3X_WORLD_HEADER_BYTES / 4 + (size_t)(k0 + kk) * NYW + c, l));
+        }
+        async_wait();
+        return;
+    }
     for (int l = w; l < kLanes; l += kCtaWarps) {
         const int n = (sh.nb[l] < k0 + K ? sh.nb[l] : k0 + K) - k0;
         if (n <= 0) continue;
@@ -998,8 +1055,18 @@ B3X_HD void o_bodies(const Args& a, float* slot, OutShared& sh, int k0, int K, i
     }
 }
 
+template <bool kRes>
 B3X_HD void o_body_write(const Args& a, int tile, OutShared& sh, int k0, int K, int t) {
     const int w = t >> 5, i = t & 31;
+    if constexpr (kRes) {
+        for (int idx = t; idx < K * NYW * kLanes; idx += kCta) {
+            const int l = idx & 31, r = idx >> 5, kk = r / NYW, c = r - kk * NYW;
+            if (k0 + kk < sh.nb[l])
+                store_world(res_word(a, tile, B3X_WORLD_HEADER_BYTES / 4 + (size_t)(k0 + kk) * NYW + c, l),
+                            out_row(sh, l, kk, K, kRow)[c]);
+        }
+        return;
+    }
     for (int l = w; l < kLanes; l += kCtaWarps) {
         const int n = (sh.nb[l] < k0 + K ? sh.nb[l] : k0 + K) - k0;
         if (n <= 0) continue;
@@ -1054,8 +1121,20 @@ B3X_HD void o_contacts(const Args& a, float* slot, OutShared& sh, int k0, int K,
 // Contacts [k0, k0 + K) of every world.  Point slots past a contact's point
 // count keep their previous bytes, as in the reference (b3_contact_from_mani
 // writes only the manifold's points).
+template <bool kRes>
 B3X_HD void o_contact_write(const Args& a, int tile, OutShared& sh, int k0, int K, int t) {
     const int w = t >> 5, i = t & 31;
+    if constexpr (kRes) {
+        for (int idx = t; idx < K * NCW * kLanes; idx += kCta) {
+            const int l = idx & 31, r = idx >> 5, kk = r / NCW, c = r - kk * NCW;
+            if (k0 + kk >= sh.n[l]) continue;
+            const float* row = out_row(sh, l, kk, K, NCW);
+            const int hi = WP + clampi(b3x_f2i(row[WCNT]), 0, B3_MAX_MANIFOLD) * NQW;
+            if (c < hi || c >= WCA)
+                store_world(res_word(a, tile, a.L.contact_off / 4 + (size_t)(k0 + kk) * NCW + c, l), row[c]);
+        }
+        return;
+    }
     for (int l = w; l < kLanes; l += kCtaWarps) {
         const int n = (sh.n[l] < k0 + K ? sh.n[l] : k0 + K) - k0;
         if (n <= 0) continue;
@@ -1100,8 +1179,18 @@ B3X_HD void o_joints(const Args& a, float* slot, OutShared& sh, int q0, int K, i
 
 // Joints [q0, q0 + K) of every world; invalid joints (body index out of
 // range) are left as they were.
+template <bool kRes>
 B3X_HD void o_joint_write(const Args& a, int tile, float* slot, OutShared& sh, int q0, int K, int t) {
     const int w = t >> 5, i = t & 31;
+    if constexpr (kRes) {
+        for (int idx = t; idx < K * NVW * kLanes; idx += kCta) {
+            const int l = idx & 31, r = idx >> 5, kk = r / NVW, c = r - kk * NVW;
+            if (q0 + kk >= sh.nj[l] || !ldi(item(slot + a.SP.joint, q0 + kk, NJF) + l, JOK)) continue;
+            store_world(res_word(a, tile, a.L.joint_off / 4 + (size_t)(q0 + kk) * NVW + c, l),
+                        out_row(sh, l, kk, K, NVW)[c]);
+        }
+        return;
+    }
     for (int l = w; l < kLanes; l += kCtaWarps) {
         const int n = (sh.nj[l] < q0 + K ? sh.nj[l] : q0 + K) - q0;
         if (n <= 0) continue;
@@ -1123,16 +1212,23 @@ B3X_HDI int out_items(int count, int row_floats) {
     return (count + rounds - 1) / rounds;
 }
 
+template <bool kRes>
 B3X_HD void o_header(const Args& a, int tile, float* slot, OutShared& sh, int l) {
     if (!sh.live[l]) return;
     const float* rec = slot + a.SP.rec + l;
+    if constexpr (kRes) {
+        *res_word(a, tile, HNC, l) = COL(rec, RN);
+        *res_word(a, tile, HOVC, l) = COL(rec, ROVF);
+        *res_word(a, tile, HDROP, l) = COL(rec, RDROP);
+        return;
+    }
     float* hw = world_words_w(a, tile * kLanes + l);
     hw[HNC] = COL(rec, RN);
     hw[HOVC] = COL(rec, ROVF);
     hw[HDROP] = COL(rec, RDROP);
 }
 
-template <class X>
+template <bool kRes, class X>
 B3X_HD void out_tile(X& x, const Args& a, int bt, OutShared& sh) {
     float* slot = slot_of(a, bt);
     const int tile = a.tile0 + bt;
@@ -1141,9 +1237,9 @@ B3X_HD void out_tile(X& x, const Args& a, int bt, OutShared& sh) {
     {
         const int K = out_items(sh.maxnb, kRow);
         for (int k0 = 0; k0 < sh.maxnb; k0 += K) {
-            x.each([&](int t) { o_body_gather(a, tile, sh, k0, K, t); });
+            x.each([&](int t) { o_body_gather<kRes>(a, tile, sh, k0, K, t); });
             x.each([&](int t) { o_bodies(a, slot, sh, k0, K, t); });
-            x.each([&](int t) { o_body_write(a, tile, sh, k0, K, t); });
+            x.each([&](int t) { o_body_write<kRes>(a, tile, sh, k0, K, t); });
         }
     }
     {
@@ -1154,7 +1250,7 @@ B3X_HD void out_tile(X& x, const Args& a, int bt, OutShared& sh) {
             // fill below overwrites
             x.each([&](int t) { o_stage(item(slot + a.SP.cont, k0, kCI), sh, Kr, kCI, NCW, t); });
             x.each([&](int t) { o_contacts(a, slot, sh, k0, Kr, t); });
-            x.each([&](int t) { o_contact_write(a, tile, sh, k0, Kr, t); });
+            x.each([&](int t) { o_contact_write<kRes>(a, tile, sh, k0, Kr, t); });
         }
     }
     {
@@ -1163,10 +1259,10 @@ B3X_HD void out_tile(X& x, const Args& a, int bt, OutShared& sh) {
             const int Kr = sh.maxnj - q0 < K ? sh.maxnj - q0 : K;
             x.each([&](int t) { o_stage(item(slot + a.SP.jimg, q0, NVW), sh, Kr, NVW, NVW, t); });
             x.each([&](int t) { o_joints(a, slot, sh, q0, Kr, t); });
-            x.each([&](int t) { o_joint_write(a, tile, slot, sh, q0, Kr, t); });
+            x.each([&](int t) { o_joint_write<kRes>(a, tile, slot, sh, q0, Kr, t); });
         }
     }
-    x.each([&](int t) { if (t < kLanes) o_header(a, tile, slot, sh, t); });
+    x.each([&](int t) { if (t < kLanes) o_header<kRes>(a, tile, slot, sh, t); });
 }
 
 }  // namespace b3x

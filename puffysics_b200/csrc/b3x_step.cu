@@ -121,13 +121,14 @@ __device__ bool solve_tile(const Args& a, unsigned char* smem_raw) {
 }
 
 // One block per tile: collide (all warps), solve (warp 0), write-back (all
-// warps).
-template <int kBody, bool kInterleave = false>
+// warps).  kRes: the worlds are the resident world columns (a.res) instead
+// of the caller's AoS array.
+template <int kBody, bool kInterleave = false, bool kRes = false>
 __global__ void __launch_bounds__(kCta, 4) step_kernel(Args a) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     __shared__ int solved;
     DevExec x;
-    collide_tile(x, a, blockIdx.x, *reinterpret_cast<CollideShared*>(smem_raw));
+    collide_tile<kRes>(x, a, blockIdx.x, *reinterpret_cast<CollideShared*>(smem_raw));
     // the solve's bulk copies (async proxy) read workspace data every thread
     // wrote and reuse shared memory the collide phase accessed, both through
     // the generic proxy: each thread orders its accesses before the barrier
@@ -139,7 +140,7 @@ __global__ void __launch_bounds__(kCta, 4) step_kernel(Args a) {
     }
     __syncthreads();
     if (!solved) return;
-    out_tile(x, a, blockIdx.x, *reinterpret_cast<OutShared*>(smem_raw));
+    out_tile<kRes>(x, a, blockIdx.x, *reinterpret_cast<OutShared*>(smem_raw));
 }
 
 // ---- small worlds -----------------------------------------------------------------
@@ -171,6 +172,8 @@ __device__ __forceinline__ void async_copy8(void* dst, const void* src) {
 // warp spread the worlds over more SMs and let several warps of one SM share
 // the instruction fetches of this long per-world program.
 constexpr int kSmallWorlds = SMALL_WORLDS_PER_BLOCK;
+static_assert(kLanes % kSmallWorlds == 0, "a small-world group lies inside one tile");
+template <bool kRes = false>
 __global__ void __launch_bounds__(kLanes) small_step_kernel(Args a, unsigned stride_words) {
     extern __shared__ __align__(16) unsigned char small_smem[];
     uint64_t* sw = reinterpret_cast<uint64_t*>(small_smem);
@@ -183,11 +186,26 @@ __global__ void __launch_bounds__(kLanes) small_step_kernel(Args a, unsigned str
     auto world_ptr = [&](int l) {
         return reinterpret_cast<uint64_t*>(a.data + (size_t)(first + l) * a.stride + a.offset);
     };
-    for (int l = 0; l < kSmallWorlds; l++) {
-        if (!((live_mask >> l) & 1u)) continue;
-        const uint64_t* src = world_ptr(l);
-        uint64_t* dst = sw + (size_t)l * stride_words;
-        for (unsigned idx = lane; idx < words; idx += kLanes) async_copy8(dst + idx, src + idx);
+    // resident columns: the group's worlds are lanes [lt, lt + kSmallWorlds)
+    // of one tile; thread t moves 4-byte word t / kSmallWorlds (+ 4 per round)
+    // of group world t % kSmallWorlds, so each round reads or writes four
+    // 32-byte runs
+    const int tile = (int)(first / kLanes), lt = (int)(first % kLanes);
+    const int rg = lane % kSmallWorlds, rw = lane / kSmallWorlds;
+    constexpr int kRoundWords = kLanes / kSmallWorlds;
+    if constexpr (kRes) {
+        if ((live_mask >> rg) & 1u) {
+            float* dst = reinterpret_cast<float*>(sw + (size_t)rg * stride_words);
+            for (unsigned w = rw; w < 2 * words; w += kRoundWords)
+                async_copy4_world(dst + w, res_word(a, tile, w, lt + rg));
+        }
+    } else {
+        for (int l = 0; l < kSmallWorlds; l++) {
+            if (!((live_mask >> l) & 1u)) continue;
+            const uint64_t* src = world_ptr(l);
+            uint64_t* dst = sw + (size_t)l * stride_words;
+            for (unsigned idx = lane; idx < words; idx += kLanes) async_copy8(dst + idx, src + idx);
+        }
     }
     asm volatile("cp.async.wait_all;" ::: "memory");
     __syncwarp();
@@ -206,6 +224,13 @@ __global__ void __launch_bounds__(kLanes) small_step_kernel(Args a, unsigned str
         one::step_view(v, a.dt, a.substeps, a.joint_iters, a.relax_iters, a.flags);
     }
     __syncwarp();
+    if constexpr (kRes) {
+        if ((live_mask >> rg) & 1u) {
+            const float* src = reinterpret_cast<const float*>(sw + (size_t)rg * stride_words);
+            for (unsigned w = rw; w < 2 * words; w += kRoundWords) store_world(res_word(a, tile, w, lt + rg), src[w]);
+        }
+        return;
+    }
     for (int l = 0; l < kSmallWorlds; l++) {
         if (!((live_mask >> l) & 1u)) continue;
         uint64_t* dst = world_ptr(l);
@@ -228,50 +253,144 @@ __global__ void restore_kernel(unsigned char* data, unsigned long long stride, u
     }
 }
 
+// A world's 4-byte words, in the caller's AoS array or in the resident
+// columns (word w of lane l of a tile at base[w * 32]).
+struct AosAt {
+    unsigned char* base;
+    __device__ __forceinline__ float& operator()(size_t w) const { return reinterpret_cast<float*>(base)[w]; }
+};
+struct ColAt {
+    float* base;
+    __device__ __forceinline__ float& operator()(size_t w) const { return base[w * kLanes]; }
+};
+__device__ __forceinline__ AosAt aos_at(unsigned char* data, unsigned long long stride, unsigned long long offset,
+        int wi) {
+    return {data + (size_t)wi * stride + offset};
+}
+__device__ __forceinline__ ColAt col_at(float* res, unsigned long long W, int wi) {
+    return {res + (size_t)(wi / kLanes) * W * kLanes + (wi % kLanes)};
+}
+
+// Actions of one world (b3_apply_force / b3_apply_torque /
+// b3_apply_linear_impulse, 09_step.inl:132-146, and the spring target of
+// b3_joint_set_spring) on its words.
+template <class At>
+__device__ void apply_world(const At& w, const Layout& L, int kind, int index, const float* v, int vpw) {
+    if (kind == B3X_ACTION_JOINT_TARGET) {
+        const int nj = clampi(b3x_f2i(w(HNJ)), 0, L.J);
+        for (int k = 0; k < vpw; k++)
+            if (index + k >= 0 && index + k < nj)
+                w(L.joint_off / 4 + (size_t)(index + k) * NVW + VTA) = b3_clamp(v[k], -B3_PI, B3_PI);
+        return;
+    }
+    const int nb = clampi(b3x_f2i(w(HNB)), 0, L.B);
+    for (int k = 0; 3 * k + 2 < vpw; k++) {
+        const int bi = index + k;
+        if (bi < 0 || bi >= nb) continue;
+        const size_t b = B3X_WORLD_HEADER_BYTES / 4 + (size_t)bi * NYW;
+        const float x[3] = {v[3 * k], v[3 * k + 1], v[3 * k + 2]};
+        if (kind == B3X_ACTION_FORCE) {
+            for (int c = 0; c < 3; c++) w(b + YF + c) = w(b + YF + c) + x[c];
+        } else if (kind == B3X_ACTION_TORQUE) {
+            for (int c = 0; c < 3; c++) w(b + YT + c) = w(b + YT + c) + x[c];
+        } else if (b3x_f2i(w(b + YTYPE)) == B3_DYNAMIC) {
+            const float im = w(b + YIM);
+            for (int c = 0; c < 3; c++) w(b + YLV + c) = w(b + YLV + c) + im * x[c];
+        }
+    }
+}
+
 __global__ void apply_kernel(unsigned char* data, unsigned long long stride, unsigned long long offset, int count,
         Layout L, int kind, int index, const float* values, int vpw, const unsigned char* active) {
     int wi = blockIdx.x * blockDim.x + threadIdx.x;
     if (wi >= count || (active && !active[wi])) return;
-    unsigned char* wp = data + (size_t)wi * stride + offset;
-    const Header* hd = reinterpret_cast<const Header*>(wp);
-    const float* v = values + (size_t)wi * vpw;
-    if (kind == B3X_ACTION_JOINT_TARGET) {
-        B3Joint* joints = reinterpret_cast<B3Joint*>(wp + L.joint_off);
-        int nj = clampi(hd->joint_count, 0, L.J);
-        for (int k = 0; k < vpw; k++)
-            if (index + k >= 0 && index + k < nj) joints[index + k].target_angle = b3_clamp(v[k], -B3_PI, B3_PI);
-        return;
-    }
-    B3Body* bodies = reinterpret_cast<B3Body*>(wp + B3X_WORLD_HEADER_BYTES);
-    int nb = clampi(hd->body_count, 0, L.B);
-    for (int k = 0; 3 * k + 2 < vpw; k++) {
-        int bi = index + k;
-        if (bi < 0 || bi >= nb) continue;
-        B3Body* b = &bodies[bi];
-        B3Vec3 x = b3_v(v[3 * k], v[3 * k + 1], v[3 * k + 2]);
-        if (kind == B3X_ACTION_FORCE) b->force = b3_add(b->force, x);
-        else if (kind == B3X_ACTION_TORQUE) b->torque = b3_add(b->torque, x);
-        else if (b->type == B3_DYNAMIC) b->lin_vel = b3_madd(b->lin_vel, b->inv_mass, x);
-    }
+    apply_world(aos_at(data, stride, offset, wi), L, kind, index, values + (size_t)wi * vpw, vpw);
 }
 
-// One thread per world: position, rotation, lin_vel, ang_vel of one body.
+__global__ void apply_columns_kernel(float* res, unsigned long long W, int count, Layout L, int kind, int index,
+        const float* values, int vpw, const unsigned char* active) {
+    int wi = blockIdx.x * blockDim.x + threadIdx.x;
+    if (wi >= count || (active && !active[wi])) return;
+    apply_world(col_at(res, W, wi), L, kind, index, values + (size_t)wi * vpw, vpw);
+}
+
+// Position, rotation (x y z s), lin_vel, ang_vel of one body (NaN past the
+// world's bodies).
+template <class At>
+__device__ void observe_world(const At& w, int body, float* o) {
+    if (body < 0 || body >= b3x_f2i(w(HNB))) {
+        for (int k = 0; k < 13; k++) o[k] = NAN;
+        return;
+    }
+    const size_t b = B3X_WORLD_HEADER_BYTES / 4 + (size_t)body * NYW;
+    for (int k = 0; k < 7; k++) o[k] = w(b + YPOS + k);    // position, rotation
+    for (int k = 0; k < 3; k++) o[7 + k] = w(b + YLV + k);
+    for (int k = 0; k < 3; k++) o[10 + k] = w(b + YAV + k);
+}
+
+// One thread per world.
 __global__ void observe_kernel(const unsigned char* data, unsigned long long stride, unsigned long long offset,
         int count, int body, float* out) {
     int wi = blockIdx.x * blockDim.x + threadIdx.x;
     if (wi >= count) return;
-    const unsigned char* wp = data + (size_t)wi * stride + offset;
-    const Header* hd = reinterpret_cast<const Header*>(wp);
-    float* o = out + (size_t)wi * 13;
-    if (body < 0 || body >= hd->body_count) {
-        for (int k = 0; k < 13; k++) o[k] = NAN;
-        return;
+    observe_world(aos_at(const_cast<unsigned char*>(data), stride, offset, wi), body, out + (size_t)wi * 13);
+}
+
+__global__ void observe_columns_kernel(const float* res, unsigned long long W, int count, int body, float* out) {
+    int wi = blockIdx.x * blockDim.x + threadIdx.x;
+    if (wi >= count) return;
+    observe_world(col_at(const_cast<float*>(res), W, wi), body, out + (size_t)wi * 13);
+}
+
+// ---- resident world columns: transposes between the AoS worlds and the
+// columns, one block per tile, kTrChunk words of its 32 worlds per round
+// through shared memory (AoS side: consecutive lanes read or write
+// consecutive words of one world; column side: one word of the 32 worlds,
+// one 128-byte line).  Only selected worlds move; a tile without any is
+// skipped.
+constexpr int kTrChunk = 64;
+template <bool kIn>
+__global__ void __launch_bounds__(kCta) columns_kernel(float* res, unsigned long long W, unsigned char* data,
+        unsigned long long stride, unsigned long long offset, int count, const unsigned char* select) {
+    __shared__ float buf[kLanes][kTrChunk + 1];
+    __shared__ unsigned sel;
+    const int tile = blockIdx.x, t = threadIdx.x;
+    if (t < kLanes) {
+        const int wi = tile * kLanes + t;
+        const unsigned m = __ballot_sync(0xffffffffu, wi < count && (!select || select[wi]));
+        if (t == 0) sel = m;
     }
-    const B3Body* b = reinterpret_cast<const B3Body*>(wp + B3X_WORLD_HEADER_BYTES) + body;
-    o[0] = b->position.x; o[1] = b->position.y; o[2] = b->position.z;
-    o[3] = b->rotation.v.x; o[4] = b->rotation.v.y; o[5] = b->rotation.v.z; o[6] = b->rotation.s;
-    o[7] = b->lin_vel.x; o[8] = b->lin_vel.y; o[9] = b->lin_vel.z;
-    o[10] = b->ang_vel.x; o[11] = b->ang_vel.y; o[12] = b->ang_vel.z;
+    __syncthreads();
+    const unsigned m = sel;
+    if (m == 0) return;
+    for (unsigned long long w0 = 0; w0 < W; w0 += kTrChunk) {
+        const int n = W - w0 < (unsigned long long)kTrChunk ? (int)(W - w0) : kTrChunk;
+        if (kIn) {
+            for (int l = t >> 5; l < kLanes; l += kCtaWarps) {
+                if (!((m >> l) & 1u)) continue;
+                const float* src = reinterpret_cast<const float*>(data + (size_t)(tile * kLanes + l) * stride
+                                                                  + offset) + w0;
+                for (int i = t & 31; i < n; i += kLanes) buf[l][i] = src[i];
+            }
+            __syncthreads();
+            for (int idx = t; idx < n * kLanes; idx += kCta) {
+                const int l = idx & 31, i = idx >> 5;
+                if ((m >> l) & 1u) res[((size_t)tile * W + w0 + i) * kLanes + l] = buf[l][i];
+            }
+        } else {
+            for (int idx = t; idx < n * kLanes; idx += kCta) {
+                const int l = idx & 31, i = idx >> 5;
+                if ((m >> l) & 1u) buf[l][i] = res[((size_t)tile * W + w0 + i) * kLanes + l];
+            }
+            __syncthreads();
+            for (int l = t >> 5; l < kLanes; l += kCtaWarps) {
+                if (!((m >> l) & 1u)) continue;
+                float* dst = reinterpret_cast<float*>(data + (size_t)(tile * kLanes + l) * stride + offset) + w0;
+                for (int i = t & 31; i < n; i += kLanes) dst[i] = buf[l][i];
+            }
+        }
+        __syncthreads();
+    }
 }
 
 // ---- host side --------------------------------------------------------------
@@ -373,7 +492,11 @@ static cudaError_t make_plan(int dev, unsigned long long sig, const Layout& L, P
     if (p.smem_bytes > (size_t)cap) return cudaErrorInvalidValue;
     for (auto fn : {step_kernel<kBodyNone>, step_kernel<kBodyVel>, step_kernel<kBodyState>, step_kernel<kBodyAll>,
                     step_kernel<kBodyNone, true>, step_kernel<kBodyVel, true>, step_kernel<kBodyState, true>,
-                    step_kernel<kBodyAll, true>}) {
+                    step_kernel<kBodyAll, true>,
+                    step_kernel<kBodyNone, false, true>, step_kernel<kBodyVel, false, true>,
+                    step_kernel<kBodyState, false, true>, step_kernel<kBodyAll, false, true>,
+                    step_kernel<kBodyNone, true, true>, step_kernel<kBodyVel, true, true>,
+                    step_kernel<kBodyState, true, true>, step_kernel<kBodyAll, true, true>}) {
         e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, cap);
         if (e != cudaSuccess) return e;
     }
@@ -384,7 +507,11 @@ static cudaError_t make_plan(int dev, unsigned long long sig, const Layout& L, P
     p.small = L.B <= kSmallB && L.S <= kSmallS && L.C <= kSmallC && p.small_smem <= kSmallSmemMax
               && p.small_smem <= (size_t)optin;
     if (p.small) {
-        e = cudaFuncSetAttribute(small_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.small_smem);
+        e = cudaFuncSetAttribute(small_step_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)p.small_smem);
+        if (e != cudaSuccess) return e;
+        e = cudaFuncSetAttribute(small_step_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)p.small_smem);
         if (e != cudaSuccess) return e;
     }
     g_plans[{dev, sig}] = p;
@@ -403,14 +530,24 @@ static bool aligned8(const B3Batch& b) {
     return (((uintptr_t)b.data + b.world_offset) % 8 == 0) && (b.stride % 8 == 0);
 }
 
-// The step over chunks of `chunk` tiles, one step_kernel launch per chunk.
-static cudaError_t launch_step(const B3Batch& batch, float dt, int substeps, const unsigned char* active,
-        cudaStream_t stream, const Layout& L, int ji, int ri, int flags, const Plan& p, void* ws, int chunk) {
+// The worlds a step runs on: the caller's AoS batch, or resident world
+// columns (res != null, the b3x_engine_* entry points).
+struct Worlds {
+    unsigned char* data;
+    size_t stride, offset;
+    int count;
+    float* res;
+};
+
+static Worlds aos_worlds(const B3Batch& b) { return {(unsigned char*)b.data, b.stride, b.world_offset, b.count, nullptr}; }
+
+static Args step_args(const Worlds& w, float dt, int substeps, const unsigned char* active, const Layout& L, int ji,
+        int ri, int flags, const Plan& p) {
     Args a;
-    a.data = (unsigned char*)batch.data;
-    a.stride = batch.stride;
-    a.offset = batch.world_offset;
-    a.count = batch.count;
+    a.data = w.data;
+    a.stride = w.stride;
+    a.offset = w.offset;
+    a.count = w.count;
     a.active = active;
     a.dt = dt;
     a.substeps = substeps;
@@ -419,22 +556,33 @@ static cudaError_t launch_step(const B3Batch& batch, float dt, int substeps, con
     a.flags = flags;
     a.L = L;
     a.SP = p.SP;
+    a.ws = nullptr;
+    a.tile0 = 0;
+    a.res = w.res;
+    a.resW = L.size / 4;
+    return a;
+}
+
+template <bool kI, bool kR>
+static void launch_tiles(const Plan& p, int nt, cudaStream_t stream, const Args& a) {
+    if (p.body == kBodyAll) step_kernel<kBodyAll, kI, kR><<<nt, kCta, p.smem_bytes, stream>>>(a);
+    else if (p.body == kBodyState) step_kernel<kBodyState, kI, kR><<<nt, kCta, p.smem_bytes, stream>>>(a);
+    else if (p.body == kBodyVel) step_kernel<kBodyVel, kI, kR><<<nt, kCta, p.smem_bytes, stream>>>(a);
+    else step_kernel<kBodyNone, kI, kR><<<nt, kCta, p.smem_bytes, stream>>>(a);
+}
+
+// The step over chunks of `chunk` tiles, one step_kernel launch per chunk.
+static cudaError_t launch_step(const Worlds& w, float dt, int substeps, const unsigned char* active,
+        cudaStream_t stream, const Layout& L, int ji, int ri, int flags, const Plan& p, void* ws, int chunk) {
+    Args a = step_args(w, dt, substeps, active, L, ji, ri, flags, p);
     a.ws = (float*)ws;
-    const int ntiles = (batch.count + kLanes - 1) / kLanes;
+    const bool il = (flags & kStepInterleaveContacts) != 0, res = w.res != nullptr;
+    const int ntiles = (w.count + kLanes - 1) / kLanes;
     for (int t0 = 0; t0 < ntiles; t0 += chunk) {
         const int nt = ntiles - t0 < chunk ? ntiles - t0 : chunk;
         a.tile0 = t0;
-        if (flags & kStepInterleaveContacts) {
-            if (p.body == kBodyAll) step_kernel<kBodyAll, true><<<nt, kCta, p.smem_bytes, stream>>>(a);
-            else if (p.body == kBodyState) step_kernel<kBodyState, true><<<nt, kCta, p.smem_bytes, stream>>>(a);
-            else if (p.body == kBodyVel) step_kernel<kBodyVel, true><<<nt, kCta, p.smem_bytes, stream>>>(a);
-            else step_kernel<kBodyNone, true><<<nt, kCta, p.smem_bytes, stream>>>(a);
-        } else {
-            if (p.body == kBodyAll) step_kernel<kBodyAll><<<nt, kCta, p.smem_bytes, stream>>>(a);
-            else if (p.body == kBodyState) step_kernel<kBodyState><<<nt, kCta, p.smem_bytes, stream>>>(a);
-            else if (p.body == kBodyVel) step_kernel<kBodyVel><<<nt, kCta, p.smem_bytes, stream>>>(a);
-            else step_kernel<kBodyNone><<<nt, kCta, p.smem_bytes, stream>>>(a);
-        }
+        if (il) res ? launch_tiles<true, true>(p, nt, stream, a) : launch_tiles<true, false>(p, nt, stream, a);
+        else res ? launch_tiles<false, true>(p, nt, stream, a) : launch_tiles<false, false>(p, nt, stream, a);
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     }
@@ -483,7 +631,7 @@ enum class WsFrom { kLibrary, kCaller, kNoAlloc };
 
 // Chunked launches on the library's fixed array, ordered after the previous
 // user of the array when that was another stream.
-static cudaError_t step_on_fixed(int dev, const B3Batch& batch, float dt, int substeps,
+static cudaError_t step_on_fixed(int dev, const Worlds& batch, float dt, int substeps,
         const unsigned char* active, void* stream, const Layout& L, int ji, int ri, int flags, const Plan& p) {
     void* ws = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&ws, g_step_scratch);
@@ -518,15 +666,10 @@ static cudaError_t step_on_fixed(int dev, const B3Batch& batch, float dt, int su
     return cudaSuccess;
 }
 
-static int step_common(B3Batch batch, float dt, int substeps, const unsigned char* active, void* stream,
-        unsigned long long sig, int ji, int ri, WsFrom from, void* ws, size_t ws_bytes, int flags = 0) {
-    Layout L;
-    if (!layout_from_signature(sig, &L)) return cudaErrorInvalidValue;
-    if (!batch_ok(batch, L.size) || !std::isfinite(dt) || dt < 0 || substeps < 1 || ji < 1 || ri < 1
-            || (flags & ~(kStepInterleaveContacts | kStepSkipRestitution)) != 0)
-        return cudaErrorInvalidValue;
-    if (batch.count == 0 || dt == 0) return cudaSuccess;
-    if (!aligned8(batch)) return cudaErrorInvalidValue;
+// The step of validated worlds: the small-world kernel, or the tile kernel on
+// the workspace `from` names.
+static int run_step(const Worlds& w, float dt, int substeps, const unsigned char* active, void* stream,
+        unsigned long long sig, const Layout& L, int ji, int ri, WsFrom from, void* ws, size_t ws_bytes, int flags) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
@@ -535,23 +678,10 @@ static int step_common(B3Batch batch, float dt, int substeps, const unsigned cha
     if (e != cudaSuccess) return e;
     if (p.small) {
         // no workspace: the worlds are stepped in shared memory
-        Args a;
-        a.data = (unsigned char*)batch.data;
-        a.stride = batch.stride;
-        a.offset = batch.world_offset;
-        a.count = batch.count;
-        a.active = active;
-        a.dt = dt;
-        a.substeps = substeps;
-        a.joint_iters = ji;
-        a.relax_iters = ri;
-        a.flags = flags;
-        a.L = L;
-        a.SP = p.SP;
-        a.ws = nullptr;
-        a.tile0 = 0;
-        const unsigned groups = (unsigned)((batch.count + kSmallWorlds - 1) / kSmallWorlds);
-        small_step_kernel<<<groups, kLanes, p.small_smem, (cudaStream_t)stream>>>(a, p.small_stride);
+        Args a = step_args(w, dt, substeps, active, L, ji, ri, flags, p);
+        const unsigned groups = (unsigned)((w.count + kSmallWorlds - 1) / kSmallWorlds);
+        if (w.res) small_step_kernel<true><<<groups, kLanes, p.small_smem, (cudaStream_t)stream>>>(a, p.small_stride);
+        else small_step_kernel<false><<<groups, kLanes, p.small_smem, (cudaStream_t)stream>>>(a, p.small_stride);
         return (int)cudaGetLastError();
     }
     if (from == WsFrom::kLibrary) {
@@ -564,7 +694,7 @@ static int step_common(B3Batch batch, float dt, int substeps, const unsigned cha
             }
         }
         if (ws == nullptr)
-            return step_on_fixed(dev, batch, dt, substeps, active, stream, L, ji, ri, flags, p);
+            return step_on_fixed(dev, w, dt, substeps, active, stream, L, ji, ri, flags, p);
     } else if (from == WsFrom::kNoAlloc) {
         // looked up on every call: the address is per device and per context
         e = cudaGetSymbolAddress(&ws, g_noalloc_scratch);
@@ -577,7 +707,22 @@ static int step_common(B3Batch batch, float dt, int substeps, const unsigned cha
     long long slots = (long long)(ws_bytes / p.tile_bytes);
     if (slots < 1) return cudaErrorInvalidValue;
     int chunk = (int)(slots < p.chunk_tiles ? slots : p.chunk_tiles);
-    return launch_step(batch, dt, substeps, active, (cudaStream_t)stream, L, ji, ri, flags, p, ws, chunk);
+    return launch_step(w, dt, substeps, active, (cudaStream_t)stream, L, ji, ri, flags, p, ws, chunk);
+}
+
+static bool step_params_ok(float dt, int substeps, int ji, int ri, int flags) {
+    return std::isfinite(dt) && dt >= 0 && substeps >= 1 && ji >= 1 && ri >= 1
+        && (flags & ~(kStepInterleaveContacts | kStepSkipRestitution)) == 0;
+}
+
+static int step_common(B3Batch batch, float dt, int substeps, const unsigned char* active, void* stream,
+        unsigned long long sig, int ji, int ri, WsFrom from, void* ws, size_t ws_bytes, int flags = 0) {
+    Layout L;
+    if (!layout_from_signature(sig, &L)) return cudaErrorInvalidValue;
+    if (!batch_ok(batch, L.size) || !step_params_ok(dt, substeps, ji, ri, flags)) return cudaErrorInvalidValue;
+    if (batch.count == 0 || dt == 0) return cudaSuccess;
+    if (!aligned8(batch)) return cudaErrorInvalidValue;
+    return run_step(aos_worlds(batch), dt, substeps, active, stream, sig, L, ji, ri, from, ws, ws_bytes, flags);
 }
 
 B3X_API int b3x_batch_step_gpu(B3Batch batch, float dt, int substeps, const unsigned char* active, void* stream,
@@ -707,6 +852,85 @@ B3X_API int b3x_batch_observe_gpu(B3Batch batch, int body, float* out, void* str
     if (!aligned8(batch)) return cudaErrorInvalidValue;
     observe_kernel<<<(batch.count + 127) / 128, 128, 0, (cudaStream_t)stream>>>((const unsigned char*)batch.data,
         batch.stride, batch.world_offset, batch.count, body, out);
+    return cudaGetLastError();
+}
+
+// ---- resident world columns (b3x_engine_*) ----------------------------------------
+// The worlds live in HBM as structure-of-arrays across worlds: word w of the
+// B3World of world i at engine[((i / 32) * W + w) * 32 + i % 32], W =
+// sizeof(B3World) / 4.  Steps read and write these columns (one word of a
+// tile's 32 worlds is one 128-byte line) instead of the caller's AoS array;
+// bind and sync move worlds between the two layouts.
+
+static bool engine_ok(const void* engine, int count) {
+    return count >= 0 && (count == 0 || (engine != nullptr && ((uintptr_t)engine % 16) == 0));
+}
+
+B3X_API size_t b3x_engine_bytes(unsigned long long sig, int count) {
+    Layout L;
+    if (!layout_from_signature(sig, &L) || count < 0) return 0;
+    const size_t tiles = ((size_t)count + kLanes - 1) / kLanes;
+    return tiles * (size_t)L.size * kLanes;
+}
+
+static int engine_move(void* engine, int count, B3Batch worlds, const unsigned char* select, void* stream,
+        unsigned long long sig, bool in) {
+    Layout L;
+    if (!layout_from_signature(sig, &L)) return cudaErrorInvalidValue;
+    if (!engine_ok(engine, count) || !batch_ok(worlds, L.size) || worlds.count != count) return cudaErrorInvalidValue;
+    if (count == 0) return cudaSuccess;
+    if (!aligned8(worlds)) return cudaErrorInvalidValue;
+    const unsigned tiles = (unsigned)((count + kLanes - 1) / kLanes);
+    if (in)
+        columns_kernel<true><<<tiles, kCta, 0, (cudaStream_t)stream>>>((float*)engine, L.size / 4,
+            (unsigned char*)worlds.data, worlds.stride, worlds.world_offset, count, select);
+    else
+        columns_kernel<false><<<tiles, kCta, 0, (cudaStream_t)stream>>>((float*)engine, L.size / 4,
+            (unsigned char*)worlds.data, worlds.stride, worlds.world_offset, count, select);
+    return cudaGetLastError();
+}
+
+B3X_API int b3x_engine_bind(void* engine, int count, B3Batch worlds, const unsigned char* select, void* stream,
+        unsigned long long sig) {
+    return engine_move(engine, count, worlds, select, stream, sig, true);
+}
+
+B3X_API int b3x_engine_sync_to_aos(const void* engine, int count, B3Batch worlds, const unsigned char* select,
+        void* stream, unsigned long long sig) {
+    return engine_move(const_cast<void*>(engine), count, worlds, select, stream, sig, false);
+}
+
+B3X_API int b3x_engine_step(void* engine, int count, float dt, int substeps, const unsigned char* active,
+        void* stream, unsigned long long sig, int ji, int ri, int flags) {
+    Layout L;
+    if (!layout_from_signature(sig, &L)) return cudaErrorInvalidValue;
+    if (!engine_ok(engine, count) || !step_params_ok(dt, substeps, ji, ri, flags)) return cudaErrorInvalidValue;
+    if (count == 0 || dt == 0) return cudaSuccess;
+    Worlds w{nullptr, 0, 0, count, (float*)engine};
+    return run_step(w, dt, substeps, active, stream, sig, L, ji, ri, WsFrom::kLibrary, nullptr, 0, flags);
+}
+
+B3X_API int b3x_engine_apply(void* engine, int count, int kind, int index, const float* values, int vpw,
+        const unsigned char* active, void* stream, unsigned long long sig) {
+    Layout L;
+    if (!layout_from_signature(sig, &L)) return cudaErrorInvalidValue;
+    if (!engine_ok(engine, count) || kind < 0 || kind > 3 || vpw < 1 || (count && !values))
+        return cudaErrorInvalidValue;
+    if (kind != B3X_ACTION_JOINT_TARGET && vpw % 3 != 0) return cudaErrorInvalidValue;
+    if (!count) return cudaSuccess;
+    apply_columns_kernel<<<(count + 127) / 128, 128, 0, (cudaStream_t)stream>>>((float*)engine, L.size / 4, count, L,
+        kind, index, values, vpw, active);
+    return cudaGetLastError();
+}
+
+B3X_API int b3x_engine_observe(const void* engine, int count, int body, float* out, void* stream,
+        unsigned long long sig) {
+    Layout L;
+    if (!layout_from_signature(sig, &L)) return cudaErrorInvalidValue;
+    if (!engine_ok(engine, count) || body < 0 || body >= L.B || (count && !out)) return cudaErrorInvalidValue;
+    if (!count) return cudaSuccess;
+    observe_columns_kernel<<<(count + 127) / 128, 128, 0, (cudaStream_t)stream>>>((const float*)engine, L.size / 4,
+        count, body, out);
     return cudaGetLastError();
 }
 

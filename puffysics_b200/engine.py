@@ -73,6 +73,20 @@ def lib():
         L.b3x_batch_apply_gpu.restype = ctypes.c_int
         L.b3x_batch_observe_gpu.argtypes = [B3Batch, ctypes.c_int, vp, vp, ctypes.c_ulonglong]
         L.b3x_batch_observe_gpu.restype = ctypes.c_int
+        L.b3x_engine_bytes.argtypes = [ctypes.c_ulonglong, ctypes.c_int]
+        L.b3x_engine_bytes.restype = ctypes.c_size_t
+        for name in ("b3x_engine_bind", "b3x_engine_sync_to_aos"):
+            f = getattr(L, name)
+            f.argtypes = [vp, ctypes.c_int, B3Batch, u8p, vp, ctypes.c_ulonglong]
+            f.restype = ctypes.c_int
+        L.b3x_engine_step.argtypes = [vp, ctypes.c_int, ctypes.c_float, ctypes.c_int, u8p, vp, ctypes.c_ulonglong,
+                                      ctypes.c_int, ctypes.c_int, ctypes.c_int]
+        L.b3x_engine_step.restype = ctypes.c_int
+        L.b3x_engine_apply.argtypes = [vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, vp, ctypes.c_int, u8p, vp,
+                                       ctypes.c_ulonglong]
+        L.b3x_engine_apply.restype = ctypes.c_int
+        L.b3x_engine_observe.argtypes = [vp, ctypes.c_int, ctypes.c_int, vp, vp, ctypes.c_ulonglong]
+        L.b3x_engine_observe.restype = ctypes.c_int
         L.b3x_world_bytes.argtypes = [ctypes.c_ulonglong]
         L.b3x_world_bytes.restype = ctypes.c_size_t
         L.b3x_version.restype = ctypes.c_char_p
@@ -174,6 +188,44 @@ def step_launches(caps, count, device=0):
 
 def world_bytes(caps):
     return lib().b3x_world_bytes(layout.signature(*caps))
+
+
+# ---- resident world columns (b3x_engine_*) --------------------------------------------
+class Columns:
+    """Worlds resident in HBM as structure-of-arrays across worlds (the
+    b3x_engine_* entry points): a uint8 device tensor of b3x_engine_bytes and
+    the world count.  bind / sync_to_aos move worlds from / to an AoS batch;
+    step / apply / observe work on the columns directly."""
+
+    def __init__(self, caps, count, device=None):
+        import torch
+        self.caps, self.count = tuple(caps), count
+        self.sig = layout.signature(*caps)
+        nbytes = lib().b3x_engine_bytes(self.sig, count)
+        self.store = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=device or "cuda")
+
+    def _p(self):
+        return ctypes.c_void_p(self.store.data_ptr())
+
+    def bind(self, worlds, select=None, stream=None, stride=None, offset=0):
+        return lib().b3x_engine_bind(self._p(), self.count, make_batch(worlds, stride, offset), _ptr(select),
+                                     _stream(stream), self.sig)
+
+    def sync_to_aos(self, worlds, select=None, stream=None, stride=None, offset=0):
+        return lib().b3x_engine_sync_to_aos(self._p(), self.count, make_batch(worlds, stride, offset), _ptr(select),
+                                            _stream(stream), self.sig)
+
+    def step(self, dt, substeps, active=None, stream=None, joint_iters=2, relax_iters=None, flags=0):
+        relax_iters = joint_iters if relax_iters is None else relax_iters
+        return lib().b3x_engine_step(self._p(), self.count, dt, substeps, _ptr(active), _stream(stream), self.sig,
+                                     joint_iters, relax_iters, flags)
+
+    def apply(self, kind, index, values, active=None, stream=None):
+        return lib().b3x_engine_apply(self._p(), self.count, kind, index, _ptr(values), values.shape[1],
+                                      _ptr(active), _stream(stream), self.sig)
+
+    def observe(self, body, out, stream=None):
+        return lib().b3x_engine_observe(self._p(), self.count, body, _ptr(out), _stream(stream), self.sig)
 
 
 # ---- per-thread device b3_step (include/puffysics.cuh) ------------------------------
