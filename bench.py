@@ -49,6 +49,7 @@ METRIC = "physics-only env-steps/sec (worlds×steps/s) at 1/2/4/8 B200; % HBM ro
 UNIT = "env-steps/s"
 SEED = 1
 L2_BYTES = 126e6
+STATE_ONLY = 4       # B3X_STEP_STATE_ONLY
 
 # Algorithmic bytes of one world-step, read + write, minimal SoA model:
 # dynamic body 196 B (pose+velocity 52 r / 52 w, force+torque 24 r / 24 w,
@@ -84,8 +85,9 @@ def parse_args():
     ap.add_argument("--no-graph", action="store_true", help="e2e with direct calls instead of a CUDA graph")
     ap.add_argument("--no-per-thread-path", action="store_true",
                     help="skip the timing of the per-thread device b3_step after the main measurement")
-    ap.add_argument("--path", default="aos", choices=["columns", "aos"],
-                    help="world layout of the headline: resident columns (b3x_engine_*) or the AoS drop-in")
+    ap.add_argument("--path", default="aos", choices=["columns", "columns_state_only", "aos"],
+                    help="world layout of the headline: the AoS drop-in, or resident columns (b3x_engine_*), "
+                         "optionally with the state-only write-back")
     ap.add_argument("--extra-configs", default="pile",
                     help="comma list of configurations measured after the main one on one GPU ('' for none)")
     return ap.parse_args()
@@ -489,7 +491,9 @@ def run_ours(name, args, rank, world, local, dev, barrier, path="columns"):
     worlds = torch.from_numpy(scenes.build(per_gpu, SEED, first=first)).to(dev)
     seeded = worlds.clone() if (cfg.reset_fraction or window) else None
     stream = torch.cuda.current_stream(dev)
-    cols = engine.Columns(caps, per_gpu, device=dev) if path == "columns" else None
+    cols = engine.Columns(caps, per_gpu, device=dev) if path.startswith("columns") else None
+    # the state-only write-back (b3x_engine_step's B3X_STEP_STATE_ONLY)
+    step_flags = cfg.flags | (STATE_ONLY if path == "columns_state_only" else 0)
     if cols is not None:
         assert cols.bind(worlds, stream=stream) == 0
     # set-up: the step's workspace for this stream (the step itself never allocates)
@@ -524,7 +528,7 @@ def run_ours(name, args, rank, world, local, dev, barrier, path="columns"):
         if ev is not None:
             ev.record(stream)
         if cols is not None:
-            rc = cols.step(cfg.dt, cfg.substeps, None, stream, cfg.joint_iters, cfg.relax_iters, flags=cfg.flags)
+            rc = cols.step(cfg.dt, cfg.substeps, None, stream, cfg.joint_iters, cfg.relax_iters, flags=step_flags)
         else:
             rc = engine.batch_step_gpu(worlds, cfg.dt, cfg.substeps, None, stream, caps, cfg.joint_iters,
                                        cfg.relax_iters, flags=cfg.flags)
@@ -565,6 +569,7 @@ def run_ours(name, args, rank, world, local, dev, barrier, path="columns"):
 
     # diagnostics of the final state (outside the timed region)
     if cols is not None:
+        # (after state-only steps the header counts and bodies read here are whole)
         assert cols.sync_to_aos(worlds, stream=stream) == 0
     final = worlds.cpu().numpy()
     stats = shard.world_stats(final, caps)
@@ -594,7 +599,7 @@ def run_ours(name, args, rank, world, local, dev, barrier, path="columns"):
             else:
                 assert engine.batch_apply_gpu(worlds, kind, aidx, vals, None, s, caps) == 0
         if cols is not None:
-            assert cols.step(cfg.dt, cfg.substeps, None, s, cfg.joint_iters, cfg.relax_iters, flags=cfg.flags) == 0
+            assert cols.step(cfg.dt, cfg.substeps, None, s, cfg.joint_iters, cfg.relax_iters, flags=step_flags) == 0
             assert cols.observe(obs_body, d_obs, stream=s) == 0
         else:
             assert engine.batch_step_gpu(worlds, cfg.dt, cfg.substeps, None, s, caps, cfg.joint_iters,
@@ -644,7 +649,7 @@ def run_ours(name, args, rank, world, local, dev, barrier, path="columns"):
     e2e_local = e_start.elapsed_time(e_end)
     del graph
     assert engine.release_workspaces() == 0
-    if path == "columns":
+    if path.startswith("columns"):
         e2e_path = ("pinned H2D actions -> b3x_engine_apply -> b3x_engine_step -> b3x_engine_observe -> D2H "
                     "(%s), stream synchronised every step" % e2e_mode)
     else:
@@ -779,7 +784,7 @@ def main():
                         "d2h_bytes_per_step": r["bo"], "steps": r["E"], "path": r["e2e_path"]},
                 "gpu_launches": r["launches"], "clocks": r["clocks"]}
 
-    other = "aos" if args.path == "columns" else "columns"
+    others = [p for p in ("aos", "columns", "columns_state_only") if p != args.path]
     if rank == 0:
         per_gpu = res["per_gpu"]
         stream = torch.cuda.current_stream(dev)
@@ -793,8 +798,9 @@ def main():
                                "dropped_contacts": int(tot[3]), "mean_contacts": res["counts"]["contact"],
                                "mean_bodies": res["counts"]["body"]}
         if world == 1:
-            r2 = run_ours(args.config, args, 0, 1, local, dev, barrier, path=other)
-            line[other + "_path"] = measured(r2, r2["t"], r2["k"], r2["e2e"], 1)
+            for other in others:
+                r2 = run_ours(args.config, args, 0, 1, local, dev, barrier, path=other)
+                line[other + "_path"] = measured(r2, r2["t"], r2["k"], r2["e2e"], 1)
         if world == 1 and not args.no_per_thread_path:
             line["per_thread_path"] = thread_path_run(res["cfg"], per_gpu, res["K"], args.warmup, stream,
                                                       window=res["window"])
@@ -811,8 +817,9 @@ def main():
                 sub.update(measured(r, r["t"], r["k"], r["e2e"], 1))
                 sub["diagnostics"] = {"mean_contacts": r["counts"]["contact"], "mean_bodies": r["counts"]["body"],
                                       "overflowed_worlds": int(r["stats"][2]), "dropped_contacts": int(r["stats"][3])}
-                r2 = run_ours(name, args, 0, 1, local, dev, barrier, path=other)
-                sub[other + "_path"] = measured(r2, r2["t"], r2["k"], r2["e2e"], 1)
+                for other in others:
+                    r2 = run_ours(name, args, 0, 1, local, dev, barrier, path=other)
+                    sub[other + "_path"] = measured(r2, r2["t"], r2["k"], r2["e2e"], 1)
                 if not args.no_per_thread_path:
                     sub["per_thread_path"] = thread_path_run(r["cfg"], r["per_gpu"], r["K"], args.warmup, stream,
                                                              window=r["window"])

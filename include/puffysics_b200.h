@@ -963,7 +963,18 @@ B3X_API int b3x_engine_sync_to_aos(const void* engine, int count, B3Batch worlds
     void* stream, unsigned long long config_signature);
 
 /* b3x_batch_step_gpu_flags on the columns: same validation, no-op cases,
- * mask, modes, workspace (reservation or the library's array) and results. */
+ * mask, modes, workspace (reservation or the library's array) and results.
+ * One more flag: B3X_STEP_STATE_ONLY writes back only the world state later
+ * steps read -- bodies, header counts, each contact's warm-start cache (pair,
+ * point count, features, impulses) and joint impulses -- and skips the words
+ * a step merely outputs (a contact's anchors, masses, tangents, softness; a
+ * joint's prepared frames, masses and softness), which keep the bytes of the
+ * last step without the flag.  Trajectories are unchanged.  After a step
+ * without the flag every word the reference defines is again byte-equal to
+ * the AoS path; contact slots past a world's contact count and point slots
+ * past a contact's point count (whose bytes the reference leaves over from
+ * earlier steps) may then hold bytes of an earlier step than there. */
+#define B3X_STEP_STATE_ONLY 4
 B3X_API int b3x_engine_step(void* engine, int count, float dt, int substeps, const unsigned char* active,
     void* stream, unsigned long long config_signature, int joint_iters, int relax_iters, int flags);
 

@@ -24,7 +24,7 @@ namespace b3x {
 // 07_packed.inl:63-65, 09_step.inl:169-181): contacts swept inside every
 // joint iteration instead of once per phase (B3_INTERLEAVE_CONTACTS), and no
 // restitution pass (B3_SKIP_RESTITUTION).
-enum : int { kStepInterleaveContacts = 1, kStepSkipRestitution = 2 };
+enum : int { kStepInterleaveContacts = 1, kStepSkipRestitution = 2, kStepStateOnly = 4 };
 
 // Bit casts between 32-bit words (ints and flags share the float columns).
 B3X_HDI int b3x_f2i(float f) {

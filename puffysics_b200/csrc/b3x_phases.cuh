@@ -1203,6 +1203,50 @@ B3X_HD void o_joint_write(const Args& a, int tile, float* slot, OutShared& sh, i
     }
 }
 
+// The state-only write-back of the resident columns (kStepStateOnly): of a
+// contact only the words a later step reads -- its warm-start cache (pair,
+// point count, features, impulses; point words up to the point count, as the
+// full write-back) -- straight from the workspace columns; of a joint only
+// its impulses.  The words steps merely output (prepared solver terms) keep
+// the bytes of the last full write-back.
+B3X_HD void o_contact_state(const Args& a, int tile, float* slot, OutShared& sh, int t) {
+    for (int j = t; j < sh.maxn * kLanes; j += kCta) {
+        const int k = j >> 5, l = j & 31;
+        if (k >= sh.n[l]) continue;
+        const float* co = item(slot + a.SP.cont, k, kCI) + l;
+        const int cnt = clampi(ldi(co, WCNT), 0, B3_MAX_MANIFOLD);
+        const size_t base = a.L.contact_off / 4 + (size_t)k * NCW;
+        for (int f = 0; f < NOF; f++) {
+            const int p = f < OFEAT ? -1 : (f < ONI ? f - OFEAT : f - ONI);
+            if (p >= cnt) continue;
+            const int w = old_word(f);
+            store_world(res_word(a, tile, base + w, l), COL(co, w));
+        }
+    }
+}
+
+B3X_HD void o_joint_state(const Args& a, int tile, float* slot, OutShared& sh, int t) {
+    for (int j = t; j < sh.maxnj * kLanes; j += kCta) {
+        const int q = j >> 5, l = j & 31;
+        if (q >= sh.nj[l]) continue;
+        const float* jo = item(slot + a.SP.joint, q, NJF) + l;
+        if (!ldi(jo, JOK)) continue;
+        const size_t base = a.L.joint_off / 4 + (size_t)q * NVW;
+        auto put = [&](int v, int c) { store_world(res_word(a, tile, base + v, l), COL(jo, c)); };
+        for (int c = 0; c < 3; c++) put(VLI + c, JLI + c);
+        if (ldi(jo, JTYPE) == B3_JOINT_WELD) {
+            for (int c = 0; c < 3; c++) put(VAI + c, JAI + c);
+        } else {
+            put(VPI, JPI);
+            put(VPI + 1, JPI + 1);
+            put(VSI, JSI);
+            put(VMI, JMI);
+            put(VLOI, JLOI);
+            put(VUPI, JUPI);
+        }
+    }
+}
+
 // Items per write-back round: as many as the staging area holds, balanced.
 B3X_HDI int out_items(int count, int row_floats) {
     int k = kStageFloats / (kLanes * row_floats);
@@ -1242,7 +1286,12 @@ B3X_HD void out_tile(X& x, const Args& a, int bt, OutShared& sh) {
             x.each([&](int t) { o_body_write<kRes>(a, tile, sh, k0, K, t); });
         }
     }
-    {
+    const bool state_only = kRes && (a.flags & kStepStateOnly) != 0;
+    if (state_only) {
+        x.each([&](int t) { o_contact_state(a, tile, slot, sh, t); });
+        x.each([&](int t) { o_joint_state(a, tile, slot, sh, t); });
+    }
+    if (!state_only) {
         const int K = out_items(sh.maxn, NCW);
         for (int k0 = 0; k0 < sh.maxn; k0 += K) {
             const int Kr = sh.maxn - k0 < K ? sh.maxn - k0 : K;
@@ -1253,7 +1302,7 @@ B3X_HD void out_tile(X& x, const Args& a, int bt, OutShared& sh) {
             x.each([&](int t) { o_contact_write<kRes>(a, tile, sh, k0, Kr, t); });
         }
     }
-    {
+    if (!state_only) {
         const int K = out_items(sh.maxnj, NVW);
         for (int q0 = 0; q0 < sh.maxnj; q0 += K) {
             const int Kr = sh.maxnj - q0 < K ? sh.maxnj - q0 : K;

@@ -710,9 +710,9 @@ static int run_step(const Worlds& w, float dt, int substeps, const unsigned char
     return launch_step(w, dt, substeps, active, (cudaStream_t)stream, L, ji, ri, flags, p, ws, chunk);
 }
 
-static bool step_params_ok(float dt, int substeps, int ji, int ri, int flags) {
-    return std::isfinite(dt) && dt >= 0 && substeps >= 1 && ji >= 1 && ri >= 1
-        && (flags & ~(kStepInterleaveContacts | kStepSkipRestitution)) == 0;
+static bool step_params_ok(float dt, int substeps, int ji, int ri, int flags,
+        int allowed = kStepInterleaveContacts | kStepSkipRestitution) {
+    return std::isfinite(dt) && dt >= 0 && substeps >= 1 && ji >= 1 && ri >= 1 && (flags & ~allowed) == 0;
 }
 
 static int step_common(B3Batch batch, float dt, int substeps, const unsigned char* active, void* stream,
@@ -904,7 +904,10 @@ B3X_API int b3x_engine_step(void* engine, int count, float dt, int substeps, con
         void* stream, unsigned long long sig, int ji, int ri, int flags) {
     Layout L;
     if (!layout_from_signature(sig, &L)) return cudaErrorInvalidValue;
-    if (!engine_ok(engine, count) || !step_params_ok(dt, substeps, ji, ri, flags)) return cudaErrorInvalidValue;
+    if (!engine_ok(engine, count)
+            || !step_params_ok(dt, substeps, ji, ri, flags,
+                               kStepInterleaveContacts | kStepSkipRestitution | kStepStateOnly))
+        return cudaErrorInvalidValue;
     if (count == 0 || dt == 0) return cudaSuccess;
     Worlds w{nullptr, 0, 0, count, (float*)engine};
     return run_step(w, dt, substeps, active, stream, sig, L, ji, ri, WsFrom::kLibrary, nullptr, 0, flags);

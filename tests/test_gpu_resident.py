@@ -150,3 +150,72 @@ def test_columns_more_tiles_than_workspace_slots(oracle_kind, gpu_lib):
     assert cols.sync_to_aos(out, stream=stream) == 0
     stream.synchronize()
     assert np.array_equal(out.cpu().numpy(), host)
+
+
+STATE_ONLY = 4
+
+
+def defined_words(raw, caps):
+    """A copy with the words the reference leaves undefined zeroed: contact
+    slots past a world's contact count, point slots past a contact's point
+    count (they keep whatever bytes an earlier step left there)."""
+    out = raw.copy()
+    v = layout.view(out, caps)
+    for wi in range(len(out)):
+        k = int(v["contact_count"][wi])
+        v["contacts"][wi, k:] = np.zeros(1, v["contacts"].dtype)
+        for c in range(k):
+            pc = int(v["contacts"][wi, c]["point_count"])
+            v["contacts"][wi, c]["points"][pc:] = np.zeros(1, v["contacts"]["points"].dtype.base)
+    return out
+
+
+@pytest.mark.parametrize("name", ["stack", "pile", "chain", "capsule"])
+def test_state_only_steps_keep_the_trajectory(name, oracle_kind, gpu_lib):
+    """Steps with B3X_STEP_STATE_ONLY write back only what later steps read:
+    after such steps the bodies, header and warm-start words equal the
+    reference's; after a step without the flag every word the reference
+    defines does (contact slots past the contact count and point slots past
+    the point count hold stale bytes in both and are not compared)."""
+    cfg = CONFIGS[name]
+    o = orc.Oracle(name, oracle_kind)
+    n = 96 if name == "pile" else 160
+    host = o.build(n, cfg.scene, 2024)
+    aos = torch.from_numpy(host.copy()).cuda()
+    cols = engine.Columns(cfg.caps, n)
+    assert cols.bind(aos) == 0
+    kind, idx, nv = cfg.action
+    vals = torch.zeros((n, max(nv, 1)), dtype=torch.float32, device="cuda")
+    for s in range(1, 21):
+        full = s % 5 == 0
+        o.apply(host, cfg.scene, 2024, 0, s)
+        if nv:
+            assert synth.actions_gpu(vals, n, cfg.scene, 2024, 0, s) == nv
+            assert cols.apply(kind, idx, vals) == 0
+        assert o.batch_step(host, cfg.dt, cfg.substeps) == 1
+        assert cols.step(cfg.dt, cfg.substeps, joint_iters=cfg.joint_iters, relax_iters=cfg.relax_iters,
+                         flags=cfg.flags | (0 if full else STATE_ONLY)) == 0
+        assert cols.sync_to_aos(aos) == 0
+        torch.cuda.synchronize()
+        got = aos.cpu().numpy()
+        if full:
+            compare(name, defined_words(got, cfg.caps), defined_words(host, cfg.caps), s)
+            continue
+        g, w = layout.view(got, cfg.caps), layout.view(host, cfg.caps)
+        assert contact_keys(got, cfg.caps) == contact_keys(host, cfg.caps), "contact sets differ at step %d" % s
+        if cfg.scene == SCENE_CHAIN:
+            ok, err = state_close(got, host, cfg.caps, TOL_60STEP)
+            assert ok, err
+            continue
+        assert np.array_equal(g["bodies"], w["bodies"]), "bodies differ at step %d" % s
+        for f in ("contact_count", "contact_overflow", "contacts_dropped"):
+            assert np.array_equal(g[f], w[f])
+        for wi in range(n):
+            k = int(w["contact_count"][wi])
+            gc, wc = g["contacts"][wi, :k], w["contacts"][wi, :k]
+            for f in ("friction_impulse", "twist_impulse", "rolling_impulse"):
+                assert np.array_equal(gc[f], wc[f]), (s, wi, f)
+            for c in range(k):
+                pc = int(wc["point_count"][c])
+                assert np.array_equal(gc["points"][c, :pc]["normal_impulse"], wc["points"][c, :pc]["normal_impulse"])
+    assert engine.fault_flags() == 0
