@@ -36,8 +36,8 @@
 #define B3X_THREAD_BOUNDS __launch_bounds__(32, 16)
 
 __device__ inline void b3_step(B3World* w, float dt, int substeps) {
-    b3x::one::step_world(w, dt, substeps, B3_JOINT_ITERS, B3_RELAX_ITERS,
-                         B3X_MODE_INTERLEAVE | B3X_MODE_SKIP_RESTITUTION);
+    b3x::one::step_world<(B3_ART_CONTACTS != 0)>(w, dt, substeps, B3_JOINT_ITERS, B3_RELAX_ITERS,
+                                                 B3X_MODE_INTERLEAVE | B3X_MODE_SKIP_RESTITUTION);
 }
 
 static __global__ void B3X_THREAD_BOUNDS b3_step_kernel(B3World* worlds, int n, float dt, int substeps) {
@@ -45,9 +45,10 @@ static __global__ void B3X_THREAD_BOUNDS b3_step_kernel(B3World* worlds, int n, 
     if (i < n) b3_step(&worlds[i], dt, substeps);
 }
 
-#if B3_HAS_USER_FORCES
-/* With a per-substep force hook the batch step runs this translation unit's
- * per-thread b3_step, which runs the hook (reference b3_batch.cuh:63-89
+#if B3_HAS_USER_FORCES || B3_ART_CONTACTS
+/* With a per-substep force hook, or with the articulated contact response
+ * of B3_ART_CONTACTS=1, the batch step runs this translation unit's
+ * per-thread b3_step, which has them (reference b3_batch.cuh:63-89
  * semantics: same validation, no-ops, mask, stream; no allocation). */
 static __global__ void B3X_THREAD_BOUNDS b3x_user_force_batch_kernel(B3Batch batch, float dt, int substeps,
         const unsigned char* active) {

@@ -23,7 +23,8 @@
  * reference.  The library reads them at run time from each call.
  *
  * Not supported (compile error): the reference's experimental layout flags
- * B3_REVOLUTE_ONLY and B3_CACHE_JOINTS, and B3_ART_CONTACTS=1.
+ * B3_REVOLUTE_ONLY, B3_CACHE_JOINTS and B3_PACKED_GS.  B3_ART_CONTACTS=1 is
+ * supported by the device b3_step of puffysics.cuh (see below).
  */
 #ifndef PUFFYSICS_B200_H
 #define PUFFYSICS_B200_H
@@ -80,9 +81,11 @@
 #if defined(B3_REVOLUTE_ONLY) || defined(B3_CACHE_JOINTS) || defined(B3_PACKED_GS)
 #error "puffysics_b200 implements the default joint layout only"
 #endif
-#if defined(B3_ART_CONTACTS) && B3_ART_CONTACTS
-#error "puffysics_b200 implements the B3_ART_CONTACTS=0 contact model only"
-#endif
+/* B3_ART_CONTACTS=1 (reference 01_config.inl:43, 185-187): contacts of
+ * worlds with joints are resolved through the articulation of their
+ * revolute joints.  Run by the device b3_step of puffysics.cuh (built in
+ * when the macro is 1); b3_batch_step_gpu then steps with that per-thread
+ * b3_step, as with a force hook. */
 #ifndef B3_ART_CONTACTS
 #define B3_ART_CONTACTS 0
 #endif
@@ -1007,7 +1010,7 @@ B3X_API const char* b3x_version(void);
 
 /* Inline shims with the exact reference signatures (reference
  * b3_batch.cuh:81-99), available wherever the CUDA runtime types are. */
-#if (defined(__CUDACC__) || defined(CUDART_VERSION)) && !B3_HAS_USER_FORCES
+#if (defined(__CUDACC__) || defined(CUDART_VERSION)) && !B3_HAS_USER_FORCES && !B3_ART_CONTACTS
 B3_INL cudaError_t b3_batch_step_gpu(B3Batch batch, float dt, int substeps,
         const unsigned char* active, cudaStream_t stream) {
 #if defined(B3_INTERLEAVE_CONTACTS) || defined(B3_SKIP_RESTITUTION)

@@ -22,11 +22,13 @@ HEADERS = [os.path.join(ROOT, "include", "puffysics_b200.h"),
            os.path.join(PKG, "csrc", "b3x_layout.cuh"),
            os.path.join(PKG, "csrc", "b3x_solver.cuh"),
            os.path.join(PKG, "csrc", "b3x_phases.cuh"),
+           os.path.join(PKG, "csrc", "b3x_world_step.cuh"),
+           os.path.join(PKG, "csrc", "b3x_art.cuh"),
            os.path.join(PKG, "scenes", "b3_scenes.h")]
 SCENES_SRC = os.path.join(PKG, "scenes", "b3_scenes_host.c")
 THREAD_SRC = os.path.join(PKG, "csrc", "b3x_thread_step.cu")
 THREAD_HEADERS = [os.path.join(ROOT, "include", "puffysics.cuh"),
-                  os.path.join(PKG, "csrc", "b3x_world_step.cuh")]
+                  os.path.join(PKG, "csrc", "b3x_world_step.cuh"), os.path.join(PKG, "csrc", "b3x_art.cuh")]
 # the hover environment fused into one launch per step (libb3hover.so)
 HOVER_SRC = os.path.join(PKG, "csrc", "b3x_hover_env.cu")
 HOVER_LIB = os.path.join(LIB_DIR, "libb3hover.so")
@@ -41,20 +43,21 @@ SCENE_CONFIGS = {"hover": (2, 2, 4, 1), "stack": (9, 9, 32, 1), "chain": (12, 12
                  "pile": (37, 37, 128, 1), "hovertask": (2, 2, 4, 2), "default": (80, 128, 128, 32),
                  "stacksmall": (9, 9, 4, 1), "bounce": (9, 9, 32, 1), "capsule": (17, 17, 64, 1), "stackil": (9, 9, 32, 1),
                  "chainil": (12, 12, 32, 10), "bouncenr": (9, 9, 32, 1), "bounceilnr": (9, 9, 32, 1),
-                 "hoveruf": (2, 2, 4, 1)}
+                 "hoveruf": (2, 2, 4, 1), "chainart": (12, 12, 32, 10)}
 # per-thread step launchers (include/puffysics.cuh's device b3_step): name ->
 # (bodies, shapes, contacts, joints, B3_JOINT_ITERS), the capacities of the
 # benchmark configurations and of the reference's defaults
 THREAD_CONFIGS = {"hover": (2, 2, 4, 1, 8), "stack": (9, 9, 32, 1, 8), "chain": (12, 12, 32, 10, 8),
                   "pile": (37, 37, 128, 1, 8), "hovertask": (2, 2, 4, 2, 2), "default": (80, 128, 128, 32, 2),
                   "bounce": (9, 9, 32, 1, 8), "capsule": (17, 17, 64, 1, 8), "stackil": (9, 9, 32, 1, 8),
-                  "chainil": (12, 12, 32, 10, 8),
+                  "chainil": (12, 12, 32, 10, 8), "chainart": (12, 12, 32, 10, 8),
                   "bouncenr": (9, 9, 32, 1, 8), "bounceilnr": (9, 9, 32, 1, 8), "hoveruf": (2, 2, 4, 1, 8)}
 # the reference's mode macros of the per-thread configurations
 THREAD_MODES = {"stackil": ["-DB3_INTERLEAVE_CONTACTS"], "chainil": ["-DB3_INTERLEAVE_CONTACTS"],
                 "bouncenr": ["-DB3_SKIP_RESTITUTION"],
                 "bounceilnr": ["-DB3_INTERLEAVE_CONTACTS", "-DB3_SKIP_RESTITUTION"],
-                "hoveruf": ["-include", os.path.join(PKG, "scenes", "b3_test_forces.h")]}
+                "hoveruf": ["-include", os.path.join(PKG, "scenes", "b3_test_forces.h")],
+                "chainart": ["-DB3_ART_CONTACTS=1"]}
 CC = os.environ.get("CC", "gcc")
 
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc" if os.path.exists("/usr/local/cuda/bin/nvcc") else "nvcc")

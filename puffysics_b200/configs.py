@@ -68,6 +68,9 @@ CONFIGS = {
     "bounceilnr": Config("bounceilnr", SCENE_BOUNCE, (9, 9, 32, 1), 8, 8, 1.0 / 60.0, 4, 1024,
                          flags=STEP_INTERLEAVE_CONTACTS | STEP_SKIP_RESTITUTION,
                          description="bounce, both modes"),
+    "chainart": Config("chainart", SCENE_CHAIN, (12, 12, 32, 10), 8, 8, 1.0 / 120.0, 2, 1024,
+                       description="chain with the articulated contact response (B3_ART_CONTACTS=1; "
+                                   "per-thread step only)"),
     "hoveruf": Config("hoveruf", SCENE_HOVER, (2, 2, 4, 1), 8, 8, 1.0 / 60.0, 4, 1024,
                       description="hover with the per-substep force hook of scenes/b3_test_forces.h "
                                   "(B3_USER_FORCES; per-thread step only)"),

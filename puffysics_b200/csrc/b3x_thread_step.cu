@@ -44,6 +44,18 @@ B3T_API int b3x_thread_step_gpu(B3Batch batch, float dt, int substeps, const uns
     return (int)cudaGetLastError();
 }
 
+// The header's own b3_batch_step_gpu (the inline shim an adapter compiles):
+// a call into libpuffysics_b200.so, or, with a force hook or
+// B3_ART_CONTACTS=1, this translation unit's per-thread step.  Exported only
+// where it stays inside this library (hook and articulation builds), so that
+// the route an adapter gets can be checked on the GPU.
+#if B3_HAS_USER_FORCES || B3_ART_CONTACTS
+B3T_API int b3x_thread_shim_step_gpu(B3Batch batch, float dt, int substeps, const unsigned char* active,
+        void* stream) {
+    return (int)b3_batch_step_gpu(batch, dt, substeps, active, (cudaStream_t)stream);
+}
+#endif
+
 // b3_step_kernel (reference 09_step.inl:325-333) over contiguous worlds.
 B3T_API int b3x_thread_step_worlds_gpu(B3World* worlds, int n, float dt, int substeps, void* stream) {
     if (n < 0 || (n > 0 && !worlds)) return (int)cudaErrorInvalidValue;

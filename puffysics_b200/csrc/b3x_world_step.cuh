@@ -32,6 +32,8 @@
 #define B3X_NARROW static B3X_HD
 #endif
 #include "b3x_narrow.cuh"
+#include "b3x_art.cuh"
+#include <type_traits>
 
 #if defined(__CUDACC__)
 namespace b3x {
@@ -153,9 +155,15 @@ __device__ __forceinline__ int clamp_count(int n, int cap) { return n < 0 ? 0 : 
 // memory, as in the reference.  Counts beyond the capacities are clamped and
 // shapes or joints that name a body outside the world are inert (the
 // reference would index past its arrays), so a corrupt world cannot fault.
-template <class V>
+// kArt: the articulated contact response of B3_ART_CONTACTS=1 for worlds
+// with joints and contacts (b3x_art.cuh), built into the step only where it
+// is asked for, since its tree takes several kilobytes of local memory.
+struct NoTree {};
+template <class V, bool kArt = false>
 struct Stepper {
     V v;
+    typename std::conditional<kArt, art::Tree<V::kB>, NoTree>::type tree;
+    bool art_on;   // the articulated response resolves this step's contacts
     int nb, ns, nj;
     float h, inv_h, inv_dt;
     B3Soft cs, ss;
@@ -734,6 +742,12 @@ struct Stepper {
     }
 
     __device__ void solve_contacts(bool use_bias) {
+        if constexpr (kArt) {
+            if (art_on) {
+                tree.solve_contacts(v.bodies, v.contacts, v.h->contact_count, inv_h, v.h->contact_speed, use_bias);
+                return;
+            }
+        }
         for (int i = 0; i < v.h->contact_count; i++) solve_contact(v.contacts[i], use_bias);
     }
 
@@ -813,7 +827,16 @@ struct Stepper {
         for (int i = 0; i < v.h->contact_count; i++) prepare_contact(v.contacts[i]);
         for (int i = 0; i < nj; i++)
             if (joint_ok(v.joints[i])) prepare_joint(v.joints[i]);
-        for (int i = 0; i < v.h->contact_count; i++) warm_contact(v.contacts[i]);
+        // B3_ART_CONTACTS=1: worlds with joints and contacts whose revolute
+        // joints span a tree warm start and solve contacts through it
+        // (08_contacts.inl:194-232, 424-436)
+        art_on = false;
+        if constexpr (kArt) art_on = nj > 0 && v.h->contact_count > 0 && tree.build(v.bodies, nb, v.joints, nj);
+        if constexpr (kArt) {
+            if (art_on) tree.warm_start(v.bodies, v.contacts, v.h->contact_count);
+        }
+        if (!art_on)
+            for (int i = 0; i < v.h->contact_count; i++) warm_contact(v.contacts[i]);
         for (int i = 0; i < nj; i++)
             if (joint_ok(v.joints[i])) warm_joint(v.joints[i]);
         const bool interleave = (flags & kStepInterleaveContacts) != 0;
@@ -834,12 +857,12 @@ struct Stepper {
 
 // b3_step_indep (09_step.inl:183-258) of the world a view addresses, with
 // run-time solver iteration counts.
-template <class V>
+template <class V, bool kArt = false>
 __device__ inline void step_view(const V& v, float dt, int substeps, int joint_iters, int relax_iters,
                                  int flags = 0) {
     if (dt <= 0.0f) return;
     const int subs = substeps < 1 ? 1 : substeps;
-    Stepper<V> st;
+    Stepper<V, kArt> st;
     st.v = v;
     st.nb = clamp_count(v.h->body_count, v.cap_b < V::kB ? v.cap_b : V::kB);
     st.ns = clamp_count(v.h->shape_count, v.cap_s < V::kS ? v.cap_s : V::kS);
@@ -857,10 +880,12 @@ __device__ inline void step_view(const V& v, float dt, int substeps, int joint_i
     st.run(subs);
 }
 
-// b3_step_indep on a B3World of this translation unit's capacities.
+// b3_step_indep on a B3World of this translation unit's capacities (kArt:
+// with the B3_ART_CONTACTS=1 contact response).
+template <bool kArt = false>
 __device__ inline void step_world(B3World* w, float dt, int substeps, int joint_iters, int relax_iters,
                                   int flags = 0) {
-    step_view(view_of(w), dt, substeps, joint_iters, relax_iters, flags);
+    step_view<decltype(view_of(w)), kArt>(view_of(w), dt, substeps, joint_iters, relax_iters, flags);
 }
 
 }  // namespace one

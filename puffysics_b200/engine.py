@@ -249,6 +249,10 @@ def thread_lib(name):
         L.b3x_thread_step_worlds_gpu.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_int,
                                                  ctypes.c_void_p]
         L.b3x_thread_step_worlds_gpu.restype = ctypes.c_int
+        if hasattr(L, "b3x_thread_shim_step_gpu"):
+            L.b3x_thread_shim_step_gpu.argtypes = [B3Batch, ctypes.c_float, ctypes.c_int, ctypes.c_void_p,
+                                                   ctypes.c_void_p]
+            L.b3x_thread_shim_step_gpu.restype = ctypes.c_int
         _thread_libs[name] = L
     return _thread_libs[name]
 

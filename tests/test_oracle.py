@@ -150,3 +150,22 @@ def test_step_modes_change_the_trajectory(mode, plain):
         a.batch_step(wa, cfg.dt, cfg.substeps)
         b.batch_step(wb, cfg.dt, cfg.substeps)
     assert not np.array_equal(wa, wb)
+
+
+@needs_ref
+def test_articulated_contact_build_changes_the_trajectory():
+    """The B3_ART_CONTACTS=1 reference build (the oracle of the articulated
+    contact response) leaves the default chain's trajectory once the chain
+    touches the ground, and not before."""
+    cfg = CONFIGS["chainart"]
+    a, b = orc.Oracle("chainart", "ref"), orc.Oracle("chain", "ref")
+    w = a.build(8, cfg.scene, 5)
+    wa, wb = w.copy(), w.copy()
+    for step in range(1, 121):
+        a.apply(wa, cfg.scene, 5, 0, step)
+        b.apply(wb, cfg.scene, 5, 0, step)
+        a.batch_step(wa, cfg.dt, cfg.substeps)
+        b.batch_step(wb, cfg.dt, cfg.substeps)
+        if step == 20:
+            assert np.array_equal(wa, wb)
+    assert not np.array_equal(wa, wb)
