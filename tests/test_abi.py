@@ -173,3 +173,20 @@ def test_force_hook_adapter_uses_the_per_thread_step(tmp_path):
                                        "-o", str(out)]
     res = subprocess.run(cmd, capture_output=True, text=True)
     assert res.returncode == 0, res.stdout + res.stderr
+
+
+def test_articulated_contacts_adapter_uses_the_per_thread_step(tmp_path):
+    """With B3_ART_CONTACTS=1 the header accepts the macro, the device b3_step
+    carries the articulated contact response and b3_batch_step_gpu compiles
+    to that per-thread step (no library symbol needed)."""
+    src = tmp_path / "art.cu"
+    src.write_text('#define B3_MAX_BODIES 12\n#define B3_MAX_SHAPES 12\n#define B3_MAX_CONTACTS 32\n'
+                   '#define B3_MAX_JOINTS 10\n#define B3_ART_CONTACTS 1\n'
+                   '#include "b3_batch.cuh"\n'
+                   'int main() { B3Batch b = {nullptr, sizeof(B3World), 0, 0};\n'
+                   '  return (int)b3_batch_step_gpu(b, 1.0f / 60.0f, 4, nullptr, 0); }\n')
+    out = tmp_path / "art"
+    cmd = [build.NVCC] + build.ARCH + ["-O1", "-std=c++17", "-I" + os.path.join(ROOT, "include"), str(src),
+                                       "-o", str(out)]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    assert res.returncode == 0, res.stdout + res.stderr
