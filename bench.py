@@ -88,6 +88,8 @@ def parse_args():
     ap.add_argument("--path", default="aos", choices=["columns", "columns_state_only", "aos"],
                     help="world layout of the headline: the AoS drop-in, or resident columns (b3x_engine_*), "
                          "optionally with the state-only write-back")
+    ap.add_argument("--no-other-paths", action="store_true",
+                    help="measure only the headline's world layout (no aos / columns comparison runs)")
     ap.add_argument("--extra-configs", default="pile",
                     help="comma list of configurations measured after the main one on one GPU ('' for none)")
     return ap.parse_args()
@@ -784,7 +786,7 @@ def main():
                         "d2h_bytes_per_step": r["bo"], "steps": r["E"], "path": r["e2e_path"]},
                 "gpu_launches": r["launches"], "clocks": r["clocks"]}
 
-    others = [p for p in ("aos", "columns", "columns_state_only") if p != args.path]
+    others = [] if args.no_other_paths else [p for p in ("aos", "columns", "columns_state_only") if p != args.path]
     if rank == 0:
         per_gpu = res["per_gpu"]
         stream = torch.cuda.current_stream(dev)

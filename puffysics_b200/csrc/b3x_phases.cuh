@@ -171,16 +171,16 @@ B3X_HD void c_gather_group(const Args& a, int tile, CollideShared& sh, const int
                 async_copy4_world(sh.u.flat + dst + (g * M + k) * RS + c,
                                   res_word(a, tile, base / 4 + (size_t)k * PER + c, l));
         }
-        return;
-    }
-    for (int g = w; g < G; g += kCtaWarps) {
-        const int l = l0 + g;
-        const int words = count[l] * PER;
-        const float* src = world_words(a, tile * kLanes + l) + base / 4;
-        float* row0 = sh.u.flat + dst + g * M * RS;
-        for (int idx = i; idx < words; idx += 32) {
-            const int k = idx / PER, c = idx - k * PER;
-            async_copy4_world(row0 + k * RS + c, src + idx);
+    } else {
+        for (int g = w; g < G; g += kCtaWarps) {
+            const int l = l0 + g;
+            const int words = count[l] * PER;
+            const float* src = world_words(a, tile * kLanes + l) + base / 4;
+            float* row0 = sh.u.flat + dst + g * M * RS;
+            for (int idx = i; idx < words; idx += 32) {
+                const int k = idx / PER, c = idx - k * PER;
+                async_copy4_world(row0 + k * RS + c, src + idx);
+            }
         }
     }
 }
@@ -191,6 +191,18 @@ B3X_HDI int old_word(int i) {
     return i == OSA ? WSA : i == OSB ? WSB : i == OCNT ? WCNT : i < OTWI ? WFI + (i - OFI)
         : i == OTWI ? WTWI : i < OFEAT ? WRI + (i - ORI) : i < ONI ? PW(i - OFEAT, QFEAT) : PW(i - ONI, QNI);
 }
+
+// A struct row of one world in the resident columns: word f at p[f * 32].
+struct ColRow {
+    float* p;
+    B3X_HDI float& operator[](int f) const { return p[(size_t)f * kLanes]; }
+};
+// The warm-start words of a previous-step contact row in the resident
+// columns, in OLD field order.
+struct OldColRow {
+    const float* p;
+    B3X_HDI float operator[](int f) const { return p[(size_t)old_word(f) * kLanes]; }
+};
 
 template <bool kRes>
 B3X_HD void c_gather_old(const Args& a, int tile, CollideShared& sh, int l0, int G, int M, int dst, int t) {
@@ -203,15 +215,15 @@ B3X_HD void c_gather_old(const Args& a, int tile, CollideShared& sh, int l0, int
                 async_copy4_world(sh.u.flat + dst + (g * M + k) * NOF + f,
                                   res_word(a, tile, a.L.contact_off / 4 + (size_t)k * NCW + old_word(f), l));
         }
-        return;
-    }
-    if (i >= NOF) return;
-    const int word = old_word(i);
-    for (int g = w; g < G; g += kCtaWarps) {
-        const int l = l0 + g;
-        const float* src = world_words(a, tile * kLanes + l) + a.L.contact_off / 4 + word;
-        float* row0 = sh.u.flat + dst + g * M * NOF;
-        for (int k = 0; k < sh.oldn[l]; k++) async_copy4_world(row0 + k * NOF + i, src + k * (B3X_CONTACT_BYTES / 4));
+    } else {
+        if (i >= NOF) return;
+        const int word = old_word(i);
+        for (int g = w; g < G; g += kCtaWarps) {
+            const int l = l0 + g;
+            const float* src = world_words(a, tile * kLanes + l) + a.L.contact_off / 4 + word;
+            float* row0 = sh.u.flat + dst + g * M * NOF;
+            for (int k = 0; k < sh.oldn[l]; k++) async_copy4_world(row0 + k * NOF + i, src + k * (B3X_CONTACT_BYTES / 4));
+        }
     }
 }
 
@@ -225,7 +237,8 @@ B3X_HD void c_gather_old(const Args& a, int tile, CollideShared& sh, int l0, int
 // Body k of world l (row y): solver columns, step constants and pose
 // (inverse mass / inertia gated by type as the contact and joint prepares do,
 // 08_contacts.inl:236-239; velocity increments of 09_step.inl:5-18).
-B3X_HD void c_body(const Args& a, float* slot, const CollideShared& sh, int k, int l, const float* y) {
+template <class Y>
+B3X_HD void c_body(const Args& a, float* slot, const CollideShared& sh, int k, int l, const Y& y) {
     const float h = a.dt / (float)a.substeps;
     float* bc = item(slot + a.SP.body, k, NBF) + l;
     float* kb = item(slot + a.SP.bodyk, k, NBC) + l;
@@ -263,7 +276,8 @@ B3X_HD void c_body(const Args& a, float* slot, const CollideShared& sh, int k, i
 
 // Shape s of world l (row y): world pose and padded AABB (04_world.inl:293-336,
 // 08_contacts.inl:109-114); a shape on an invalid body never overlaps.
-B3X_HD void c_shape(const Args& a, float* slot, const CollideShared& sh, int s, int l, const float* y) {
+template <class Y>
+B3X_HD void c_shape(const Args& a, float* slot, const CollideShared& sh, int s, int l, const Y& y) {
     float* so = item(slot + a.SP.shape, s, NSF) + l;
     const int body = b3x_f2i(y[XBODY]);
     const int type = b3x_f2i(y[XTYPE]);
@@ -331,8 +345,8 @@ B3X_HDI int group_size(int per_world_floats, int budget) {
 // (then the reference matches with a merge cursor, else with a full scan;
 // both pick the same entry), 08_contacts.inl:70-79.  `prev` is the staged
 // row of contact k - 1.
-B3X_HD void c_old_row(const Args& a, float* slot, CollideShared& sh, int k, int l, const float* y,
-        const float* prev) {
+template <class Y>
+B3X_HD void c_old_row(const Args& a, float* slot, CollideShared& sh, int k, int l, const Y& y, const Y& prev) {
     float* oc = item(slot + a.SP.old, k, NOF) + l;
     for (int f = 0; f < NOF; f++) COL(oc, f) = y[f];
     if (k > 0) {
@@ -364,18 +378,18 @@ B3X_HD void c_joint_gather(const Args& a, int tile, CollideShared& sh, int q0, i
                                   res_word(a, tile, a.L.joint_off / 4 + (size_t)(q0 + qq) * NVW + c, l));
         }
         async_wait();
-        return;
-    }
-    for (int l = w; l < kLanes; l += kCtaWarps) {
-        const int n = (sh.nj[l] < q0 + Q ? sh.nj[l] : q0 + Q) - q0;
-        if (n <= 0) continue;
-        const float* src = world_words(a, tile * kLanes + l) + (a.L.joint_off + (size_t)B3X_JOINT_BYTES * q0) / 4;
-        for (int idx = i; idx < n * NVW; idx += 32) {
-            const int qq = idx / NVW, c = idx - qq * NVW;
-            async_copy4_world(joint_row(sh, qq, l) + c, src + idx);
+    } else {
+        for (int l = w; l < kLanes; l += kCtaWarps) {
+            const int n = (sh.nj[l] < q0 + Q ? sh.nj[l] : q0 + Q) - q0;
+            if (n <= 0) continue;
+            const float* src = world_words(a, tile * kLanes + l) + (a.L.joint_off + (size_t)B3X_JOINT_BYTES * q0) / 4;
+            for (int idx = i; idx < n * NVW; idx += 32) {
+                const int qq = idx / NVW, c = idx - qq * NVW;
+                async_copy4_world(joint_row(sh, qq, l) + c, src + idx);
+            }
         }
+        async_wait();
     }
-    async_wait();
 }
 
 // Prepare joint q of world l (06_joints.inl:161-202): the solver columns, and
@@ -866,67 +880,91 @@ B3X_HD void collide_tile(X& x, const Args& a, int bt, CollideShared& sh) {
     const int tile = a.tile0 + bt;
     x.each([&](int t) { c_header<kRes>(a, tile, sh, t); });
     x.each([&](int t) { if (t < kLanes) c_record(a, tile, slot, sh, t); });
-    {
-        // bodies: whole body arrays of G worlds per round
-        const int M = sh.maxnb | 1, RS = kRow;
-        const int G = group_size(M * RS, kStageFloats);
-        for (int l0 = 0; l0 < kLanes; l0 += G) {
-            const int Gr = kLanes - l0 < G ? kLanes - l0 : G;
-            x.each([&](int t) {
-                c_gather_group<NYW, kRes>(a, tile, sh, sh.nb, l0, Gr, M, RS, B3X_WORLD_HEADER_BYTES, 0, t);
-                async_wait();
-            });
-            x.each([&](int t) {
-                FOR_GROUP_ITEMS(t, Gr, M, k, g) {
-                    if (k < sh.nb[l0 + g]) c_body(a, slot, sh, k, l0 + g, sh.u.flat + (g * M + k) * RS);
-                }
-            });
-        }
-    }
-    {
-        // shapes and the old contacts' warm-cache words, together when both fit
-        const int Ms = sh.maxns | 1, Mo = sh.maxold | 1;
-        const int per_s = Ms * (NXW + 1), per_o = Mo * NOF;
-        const bool joint_round = kLanes * (per_s + per_o) <= kStageFloats;
-        const int Gs = joint_round ? kLanes : group_size(per_s, kStageFloats);
-        for (int l0 = 0; l0 < kLanes; l0 += Gs) {
-            const int Gr = kLanes - l0 < Gs ? kLanes - l0 : Gs;
-            const int odst = Gr * per_s;
-            x.each([&](int t) {
-                c_gather_group<NXW, kRes>(a, tile, sh, sh.ns, l0, Gr, Ms, NXW + 1, a.L.shape_off, 0, t);
-                if (joint_round) c_gather_old<kRes>(a, tile, sh, l0, Gr, Mo, odst, t);
-                async_wait();
-            });
-            x.each([&](int t) {
-                FOR_GROUP_ITEMS(t, Gr, Ms, k, g) {
-                    if (k < sh.ns[l0 + g]) c_shape(a, slot, sh, k, l0 + g, sh.u.flat + (g * Ms + k) * (NXW + 1));
-                }
-                if (joint_round) {
-                    FOR_GROUP_ITEMS(t, Gr, Mo, k, g) {
-                        if (k < sh.oldn[l0 + g]) {
-                            const float* y = sh.u.flat + odst + (g * Mo + k) * NOF;
-                            c_old_row(a, slot, sh, k, l0 + g, y, y - NOF);
-                        }
-                    }
-                }
-            });
-        }
-        if (!joint_round) {
-            const int Go = group_size(per_o, kStageFloats);
-            for (int l0 = 0; l0 < kLanes; l0 += Go) {
-                const int Gr = kLanes - l0 < Go ? kLanes - l0 : Go;
+    if constexpr (kRes) {
+        // resident columns: each (item, world) reads its row straight from
+        // the columns, consecutive threads one word of consecutive worlds
+        const size_t bw = B3X_WORLD_HEADER_BYTES / 4, sw = a.L.shape_off / 4, cw = a.L.contact_off / 4;
+        x.each([&](int t) {
+            for (int j = t; j < sh.maxnb * kLanes; j += kCta) {
+                const int k = j >> 5, l = j & 31;
+                if (k < sh.nb[l]) c_body(a, slot, sh, k, l, ColRow{res_word(a, tile, bw + (size_t)k * NYW, l)});
+            }
+        });
+        x.each([&](int t) {
+            for (int j = t; j < sh.maxns * kLanes; j += kCta) {
+                const int k = j >> 5, l = j & 31;
+                if (k < sh.ns[l]) c_shape(a, slot, sh, k, l, ColRow{res_word(a, tile, sw + (size_t)k * NXW, l)});
+            }
+            for (int j = t; j < sh.maxold * kLanes; j += kCta) {
+                const int k = j >> 5, l = j & 31;
+                if (k >= sh.oldn[l]) continue;
+                const float* row = res_word(a, tile, cw + (size_t)k * NCW, l);
+                c_old_row(a, slot, sh, k, l, OldColRow{row}, OldColRow{k > 0 ? row - (size_t)NCW * kLanes : row});
+            }
+        });
+    } else {
+        {
+            // bodies: whole body arrays of G worlds per round
+            const int M = sh.maxnb | 1, RS = kRow;
+            const int G = group_size(M * RS, kStageFloats);
+            for (int l0 = 0; l0 < kLanes; l0 += G) {
+                const int Gr = kLanes - l0 < G ? kLanes - l0 : G;
                 x.each([&](int t) {
-                    c_gather_old<kRes>(a, tile, sh, l0, Gr, Mo, 0, t);
+                    c_gather_group<NYW, kRes>(a, tile, sh, sh.nb, l0, Gr, M, RS, B3X_WORLD_HEADER_BYTES, 0, t);
                     async_wait();
                 });
                 x.each([&](int t) {
-                    FOR_GROUP_ITEMS(t, Gr, Mo, k, g) {
-                        if (k < sh.oldn[l0 + g]) {
-                            const float* y = sh.u.flat + (g * Mo + k) * NOF;
-                            c_old_row(a, slot, sh, k, l0 + g, y, y - NOF);
+                    FOR_GROUP_ITEMS(t, Gr, M, k, g) {
+                        if (k < sh.nb[l0 + g]) c_body(a, slot, sh, k, l0 + g, sh.u.flat + (g * M + k) * RS);
+                    }
+                });
+            }
+        }
+        {
+            // shapes and the old contacts' warm-cache words, together when both fit
+            const int Ms = sh.maxns | 1, Mo = sh.maxold | 1;
+            const int per_s = Ms * (NXW + 1), per_o = Mo * NOF;
+            const bool joint_round = kLanes * (per_s + per_o) <= kStageFloats;
+            const int Gs = joint_round ? kLanes : group_size(per_s, kStageFloats);
+            for (int l0 = 0; l0 < kLanes; l0 += Gs) {
+                const int Gr = kLanes - l0 < Gs ? kLanes - l0 : Gs;
+                const int odst = Gr * per_s;
+                x.each([&](int t) {
+                    c_gather_group<NXW, kRes>(a, tile, sh, sh.ns, l0, Gr, Ms, NXW + 1, a.L.shape_off, 0, t);
+                    if (joint_round) c_gather_old<kRes>(a, tile, sh, l0, Gr, Mo, odst, t);
+                    async_wait();
+                });
+                x.each([&](int t) {
+                    FOR_GROUP_ITEMS(t, Gr, Ms, k, g) {
+                        if (k < sh.ns[l0 + g]) c_shape(a, slot, sh, k, l0 + g, sh.u.flat + (g * Ms + k) * (NXW + 1));
+                    }
+                    if (joint_round) {
+                        FOR_GROUP_ITEMS(t, Gr, Mo, k, g) {
+                            if (k < sh.oldn[l0 + g]) {
+                                const float* y = sh.u.flat + odst + (g * Mo + k) * NOF;
+                                c_old_row(a, slot, sh, k, l0 + g, y, y - NOF);
+                            }
                         }
                     }
                 });
+            }
+            if (!joint_round) {
+                const int Go = group_size(per_o, kStageFloats);
+                for (int l0 = 0; l0 < kLanes; l0 += Go) {
+                    const int Gr = kLanes - l0 < Go ? kLanes - l0 : Go;
+                    x.each([&](int t) {
+                        c_gather_old<kRes>(a, tile, sh, l0, Gr, Mo, 0, t);
+                        async_wait();
+                    });
+                    x.each([&](int t) {
+                        FOR_GROUP_ITEMS(t, Gr, Mo, k, g) {
+                            if (k < sh.oldn[l0 + g]) {
+                                const float* y = sh.u.flat + (g * Mo + k) * NOF;
+                                c_old_row(a, slot, sh, k, l0 + g, y, y - NOF);
+                            }
+                        }
+                    });
+                }
             }
         }
     }
@@ -988,19 +1026,8 @@ B3X_HDI float* out_row(OutShared& sh, int l, int kk, int K, int RS) {
 
 // Bodies [k0, k0 + K) of every world: each world's run of B3Body rows,
 // gathered from the caller's array (rows stay untouched until written back).
-template <bool kRes>
 B3X_HD void o_body_gather(const Args& a, int tile, OutShared& sh, int k0, int K, int t) {
     const int w = t >> 5, i = t & 31;
-    if constexpr (kRes) {
-        for (int idx = t; idx < K * NYW * kLanes; idx += kCta) {
-            const int l = idx & 31, r = idx >> 5, kk = r / NYW, c = r - kk * NYW;
-            if (k0 + kk < sh.nb[l])
-                async_copy4_world(out_row(sh, l, kk, K, kRow) + c,
-                                  res_word(a, tile, B3X_WORLD_HEADER_BYTES / 4 + (size_t)(k0 + kk) * NYW + c, l));
-        }
-        async_wait();
-        return;
-    }
     for (int l = w; l < kLanes; l += kCtaWarps) {
         const int n = (sh.nb[l] < k0 + K ? sh.nb[l] : k0 + K) - k0;
         if (n <= 0) continue;
@@ -1013,10 +1040,12 @@ B3X_HD void o_body_gather(const Args& a, int tile, OutShared& sh, int k0, int K,
     async_wait();
 }
 
+
 // Finalize body k of world l (09_step.inl:109-130) in its B3Body row y: the
 // fields the reference's step writes are replaced, the others keep their
 // bytes, so the write-back stores whole rows.
-B3X_HD void o_body(const Args& a, float* slot, int k, int l, float* y) {
+template <class Y>
+B3X_HD void o_body(const Args& a, float* slot, int k, int l, const Y& y) {
     const float* bc = item(slot + a.SP.body, k, NBF) + l;
     const float* kb = item(slot + a.SP.bodyk, k, NBC) + l;
     const float* pb = item(slot + a.SP.bodyp, k, NBP) + l;
@@ -1055,18 +1084,8 @@ B3X_HD void o_bodies(const Args& a, float* slot, OutShared& sh, int k0, int K, i
     }
 }
 
-template <bool kRes>
 B3X_HD void o_body_write(const Args& a, int tile, OutShared& sh, int k0, int K, int t) {
     const int w = t >> 5, i = t & 31;
-    if constexpr (kRes) {
-        for (int idx = t; idx < K * NYW * kLanes; idx += kCta) {
-            const int l = idx & 31, r = idx >> 5, kk = r / NYW, c = r - kk * NYW;
-            if (k0 + kk < sh.nb[l])
-                store_world(res_word(a, tile, B3X_WORLD_HEADER_BYTES / 4 + (size_t)(k0 + kk) * NYW + c, l),
-                            out_row(sh, l, kk, K, kRow)[c]);
-        }
-        return;
-    }
     for (int l = w; l < kLanes; l += kCtaWarps) {
         const int n = (sh.nb[l] < k0 + K ? sh.nb[l] : k0 + K) - k0;
         if (n <= 0) continue;
@@ -1077,6 +1096,7 @@ B3X_HD void o_body_write(const Args& a, int tile, OutShared& sh, int k0, int K, 
         }
     }
 }
+
 
 // Items [k0, k0 + K) of a [item][word][lane] region -> rows, copied
 // asynchronously (`words` words per item, row stride RS >= words).
@@ -1133,17 +1153,17 @@ B3X_HD void o_contact_write(const Args& a, int tile, OutShared& sh, int k0, int 
             if (c < hi || c >= WCA)
                 store_world(res_word(a, tile, a.L.contact_off / 4 + (size_t)(k0 + kk) * NCW + c, l), row[c]);
         }
-        return;
-    }
-    for (int l = w; l < kLanes; l += kCtaWarps) {
-        const int n = (sh.n[l] < k0 + K ? sh.n[l] : k0 + K) - k0;
-        if (n <= 0) continue;
-        float* dst = world_words_w(a, tile * kLanes + l) + (a.L.contact_off + (size_t)B3X_CONTACT_BYTES * k0) / 4;
-        for (int kk = 0; kk < n; kk++) {    // row by row: each row's point count is read once
-            const float* row = out_row(sh, l, kk, K, NCW);
-            const int hi = WP + clampi(b3x_f2i(row[WCNT]), 0, B3_MAX_MANIFOLD) * NQW;
-            for (int c = i; c < NCW; c += 32)
-                if (c < hi || c >= WCA) store_world(dst + kk * NCW + c, row[c]);
+    } else {
+        for (int l = w; l < kLanes; l += kCtaWarps) {
+            const int n = (sh.n[l] < k0 + K ? sh.n[l] : k0 + K) - k0;
+            if (n <= 0) continue;
+            float* dst = world_words_w(a, tile * kLanes + l) + (a.L.contact_off + (size_t)B3X_CONTACT_BYTES * k0) / 4;
+            for (int kk = 0; kk < n; kk++) {    // row by row: each row's point count is read once
+                const float* row = out_row(sh, l, kk, K, NCW);
+                const int hi = WP + clampi(b3x_f2i(row[WCNT]), 0, B3_MAX_MANIFOLD) * NQW;
+                for (int c = i; c < NCW; c += 32)
+                    if (c < hi || c >= WCA) store_world(dst + kk * NCW + c, row[c]);
+            }
         }
     }
 }
@@ -1189,16 +1209,16 @@ B3X_HD void o_joint_write(const Args& a, int tile, float* slot, OutShared& sh, i
             store_world(res_word(a, tile, a.L.joint_off / 4 + (size_t)(q0 + kk) * NVW + c, l),
                         out_row(sh, l, kk, K, NVW)[c]);
         }
-        return;
-    }
-    for (int l = w; l < kLanes; l += kCtaWarps) {
-        const int n = (sh.nj[l] < q0 + K ? sh.nj[l] : q0 + K) - q0;
-        if (n <= 0) continue;
-        float* dst = world_words_w(a, tile * kLanes + l) + (a.L.joint_off + (size_t)B3X_JOINT_BYTES * q0) / 4;
-        for (int kk = 0; kk < n; kk++) {
-            if (!ldi(item(slot + a.SP.joint, q0 + kk, NJF) + l, JOK)) continue;
-            const float* row = out_row(sh, l, kk, K, NVW);
-            for (int c = i; c < NVW; c += 32) store_world(dst + kk * NVW + c, row[c]);
+    } else {
+        for (int l = w; l < kLanes; l += kCtaWarps) {
+            const int n = (sh.nj[l] < q0 + K ? sh.nj[l] : q0 + K) - q0;
+            if (n <= 0) continue;
+            float* dst = world_words_w(a, tile * kLanes + l) + (a.L.joint_off + (size_t)B3X_JOINT_BYTES * q0) / 4;
+            for (int kk = 0; kk < n; kk++) {
+                if (!ldi(item(slot + a.SP.joint, q0 + kk, NJF) + l, JOK)) continue;
+                const float* row = out_row(sh, l, kk, K, NVW);
+                for (int c = i; c < NVW; c += 32) store_world(dst + kk * NVW + c, row[c]);
+            }
         }
     }
 }
@@ -1264,12 +1284,12 @@ B3X_HD void o_header(const Args& a, int tile, float* slot, OutShared& sh, int l)
         *res_word(a, tile, HNC, l) = COL(rec, RN);
         *res_word(a, tile, HOVC, l) = COL(rec, ROVF);
         *res_word(a, tile, HDROP, l) = COL(rec, RDROP);
-        return;
+    } else {
+        float* hw = world_words_w(a, tile * kLanes + l);
+        hw[HNC] = COL(rec, RN);
+        hw[HOVC] = COL(rec, ROVF);
+        hw[HDROP] = COL(rec, RDROP);
     }
-    float* hw = world_words_w(a, tile * kLanes + l);
-    hw[HNC] = COL(rec, RN);
-    hw[HOVC] = COL(rec, ROVF);
-    hw[HDROP] = COL(rec, RDROP);
 }
 
 template <bool kRes, class X>
@@ -1278,12 +1298,22 @@ B3X_HD void out_tile(X& x, const Args& a, int bt, OutShared& sh) {
     const int tile = a.tile0 + bt;
     x.each([&](int t) { if (t < kLanes) o_record(a, slot, sh, t); });
     x.each([&](int t) { if (t == 0) o_maxima(sh); });
-    {
+    if constexpr (kRes) {
+        // resident columns: each (body, world) is finalized in place, one
+        // word of consecutive worlds per warp access
+        const size_t bw = B3X_WORLD_HEADER_BYTES / 4;
+        x.each([&](int t) {
+            for (int j = t; j < sh.maxnb * kLanes; j += kCta) {
+                const int k = j >> 5, l = j & 31;
+                if (k < sh.nb[l]) o_body(a, slot, k, l, ColRow{res_word(a, tile, bw + (size_t)k * NYW, l)});
+            }
+        });
+    } else {
         const int K = out_items(sh.maxnb, kRow);
         for (int k0 = 0; k0 < sh.maxnb; k0 += K) {
-            x.each([&](int t) { o_body_gather<kRes>(a, tile, sh, k0, K, t); });
+            x.each([&](int t) { o_body_gather(a, tile, sh, k0, K, t); });
             x.each([&](int t) { o_bodies(a, slot, sh, k0, K, t); });
-            x.each([&](int t) { o_body_write<kRes>(a, tile, sh, k0, K, t); });
+            x.each([&](int t) { o_body_write(a, tile, sh, k0, K, t); });
         }
     }
     const bool state_only = kRes && (a.flags & kStepStateOnly) != 0;

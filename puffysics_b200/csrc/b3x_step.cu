@@ -229,13 +229,13 @@ __global__ void __launch_bounds__(kLanes) small_step_kernel(Args a, unsigned str
             const float* src = reinterpret_cast<const float*>(sw + (size_t)rg * stride_words);
             for (unsigned w = rw; w < 2 * words; w += kRoundWords) store_world(res_word(a, tile, w, lt + rg), src[w]);
         }
-        return;
-    }
-    for (int l = 0; l < kSmallWorlds; l++) {
-        if (!((live_mask >> l) & 1u)) continue;
-        uint64_t* dst = world_ptr(l);
-        const uint64_t* src = sw + (size_t)l * stride_words;
-        for (unsigned idx = lane; idx < words; idx += kLanes) dst[idx] = src[idx];
+    } else {
+        for (int l = 0; l < kSmallWorlds; l++) {
+            if (!((live_mask >> l) & 1u)) continue;
+            uint64_t* dst = world_ptr(l);
+            const uint64_t* src = sw + (size_t)l * stride_words;
+            for (unsigned idx = lane; idx < words; idx += kLanes) dst[idx] = src[idx];
+        }
     }
 }
 
