@@ -85,7 +85,7 @@ def parse_args():
     ap.add_argument("--no-graph", action="store_true", help="e2e with direct calls instead of a CUDA graph")
     ap.add_argument("--no-per-thread-path", action="store_true",
                     help="skip the timing of the per-thread device b3_step after the main measurement")
-    ap.add_argument("--path", default="aos", choices=["columns", "columns_state_only", "aos"],
+    ap.add_argument("--path", default="columns", choices=["columns", "columns_state_only", "aos"],
                     help="world layout of the headline: the AoS drop-in, or resident columns (b3x_engine_*), "
                          "optionally with the state-only write-back")
     ap.add_argument("--no-other-paths", action="store_true",
@@ -684,6 +684,8 @@ def roofline(res, kern_s, local):
     # small-world kernel: one launch for any batch size
     small_path = engine.step_launches(cfg.caps, 1 << 20, local) == 1
     kname = "small_step_kernel" if small_path else "step_kernel"
+    if res["path"].startswith("columns"):
+        kname += "_columns"
     traffic = read_number(TRAFFIC_FILE_FMT % (kname, cfg.name), "dram_bytes_per_world_step")
     flops_ws = read_number(FLOPS_FILE, "%s_flops_per_world_step" % cfg.name)
     sm_max = (peaks.get("sm_max_mhz") or 1965.0)
@@ -694,7 +696,10 @@ def roofline(res, kern_s, local):
             "kernel": ("b3x::small_step_kernel (worlds staged whole in shared memory, one thread per "
                        "world; %d launch per step)" if small_path else
                        "b3x::step_kernel (collide, solve and write-back phases; %d launch(es) per step)")
-                      % res["step_launches"], "kernel_ms": kern_s * 1e3,
+                      % res["step_launches"] + (" on the resident world columns" if res["path"].startswith("columns")
+                                                else " on the caller's AoS worlds"),
+            "kernel_ms": kern_s * 1e3,
+            "traffic_source": "profiles/%s_%s.md" % (kname, cfg.name) if traffic else None,
             "algorithmic_bytes_per_launch": alg_bytes / res["step_launches"],
             "algorithmic_bytes_per_world_step": bytes_world,
             "per_launch": "achieved = algorithmic bytes of the step's launches / their summed event time; "

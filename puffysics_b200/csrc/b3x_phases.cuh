@@ -192,6 +192,13 @@ B3X_HDI int old_word(int i) {
         : i == OTWI ? WTWI : i < OFEAT ? WRI + (i - ORI) : i < ONI ? PW(i - OFEAT, QFEAT) : PW(i - ONI, QNI);
 }
 
+// The N words of a struct row of one world in the resident columns into y.
+template <int N>
+B3X_HDI void load_row(const float* col, float (&y)[N]) {
+#pragma unroll
+    for (int f = 0; f < N; f++) y[f] = col[(size_t)f * kLanes];
+}
+
 // A struct row of one world in the resident columns: word f at p[f * 32].
 struct ColRow {
     float* p;
@@ -741,12 +748,14 @@ B3X_HD void c_build(const Args& a, float* slot, CollideShared& sh, int t, const 
         const float* si = item(sc, i, NSF) + l;
         const float* sj = item(sc, j, NSF) + l;
         const float* mo = item(slot + a.SP.mani, ci, NMW) + l;
+        // every point slot is read (those past the count hold stale
+        // values that nothing below uses), so the loads need not wait for
+        // the count
         Mani m;
         m.count = clampi(ldi(mo, MCNT), 0, B3_MAX_MANIFOLD);
         m.normal = ld3(mo, MN);
 #pragma unroll
         for (int q = 0; q < B3_MAX_MANIFOLD; q++) {
-            if (q >= m.count) continue;
             m.pa[q] = ld3(mo, MPA + 3 * q);
             m.pb[q] = ld3(mo, MPB + 3 * q);
             m.sep[q] = COL(mo, MSEP + q);
@@ -884,22 +893,37 @@ B3X_HD void collide_tile(X& x, const Args& a, int bt, CollideShared& sh) {
         // resident columns: each (item, world) reads its row straight from
         // the columns, consecutive threads one word of consecutive worlds
         const size_t bw = B3X_WORLD_HEADER_BYTES / 4, sw = a.L.shape_off / 4, cw = a.L.contact_off / 4;
+        // (each row is loaded whole into registers first, so that its loads
+        // are in flight together)
         x.each([&](int t) {
             for (int j = t; j < sh.maxnb * kLanes; j += kCta) {
                 const int k = j >> 5, l = j & 31;
-                if (k < sh.nb[l]) c_body(a, slot, sh, k, l, ColRow{res_word(a, tile, bw + (size_t)k * NYW, l)});
+                if (k >= sh.nb[l]) continue;
+                float y[NYW];
+                load_row(res_word(a, tile, bw + (size_t)k * NYW, l), y);
+                c_body(a, slot, sh, k, l, (const float*)y);
             }
         });
         x.each([&](int t) {
             for (int j = t; j < sh.maxns * kLanes; j += kCta) {
                 const int k = j >> 5, l = j & 31;
-                if (k < sh.ns[l]) c_shape(a, slot, sh, k, l, ColRow{res_word(a, tile, sw + (size_t)k * NXW, l)});
+                if (k >= sh.ns[l]) continue;
+                float y[NXW];
+                load_row(res_word(a, tile, sw + (size_t)k * NXW, l), y);
+                c_shape(a, slot, sh, k, l, (const float*)y);
             }
             for (int j = t; j < sh.maxold * kLanes; j += kCta) {
                 const int k = j >> 5, l = j & 31;
                 if (k >= sh.oldn[l]) continue;
                 const float* row = res_word(a, tile, cw + (size_t)k * NCW, l);
-                c_old_row(a, slot, sh, k, l, OldColRow{row}, OldColRow{k > 0 ? row - (size_t)NCW * kLanes : row});
+                float y[NOF];
+#pragma unroll
+                for (int f = 0; f < NOF; f++) y[f] = row[(size_t)old_word(f) * kLanes];
+                const float* prow = k > 0 ? row - (size_t)NCW * kLanes : row;
+                float prev[OSB + 1];
+                prev[OSA] = prow[(size_t)WSA * kLanes];
+                prev[OSB] = prow[(size_t)WSB * kLanes];
+                c_old_row(a, slot, sh, k, l, (const float*)y, (const float*)prev);
             }
         });
     } else {
@@ -1111,7 +1135,8 @@ B3X_HD void o_stage(const float* src, OutShared& sh, int K, int words, int RS, i
 // The words of contact k of world l the workspace does not keep, from the
 // body columns and the step softness, as b3_prepare_one_contact
 // (08_contacts.inl:234-245) computes them.
-B3X_HD void o_contact_fill(const Args& a, float* slot, int l, float* row) {
+template <class Y>
+B3X_HD void o_contact_fill(const Args& a, float* slot, int l, const Y& row) {
     const int ba = b3x_f2i(row[WBA]), bb = b3x_f2i(row[WBB]);
     const float* ca = item(slot + a.SP.bodyk, ba, NBC) + l;
     const float* cb = item(slot + a.SP.bodyk, bb, NBC) + l;
@@ -1141,32 +1166,21 @@ B3X_HD void o_contacts(const Args& a, float* slot, OutShared& sh, int k0, int K,
 // Contacts [k0, k0 + K) of every world.  Point slots past a contact's point
 // count keep their previous bytes, as in the reference (b3_contact_from_mani
 // writes only the manifold's points).
-template <bool kRes>
 B3X_HD void o_contact_write(const Args& a, int tile, OutShared& sh, int k0, int K, int t) {
     const int w = t >> 5, i = t & 31;
-    if constexpr (kRes) {
-        for (int idx = t; idx < K * NCW * kLanes; idx += kCta) {
-            const int l = idx & 31, r = idx >> 5, kk = r / NCW, c = r - kk * NCW;
-            if (k0 + kk >= sh.n[l]) continue;
+    for (int l = w; l < kLanes; l += kCtaWarps) {
+        const int n = (sh.n[l] < k0 + K ? sh.n[l] : k0 + K) - k0;
+        if (n <= 0) continue;
+        float* dst = world_words_w(a, tile * kLanes + l) + (a.L.contact_off + (size_t)B3X_CONTACT_BYTES * k0) / 4;
+        for (int kk = 0; kk < n; kk++) {    // row by row: each row's point count is read once
             const float* row = out_row(sh, l, kk, K, NCW);
             const int hi = WP + clampi(b3x_f2i(row[WCNT]), 0, B3_MAX_MANIFOLD) * NQW;
-            if (c < hi || c >= WCA)
-                store_world(res_word(a, tile, a.L.contact_off / 4 + (size_t)(k0 + kk) * NCW + c, l), row[c]);
-        }
-    } else {
-        for (int l = w; l < kLanes; l += kCtaWarps) {
-            const int n = (sh.n[l] < k0 + K ? sh.n[l] : k0 + K) - k0;
-            if (n <= 0) continue;
-            float* dst = world_words_w(a, tile * kLanes + l) + (a.L.contact_off + (size_t)B3X_CONTACT_BYTES * k0) / 4;
-            for (int kk = 0; kk < n; kk++) {    // row by row: each row's point count is read once
-                const float* row = out_row(sh, l, kk, K, NCW);
-                const int hi = WP + clampi(b3x_f2i(row[WCNT]), 0, B3_MAX_MANIFOLD) * NQW;
-                for (int c = i; c < NCW; c += 32)
-                    if (c < hi || c >= WCA) store_world(dst + kk * NCW + c, row[c]);
-            }
+            for (int c = i; c < NCW; c += 32)
+                if (c < hi || c >= WCA) store_world(dst + kk * NCW + c, row[c]);
         }
     }
 }
+
 
 // The solver's results into the prepared B3Joint row of joint q of world l:
 // linear impulse; angular impulse (weld); axial and hinge impulses and the
@@ -1305,7 +1319,19 @@ B3X_HD void out_tile(X& x, const Args& a, int bt, OutShared& sh) {
         x.each([&](int t) {
             for (int j = t; j < sh.maxnb * kLanes; j += kCta) {
                 const int k = j >> 5, l = j & 31;
-                if (k < sh.nb[l]) o_body(a, slot, k, l, ColRow{res_word(a, tile, bw + (size_t)k * NYW, l)});
+                if (k >= sh.nb[l]) continue;
+                // the row in registers (loads in flight together), finalized,
+                // then the words a finalize can write stored back (the
+                // others keep their bytes; rewriting an unchanged word
+                // stores the same bits)
+                float* col = res_word(a, tile, bw + (size_t)k * NYW, l);
+                float y[NYW];
+                load_row(col, y);
+                o_body(a, slot, k, l, (float*)y);
+#pragma unroll
+                for (int f = YPOS; f < YIM; f++) col[(size_t)f * kLanes] = y[f];
+#pragma unroll
+                for (int f = YIW; f < YIW + 9; f++) col[(size_t)f * kLanes] = y[f];
             }
         });
     } else {
@@ -1321,7 +1347,44 @@ B3X_HD void out_tile(X& x, const Args& a, int bt, OutShared& sh) {
         x.each([&](int t) { o_contact_state(a, tile, slot, sh, t); });
         x.each([&](int t) { o_joint_state(a, tile, slot, sh, t); });
     }
-    if (!state_only) {
+    if constexpr (kRes) {
+        if (!state_only) {
+            // resident columns: a contact's words [0, kCW) are the workspace
+            // item's (same [item][word][lane] order: one line per word),
+            // copied straight across (point words up to the point count);
+            // then the words the workspace does not keep are derived in place
+            const size_t cw = a.L.contact_off / 4;
+            x.each([&](int t) {
+                // thread t: world lane t % 32, words t / 32 + 4i of each of
+                // its contacts; a run of words is loaded before it is stored
+                // (the workspace and the columns are distinct memory)
+                constexpr int kRun = (kCW + kCtaWarps - 1) / kCtaWarps;
+                const int l = t & 31, w0 = t >> 5;
+                for (int k = 0; k < sh.n[l]; k++) {
+                    const float* co = item(slot + a.SP.cont, k, kCI) + l;
+                    const int hi = WP + clampi(ldi(co, WCNT), 0, B3_MAX_MANIFOLD) * NQW;
+                    float* dst = res_word(a, tile, cw + (size_t)k * NCW, l);
+                    float v[kRun];
+#pragma unroll
+                    for (int i = 0; i < kRun; i++) {
+                        const int c = w0 + i * kCtaWarps;
+                        v[i] = c < kCW ? COL(co, c) : 0.0f;
+                    }
+#pragma unroll
+                    for (int i = 0; i < kRun; i++) {
+                        const int c = w0 + i * kCtaWarps;
+                        if (c < kCW && (c < hi || c >= WCA)) store_world(dst + (size_t)c * kLanes, v[i]);
+                    }
+                }
+            });
+            x.each([&](int t) {
+                for (int j = t; j < sh.maxn * kLanes; j += kCta) {
+                    const int k = j >> 5, l = j & 31;
+                    if (k < sh.n[l]) o_contact_fill(a, slot, l, ColRow{res_word(a, tile, cw + (size_t)k * NCW, l)});
+                }
+            });
+        }
+    } else {
         const int K = out_items(sh.maxn, NCW);
         for (int k0 = 0; k0 < sh.maxn; k0 += K) {
             const int Kr = sh.maxn - k0 < K ? sh.maxn - k0 : K;
@@ -1329,7 +1392,7 @@ B3X_HD void out_tile(X& x, const Args& a, int bt, OutShared& sh) {
             // fill below overwrites
             x.each([&](int t) { o_stage(item(slot + a.SP.cont, k0, kCI), sh, Kr, kCI, NCW, t); });
             x.each([&](int t) { o_contacts(a, slot, sh, k0, Kr, t); });
-            x.each([&](int t) { o_contact_write<kRes>(a, tile, sh, k0, Kr, t); });
+            x.each([&](int t) { o_contact_write(a, tile, sh, k0, Kr, t); });
         }
     }
     if (!state_only) {
