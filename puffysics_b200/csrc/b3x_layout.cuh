@@ -78,7 +78,7 @@ static_assert(NVW * 4 == B3X_JOINT_BYTES, "joint word layout");
 // header parameters, contact / static-contact softness of the step)
 enum : int {
     RLIVE = 0, RNB = 1, RNS = 2, ROLDN = 3, RNJ = 4, RN = 5, ROVF = 6, RDROP = 7, RSPEED = 8, RRT = 9,
-    RMAXLIN = 10, RCS = 11, RSS = 14, RROUNDS = 17, NRF = 18
+    RMAXLIN = 10, RCS = 11, RSS = 14, NRF = 17
 };
 // body velocities (region body): the fields every contact and joint row
 // updates
@@ -156,44 +156,11 @@ static inline bool layout_from_signature(unsigned long long sig, Layout* L) {
 // manifolds of a pair window wait in region mani until their contact slots
 // are known.
 struct Space {
-    unsigned long long rec, body, bodyp, bodyk, konst, pose, shape, old, cont, mani, joint, jimg, cpos, cmap, occ,
-        bpm, tile_words;
-    int sched;   // contacts stored in solve-schedule positions (see below)
-    int posC;    // contact item slots of region cont
+    unsigned long long rec, body, bodyp, bodyk, konst, pose, shape, old, cont, mani, joint, jimg, tile_words;
 };
-
-// Scheduled contact solve.  Gauss-Seidel over a world's contacts only needs
-// every dynamic body to see its contacts in index order; contacts with no
-// dynamic body in common commute.  With large contact capacities the
-// collide phase therefore places each world's contact k at a position
-// p = kSchedWays * round + way: its round is the first one after the rounds
-// of the earlier contacts on its dynamic bodies that still has a free way,
-// and the ways of a round are taken in order.  The solve then runs a round
-// on kSchedWays warps at once, warp w taking position kSchedWays * r + w of
-// every world, with a block barrier between rounds: each body still receives
-// the reference's sequence of updates.  Regions of a scheduled slot: cont
-// holds kSchedWays * C positions (a world uses fewer than kSchedWays times
-// its rounds), cpos maps contact index -> position, cmap position -> index,
-// and occ packs the number of taken ways of each round (4 bits, 8 rounds a
-// word).
-constexpr int kSchedWays = 4;
-B3X_HDI bool sched_layout(const Layout& L) { return L.C >= 64 && L.C <= 128 && L.B <= 128; }
-B3X_HDI int occ_words(const Layout& L) { return (L.C + 7) / 8; }
-
-// Whole-step broadphase.  When the tile's shape AABBs fit the collide
-// staging area (6 words per shape and world), the AABB overlap of every
-// shape pair of every world is tested once per step from shared memory, and
-// the bits of the pairs that overlap go to region bpm ([word][lane], 32
-// pairs of the lexicographic order a word); the pair windows then filter
-// only those pairs.
-constexpr int kStageWords = 12 * 1024;   // the collide staging area (floats)
-B3X_HDI bool full_broadphase(const Layout& L) { return 6 * L.S * kLanes <= kStageWords && L.S >= 2; }
-B3X_HDI int pair_words(const Layout& L) { return (L.S * (L.S - 1) / 2 + 31) / 32; }
 
 static inline Space space_from_layout(const Layout& L) {
     Space s;
-    s.sched = sched_layout(L) ? 1 : 0;
-    s.posC = s.sched ? kSchedWays * L.C : L.C;
     unsigned long long w = 0;
     auto take = [&](unsigned long long items, int fields) {
         unsigned long long at = w;
@@ -208,14 +175,10 @@ static inline Space space_from_layout(const Layout& L) {
     s.pose = take(L.B, NPF);
     s.shape = take(L.S, NSF);
     s.old = take(L.C, NOF);
-    s.cont = take((unsigned long long)s.posC, kCI);
+    s.cont = take(L.C, kCI);
     s.mani = take(kPairWindow, NMW);
     s.joint = take(L.J, NJF);
     s.jimg = take(L.J, NVW);
-    s.cpos = s.sched ? take(L.C, 1) : 0;
-    s.cmap = s.sched ? take((unsigned long long)s.posC, 1) : 0;
-    s.occ = s.sched ? take((unsigned long long)occ_words(L), 1) : 0;
-    s.bpm = full_broadphase(L) ? take((unsigned long long)pair_words(L), 1) : 0;
     s.tile_words = (w + 63) & ~63ull;   // 256-byte aligned slots
     return s;
 }
@@ -295,14 +258,6 @@ B3X_HDI float ldg(const float* p) {
 #endif
 }
 
-// Load that bypasses L1 (data another warp of the block wrote through L2).
-B3X_HDI float ldcg(const float* p) {
-#if defined(__CUDA_ARCH__)
-    return __ldcg(p);
-#else
-    return *p;
-#endif
-}
 // ---- bit helpers (device intrinsics or portable equivalents) --------------------
 B3X_HDI int popc32(uint32_t x) {
 #if defined(__CUDA_ARCH__)
@@ -379,13 +334,6 @@ B3X_HDI void shared_or(uint32_t* p, uint32_t v) {
     atomicOr(p, v);
 #else
     *p |= v;
-#endif
-}
-B3X_HDI void shared_and(uint32_t* p, uint32_t v) {
-#if defined(__CUDA_ARCH__)
-    atomicAnd(p, v);
-#else
-    *p &= v;
 #endif
 }
 

@@ -29,7 +29,7 @@ constexpr int kCta = 128;            // threads of a collide / write-back block
 constexpr int kCtaWarps = kCta / 32;
 constexpr int kRow = NYW + 1;        // staged struct row (odd: conflict-free columns)
 // Collide staging area: rows of caller structs gathered for a group of worlds.
-constexpr int kStageFloats = kStageWords;
+constexpr int kStageFloats = 12 * 1024;
 
 // ---- block state ------------------------------------------------------------------
 struct CollideShared {
@@ -50,7 +50,6 @@ struct CollideShared {
     uint32_t wmask[kPairWindow];
     int off[kPairWindow + 1];
     int maxc, total;
-    int rounds[kLanes];                          // schedule rounds of world l (scheduled layouts)
     union {
         float hdr[kLanes][NHW];                  // world headers (17: odd)
         float flat[kStageFloats];                // gathered struct rows of a group of worlds
@@ -60,8 +59,7 @@ struct CollideShared {
 
 struct OutShared {
     int live[kLanes], nb[kLanes], n[kLanes], nj[kLanes];
-    int np[kLanes];                              // contact positions of world l to walk
-    int maxnb, maxn, maxnj, maxnp;
+    int maxnb, maxn, maxnj;
     float flat[kStageFloats];                    // rows of several items of every world
 };
 
@@ -72,18 +70,6 @@ B3X_HDI float* world_words_w(const Args& a, int wi) {
     return reinterpret_cast<float*>(a.data + (size_t)wi * a.stride + a.offset);
 }
 B3X_HDI float* slot_of(const Args& a, int bt) { return a.ws + (size_t)bt * a.SP.tile_words; }
-
-// The contact schedule's collide-time state (scheduled layouts), in the
-// dynamic shared memory after CollideShared: the taken ways of each round of
-// world l (occ, [word][lane], 4 bits a round) and, per body, one more than
-// the last round that updates it (last, [body][lane] bytes).
-B3X_HDI size_t sched_state_bytes(const Layout& L) {
-    return sched_layout(L) ? (size_t)occ_words(L) * kLanes * 4 + (size_t)L.B * kLanes : 0;
-}
-B3X_HDI uint32_t* sched_occ(CollideShared& sh) { return reinterpret_cast<uint32_t*>(&sh + 1); }
-B3X_HDI unsigned char* sched_last(CollideShared& sh, const Layout& L) {
-    return reinterpret_cast<unsigned char*>(sched_occ(sh) + (size_t)occ_words(L) * kLanes);
-}
 // Word w of the B3World of lane l of tile `tile` in the resident world
 // columns ([tile][word][lane]: one word of a tile's 32 worlds is one
 // contiguous 128-byte line).
@@ -139,13 +125,6 @@ B3X_HD void c_record(const Args& a, int tile, float* slot, CollideShared& sh, in
     sh.nj[l] = nj;
     sh.n[l] = 0;
     sh.sorted[l] = 1;
-    sh.rounds[l] = 0;
-    if (a.SP.sched) {
-        uint32_t* occ = sched_occ(sh);
-        unsigned char* last = sched_last(sh, L);
-        for (int w = 0; w < occ_words(L); w++) occ[w * kLanes + l] = 0u;
-        for (int b = 0; b < L.B; b++) last[b * kLanes + l] = 0;
-    }
     sh.ovf[l] = live ? b3x_f2i(hw[HOVC]) : 0;
     sh.drop[l] = live ? b3x_f2i(hw[HDROP]) : 0;
     for (int c = 0; c < 3; c++) sh.grav[l][c] = live ? hw[HGRAV + c] : 0.0f;
@@ -542,120 +521,55 @@ B3X_HDI int pair_of(int p, int ns) {
     return i | ((i + 1 + p) << 16);
 }
 
-// Window state; with the whole-step broadphase (pre) the window's
-// candidate bits start as its pairs' AABB overlaps (pair windows and bpm
-// words both start at multiples of 32 pairs; words past this step's pairs
-// are not read).
-B3X_HD void c_window_setup(const Args& a, const float* slot, CollideShared& sh, int p0, int npairs, bool pre, int t) {
+B3X_HD void c_window_setup(CollideShared& sh, int p0, int npairs, int t) {
     if (t < kPairWindow) {
         sh.ptab[t] = p0 + t < npairs ? pair_of(p0 + t, sh.maxns) : -1;
     }
     if (t < kLanes) {
         for (int c = 0; c < kPairWindow / 32; c++) {
-            const int w = (p0 >> 5) + c;
-            sh.cmask[t][c] = pre && w < (npairs + 31) / 32 ? b3x_f2u(slot[a.SP.bpm + (size_t)w * kLanes + t]) : 0u;
+            sh.cmask[t][c] = 0;
             sh.nmask[t][c] = 0;
         }
     }
 }
 
-// The AABB overlap of a pair (08_contacts.inl:44-58, its first test).
-B3X_HDI bool aabb_overlap(B3Vec3 lo_i, B3Vec3 hi_i, B3Vec3 lo_j, B3Vec3 hi_j) {
-    return lo_i.x <= hi_j.x && hi_i.x >= lo_j.x && lo_i.y <= hi_j.y && hi_i.y >= lo_j.y && lo_i.z <= hi_j.z
-        && hi_i.z >= lo_j.z;
-}
-
-// Whole-step broadphase (full_broadphase): the tile's AABBs into the staging
-// area ([shape][word][lane], 6 words: lo, hi), then for each (bpm word,
-// world) the AABB overlaps of its 32 pairs as bits.  Pairs with a shape past
-// the world's count do not overlap.
-B3X_HD void c_stage_aabbs(const Args& a, const float* slot, CollideShared& sh, int t) {
-    const float* sc = slot + a.SP.shape;
-    const int n = sh.maxns * 6 * kLanes;
-    for (int idx = t; idx < n; idx += kCta) {
-        const int l = idx & 31, r = idx >> 5, s = r / 6, f = r - s * 6;
-        async_copy4(sh.u.flat + idx, item(sc, s, NSF) + (size_t)(SLO + f) * kLanes + l);
-    }
-    async_wait();
-}
-
-B3X_HD void c_pair_bits(const Args& a, float* slot, CollideShared& sh, int t) {
-    const int ns_max = sh.maxns;
-    const int npairs = ns_max * (ns_max - 1) / 2;
-    const int nw = (npairs + 31) / 32;
-    for (int idx = t; idx < nw * kLanes; idx += kCta) {
-        const int w = idx >> 5, l = idx & 31;
-        const int ns = sh.ns[l];
-        const int pr = pair_of(w * 32, ns_max);
-        int i = pr & 0xffff, j = pr >> 16;
-        uint32_t bits = 0u;
-        const int nbits = npairs - w * 32 < 32 ? npairs - w * 32 : 32;
-        for (int b = 0; b < nbits; b++) {
-            if (j < ns) {
-                const float* bi = sh.u.flat + (size_t)i * 6 * kLanes + l;
-                const float* bj = sh.u.flat + (size_t)j * 6 * kLanes + l;
-                if (aabb_overlap(b3_v(bi[0], bi[kLanes], bi[2 * kLanes]), b3_v(bi[3 * kLanes], bi[4 * kLanes], bi[5 * kLanes]),
-                        b3_v(bj[0], bj[kLanes], bj[2 * kLanes]), b3_v(bj[3 * kLanes], bj[4 * kLanes], bj[5 * kLanes])))
-                    bits |= 1u << b;
-            }
-            if (++j == ns_max) {
-                i++;
-                j = i + 1;
-            }
-        }
-        slot[a.SP.bpm + (size_t)w * kLanes + l] = b3x_u2f(bits);
-    }
-}
-
-// The broadphase's tests after the AABB overlap (08_contacts.inl:44-58,
-// 94-104): different bodies, not both static, category / mask, no joint
-// between the bodies that disables collision.
-B3X_HDI bool pair_filter(const Args& a, const float* slot, const CollideShared& sh, const float* si, const float* sj,
-        int l) {
-    const int bi = ldi(si, SBODY), bj = ldi(sj, SBODY);
-    if (bi == bj) return false;
-    const float* kb = slot + a.SP.bodyk + l;
-    if (ldi(item(kb, bi, NBC), BTYPE) == B3_STATIC && ldi(item(kb, bj, NBC), BTYPE) == B3_STATIC) return false;
-    const uint64_t cat_i = (uint64_t)b3x_f2u(COL(si, SCAT)) | ((uint64_t)b3x_f2u(COL(si, SCAT + 1)) << 32);
-    const uint64_t msk_i = (uint64_t)b3x_f2u(COL(si, SMASK)) | ((uint64_t)b3x_f2u(COL(si, SMASK + 1)) << 32);
-    const uint64_t cat_j = (uint64_t)b3x_f2u(COL(sj, SCAT)) | ((uint64_t)b3x_f2u(COL(sj, SCAT + 1)) << 32);
-    const uint64_t msk_j = (uint64_t)b3x_f2u(COL(sj, SMASK)) | ((uint64_t)b3x_f2u(COL(sj, SMASK + 1)) << 32);
-    if ((cat_i & msk_j) == 0 || (cat_j & msk_i) == 0) return false;
-    const float* jc = slot + a.SP.joint + l;
-    for (int q = 0; q < sh.nj[l]; q++) {
-        const float* jo = item(jc, q, NJF);
-        const int ja = ldi(jo, JBA), jb = ldi(jo, JBB);
-        if (!ldi(jo, JCC) && ((ja == bi && jb == bj) || (ja == bj && jb == bi))) return false;
-    }
-    return true;
-}
-
 // Broadphase of window pair pp for world l: the reference's predicate
 // (08_contacts.inl:44-58; AABB overlap first, the side-effect-free tests in
 // a cheaper order) with its joint-connection filter (08_contacts.inl:94-104).
-// With the whole-step broadphase (pre) the window's bits already hold the
-// overlapping pairs, and the filters clear the ones they reject.
-B3X_HD void c_broadphase(const Args& a, float* slot, CollideShared& sh, int npw, bool pre, int t) {
+B3X_HD void c_broadphase(const Args& a, float* slot, CollideShared& sh, int npw, int t) {
     const float* sc = slot + a.SP.shape;
     for (int idx = t; idx < npw * kLanes; idx += kCta) {
         const int pp = idx >> 5, l = idx & 31;
-        const uint32_t bit = 1u << (pp & 31);
-        if (pre && !(sh.cmask[l][pp >> 5] & bit)) continue;
         const int pr = sh.ptab[pp];
         if (pr < 0) continue;
         const int i = pr & 0xffff, j = pr >> 16;
         if (j >= sh.ns[l]) continue;
         const float* si = item(sc, i, NSF) + l;
         const float* sj = item(sc, j, NSF) + l;
-        if (!pre && !aabb_overlap(ld3(si, SLO), ld3(si, SHI), ld3(sj, SLO), ld3(sj, SHI))) continue;
-        if (!pair_filter(a, slot, sh, si, sj, l)) {
-            if (pre) shared_and(&sh.cmask[l][pp >> 5], ~bit);
+        const B3Vec3 lo_i = ld3(si, SLO), hi_i = ld3(si, SHI), lo_j = ld3(sj, SLO), hi_j = ld3(sj, SHI);
+        if (!(lo_i.x <= hi_j.x && hi_i.x >= lo_j.x && lo_i.y <= hi_j.y && hi_i.y >= lo_j.y && lo_i.z <= hi_j.z
+                && hi_i.z >= lo_j.z))
             continue;
+        const int bi = ldi(si, SBODY), bj = ldi(sj, SBODY);
+        if (bi == bj) continue;
+        const float* kb = slot + a.SP.bodyk + l;
+        if (ldi(item(kb, bi, NBC), BTYPE) == B3_STATIC && ldi(item(kb, bj, NBC), BTYPE) == B3_STATIC) continue;
+        const uint64_t cat_i = (uint64_t)b3x_f2u(COL(si, SCAT)) | ((uint64_t)b3x_f2u(COL(si, SCAT + 1)) << 32);
+        const uint64_t msk_i = (uint64_t)b3x_f2u(COL(si, SMASK)) | ((uint64_t)b3x_f2u(COL(si, SMASK + 1)) << 32);
+        const uint64_t cat_j = (uint64_t)b3x_f2u(COL(sj, SCAT)) | ((uint64_t)b3x_f2u(COL(sj, SCAT + 1)) << 32);
+        const uint64_t msk_j = (uint64_t)b3x_f2u(COL(sj, SMASK)) | ((uint64_t)b3x_f2u(COL(sj, SMASK + 1)) << 32);
+        if ((cat_i & msk_j) == 0 || (cat_j & msk_i) == 0) continue;
+        bool connected = false;
+        const float* jc = slot + a.SP.joint + l;
+        for (int q = 0; q < sh.nj[l]; q++) {
+            const float* jo = item(jc, q, NJF);
+            const int ja = ldi(jo, JBA), jb = ldi(jo, JBB);
+            if (!ldi(jo, JCC) && ((ja == bi && jb == bj) || (ja == bj && jb == bi))) connected = true;
         }
-        if (!pre) shared_or(&sh.cmask[l][pp >> 5], bit);
+        if (connected) continue;
+        shared_or(&sh.cmask[l][pp >> 5], 1u << (pp & 31));
     }
 }
-
 
 // Per-world item counts -> the (item, world) enumeration (wmask, off, maxc,
 // total).  Run by the 32 threads of warp 0, lane = world.
@@ -721,45 +635,7 @@ B3X_HDI void decode(const CollideShared& sh, int idx, int& ci, int& l) {
 // overflow is counted -- so the r-th manifold of the window takes slot
 // nbase + r.  Then the (contact, world) enumeration of the contact build.
 // Warp 0, lane = world.
-// Schedule positions of world l's new contacts [base, base + kept) in
-// index order (scheduled layouts; see sched_layout): the first round at or
-// after the last round of each of its dynamic bodies (bodies the solve
-// writes) with a free way.  Rounds never exceed the contacts placed, so the
-// scan ends within the capacity.
-B3X_HD void c_schedule(const Args& a, float* slot, CollideShared& sh, int base, int kept, int l) {
-    uint32_t* occ = sched_occ(sh);
-    unsigned char* last = sched_last(sh, a.L);
-    const float* sc = slot + a.SP.shape + l;
-    const float* kb = slot + a.SP.bodyk + l;
-    const int nb = sh.nb[l];
-    int R = sh.rounds[l];
-    for (int r = 0; r < kept; r++) {
-        const int ci = nth_bit64(sh.nmask[l], r);
-        const int pr = sh.ptab[nth_bit64(sh.cmask[l], ci)];
-        const int i = pr & 0xffff, j = pr >> 16;
-        const int bi = ldi(item(sc, i, NSF), SBODY), bj = ldi(item(sc, j, NSF), SBODY);
-        const bool di = bi >= 0 && bi < nb && (b3x_f2u(COL(item(kb, bi, NBC), BFLAGS)) & B3_FLAG_DYNAMIC) != 0;
-        const bool dj = bj >= 0 && bj < nb && (b3x_f2u(COL(item(kb, bj, NBC), BFLAGS)) & B3_FLAG_DYNAMIC) != 0;
-        int rr = 0;
-        if (di) rr = last[bi * kLanes + l];
-        if (dj && last[bj * kLanes + l] > rr) rr = last[bj * kLanes + l];
-        int way;
-        for (;; rr++) {
-            way = (int)((occ[(rr >> 3) * kLanes + l] >> (4 * (rr & 7))) & 15u);
-            if (way < kSchedWays) break;
-        }
-        occ[(rr >> 3) * kLanes + l] += 1u << (4 * (rr & 7));
-        if (di) last[bi * kLanes + l] = (unsigned char)(rr + 1);
-        if (dj) last[bj * kLanes + l] = (unsigned char)(rr + 1);
-        if (rr + 1 > R) R = rr + 1;
-        const int pos = rr * kSchedWays + way;
-        sti(slot + a.SP.cpos + (size_t)(base + r) * kLanes + l, 0, pos);
-        sti(slot + a.SP.cmap + (size_t)pos * kLanes + l, 0, base + r);
-    }
-    sh.rounds[l] = R;
-}
-
-B3X_HD void c_plan(const Args& a, float* slot, CollideShared& sh, int l) {
+B3X_HD void c_plan(const Args& a, CollideShared& sh, int l) {
     int m = 0;
     for (int w = 0; w < kPairWindow / 32; w++) m += popc32(sh.nmask[l][w]);
     const int base = sh.n[l];
@@ -771,7 +647,6 @@ B3X_HD void c_plan(const Args& a, float* slot, CollideShared& sh, int l) {
     }
     sh.nbase[l] = base;
     sh.n[l] = base + kept;
-    if (a.SP.sched) c_schedule(a, slot, sh, base, kept, l);
     enumerate(sh, kept, l);
 }
 
@@ -895,8 +770,7 @@ B3X_HD void c_build(const Args& a, float* slot, CollideShared& sh, int t, const 
         const B3Vec3 ca = ld3(item(slot + a.SP.pose, bi, NPF) + l, PCEN);
         const B3Vec3 cb = ld3(item(slot + a.SP.pose, bj, NPF) + l, PCEN);
         const int cnt = m.count;
-        const int k = sh.nbase[l] + r;   // contact index; p: its workspace position
-        const int p = a.SP.sched ? ldi(slot + a.SP.cpos + (size_t)k * kLanes + l, 0) : k;
+        const int p = sh.nbase[l] + r;
         const B3Vec3 nrm = m.normal;
         const B3Vec3 t1 = b3_perp(nrm);
         const B3Vec3 t2 = b3_cross(t1, nrm);
@@ -914,7 +788,7 @@ B3X_HD void c_build(const Args& a, float* slot, CollideShared& sh, int t, const 
         B3Vec3 ri = b3_v(0.0f, 0.0f, 0.0f);
         const float* oc = old_base + l;
         int first, end;
-        warm_range(oc, sh.oldn[l], sh.sorted[l], i, j, k, first, end);
+        warm_range(oc, sh.oldn[l], sh.sorted[l], i, j, p, first, end);
         for (int kk = first; kk < end; kk++) {
             const float* o = item(oc, kk, NOF);
             if (ldi(o, OSA) != i || ldi(o, OSB) != j) continue;
@@ -1006,12 +880,6 @@ B3X_HD void c_finish(const Args& a, float* slot, CollideShared& sh, int l) {
     sti(rec, RN, sh.n[l]);
     sti(rec, ROVF, sh.ovf[l]);
     sti(rec, RDROP, sh.drop[l]);
-    sti(rec, RROUNDS, sh.rounds[l]);
-    if (a.SP.sched) {
-        const uint32_t* occ = sched_occ(sh);
-        float* oc = slot + a.SP.occ + l;
-        for (int w = 0; w < occ_words(a.L); w++) oc[(size_t)w * kLanes] = b3x_u2f(occ[w * kLanes + l]);
-    }
 }
 
 // The collide phases of tile `bt` of the launch.
@@ -1133,20 +1001,14 @@ B3X_HD void collide_tile(X& x, const Args& a, int bt, CollideShared& sh) {
     }
     const int maxns = sh.maxns;
     const int npairs = maxns * (maxns - 1) / 2;
-    // (one window's pairs are cheaper to test in the window itself)
-    const bool pre = a.SP.bpm != 0 && npairs > kPairWindow;
-    if (pre) {
-        x.each([&](int t) { c_stage_aabbs(a, slot, sh, t); });
-        x.each([&](int t) { c_pair_bits(a, slot, sh, t); });
-    }
     for (int p0 = 0; p0 < npairs; p0 += kPairWindow) {
-        x.each([&](int t) { c_window_setup(a, slot, sh, p0, npairs, pre, t); });
+        x.each([&](int t) { c_window_setup(sh, p0, npairs, t); });
         const int npw = npairs - p0 < kPairWindow ? npairs - p0 : kPairWindow;
-        x.each([&](int t) { c_broadphase(a, slot, sh, npw, pre, t); });
+        x.each([&](int t) { c_broadphase(a, slot, sh, npw, t); });
         x.each([&](int t) { if (t < kLanes) c_count(sh, t); });
         if (sh.total == 0) continue;
         x.each([&](int t) { c_narrow(a, slot, sh, t); });
-        x.each([&](int t) { if (t < kLanes) c_plan(a, slot, sh, t); });
+        x.each([&](int t) { if (t < kLanes) c_plan(a, sh, t); });
         if (sh.total == 0) continue;
         // the staging area is free between the narrowphase and the next window
         const bool stage_old = sh.maxold > 0 && sh.maxold * NOF * kLanes <= kStageFloats;
@@ -1164,32 +1026,18 @@ B3X_HD void o_record(const Args& a, float* slot, OutShared& sh, int l) {
     sh.nb[l] = ldi(rec, RNB);
     sh.n[l] = ldi(rec, RN);
     sh.nj[l] = ldi(rec, RNJ);
-    sh.np[l] = a.SP.sched ? kSchedWays * ldi(rec, RROUNDS) : sh.n[l];
 }
 
 B3X_HD void o_maxima(OutShared& sh) {
-    int mb = 0, mn = 0, mj = 0, mp = 0;
+    int mb = 0, mn = 0, mj = 0;
     for (int l = 0; l < kLanes; l++) {
         mb = sh.nb[l] > mb ? sh.nb[l] : mb;
         mn = sh.n[l] > mn ? sh.n[l] : mn;
         mj = sh.nj[l] > mj ? sh.nj[l] : mj;
-        mp = sh.np[l] > mp ? sh.np[l] : mp;
     }
     sh.maxnb = mb;
     sh.maxn = mn;
     sh.maxnj = mj;
-    sh.maxnp = mp;
-}
-
-// Contact index at workspace position p of world l, or -1 for a position
-// that holds no contact (identity below the count without a schedule).
-B3X_HDI int pos_contact(const Args& a, const float* slot, const OutShared& sh, int p, int l) {
-    if (!a.SP.sched) return p < sh.n[l] ? p : -1;
-    if (p >= sh.np[l]) return -1;
-    const int r = p / kSchedWays, way = p - r * kSchedWays;
-    const uint32_t w = b3x_f2u(slot[a.SP.occ + (size_t)(r >> 3) * kLanes + l]);
-    if (way >= (int)((w >> (4 * (r & 7))) & 15u)) return -1;
-    return ldi(slot + a.SP.cmap + (size_t)p * kLanes + l, 0);
 }
 
 // Items [k0, k0 + K) of every world are staged as rows ((k - k0) * 32 + l) of
@@ -1311,26 +1159,24 @@ B3X_HD void o_contact_fill(const Args& a, float* slot, int l, const Y& row) {
 B3X_HD void o_contacts(const Args& a, float* slot, OutShared& sh, int k0, int K, int t) {
     for (int j = t; j < K * kLanes; j += kCta) {
         const int kk = j >> 5, l = j & 31;
-        if (pos_contact(a, slot, sh, k0 + kk, l) >= 0) o_contact_fill(a, slot, l, out_row(sh, l, kk, K, NCW));
+        if (k0 + kk < sh.n[l]) o_contact_fill(a, slot, l, out_row(sh, l, kk, K, NCW));
     }
 }
 
-// The contacts at positions [k0, k0 + K) of every world, each to its row.
-// Point slots past a contact's point count keep their previous bytes, as in
-// the reference (b3_contact_from_mani writes only the manifold's points).
-B3X_HD void o_contact_write(const Args& a, int tile, float* slot, OutShared& sh, int k0, int K, int t) {
+// Contacts [k0, k0 + K) of every world.  Point slots past a contact's point
+// count keep their previous bytes, as in the reference (b3_contact_from_mani
+// writes only the manifold's points).
+B3X_HD void o_contact_write(const Args& a, int tile, OutShared& sh, int k0, int K, int t) {
     const int w = t >> 5, i = t & 31;
     for (int l = w; l < kLanes; l += kCtaWarps) {
-        const int n = (sh.np[l] < k0 + K ? sh.np[l] : k0 + K) - k0;
+        const int n = (sh.n[l] < k0 + K ? sh.n[l] : k0 + K) - k0;
         if (n <= 0) continue;
-        float* dst = world_words_w(a, tile * kLanes + l) + a.L.contact_off / 4;
+        float* dst = world_words_w(a, tile * kLanes + l) + (a.L.contact_off + (size_t)B3X_CONTACT_BYTES * k0) / 4;
         for (int kk = 0; kk < n; kk++) {    // row by row: each row's point count is read once
-            const int k = pos_contact(a, slot, sh, k0 + kk, l);
-            if (k < 0) continue;
             const float* row = out_row(sh, l, kk, K, NCW);
             const int hi = WP + clampi(b3x_f2i(row[WCNT]), 0, B3_MAX_MANIFOLD) * NQW;
             for (int c = i; c < NCW; c += 32)
-                if (c < hi || c >= WCA) store_world(dst + (size_t)k * NCW + c, row[c]);
+                if (c < hi || c >= WCA) store_world(dst + kk * NCW + c, row[c]);
         }
     }
 }
@@ -1398,11 +1244,10 @@ B3X_HD void o_joint_write(const Args& a, int tile, float* slot, OutShared& sh, i
 // its impulses.  The words steps merely output (prepared solver terms) keep
 // the bytes of the last full write-back.
 B3X_HD void o_contact_state(const Args& a, int tile, float* slot, OutShared& sh, int t) {
-    for (int j = t; j < sh.maxnp * kLanes; j += kCta) {
-        const int p = j >> 5, l = j & 31;
-        const int k = pos_contact(a, slot, sh, p, l);
-        if (k < 0) continue;
-        const float* co = item(slot + a.SP.cont, p, kCI) + l;
+    for (int j = t; j < sh.maxn * kLanes; j += kCta) {
+        const int k = j >> 5, l = j & 31;
+        if (k >= sh.n[l]) continue;
+        const float* co = item(slot + a.SP.cont, k, kCI) + l;
         const int cnt = clampi(ldi(co, WCNT), 0, B3_MAX_MANIFOLD);
         const size_t base = a.L.contact_off / 4 + (size_t)k * NCW;
         for (int f = 0; f < NOF; f++) {
@@ -1515,10 +1360,8 @@ B3X_HD void out_tile(X& x, const Args& a, int bt, OutShared& sh) {
                 // (the workspace and the columns are distinct memory)
                 constexpr int kRun = (kCW + kCtaWarps - 1) / kCtaWarps;
                 const int l = t & 31, w0 = t >> 5;
-                for (int p = 0; p < sh.np[l]; p++) {
-                    const int k = pos_contact(a, slot, sh, p, l);
-                    if (k < 0) continue;
-                    const float* co = item(slot + a.SP.cont, p, kCI) + l;
+                for (int k = 0; k < sh.n[l]; k++) {
+                    const float* co = item(slot + a.SP.cont, k, kCI) + l;
                     const int hi = WP + clampi(ldi(co, WCNT), 0, B3_MAX_MANIFOLD) * NQW;
                     float* dst = res_word(a, tile, cw + (size_t)k * NCW, l);
                     float v[kRun];
@@ -1542,16 +1385,14 @@ B3X_HD void out_tile(X& x, const Args& a, int bt, OutShared& sh) {
             });
         }
     } else {
-        // contacts in position order (with a schedule a position's row goes
-        // to its contact's index)
-        const int K = out_items(sh.maxnp, NCW);
-        for (int k0 = 0; k0 < sh.maxnp; k0 += K) {
-            const int Kr = sh.maxnp - k0 < K ? sh.maxnp - k0 : K;
+        const int K = out_items(sh.maxn, NCW);
+        for (int k0 = 0; k0 < sh.maxn; k0 += K) {
+            const int Kr = sh.maxn - k0 < K ? sh.maxn - k0 : K;
             // whole items: their separation words land on row words the
             // fill below overwrites
             x.each([&](int t) { o_stage(item(slot + a.SP.cont, k0, kCI), sh, Kr, kCI, NCW, t); });
             x.each([&](int t) { o_contacts(a, slot, sh, k0, Kr, t); });
-            x.each([&](int t) { o_contact_write(a, tile, slot, sh, k0, Kr, t); });
+            x.each([&](int t) { o_contact_write(a, tile, sh, k0, Kr, t); });
         }
     }
     if (!state_only) {

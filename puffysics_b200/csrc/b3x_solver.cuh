@@ -747,168 +747,4 @@ B3X_HD bool solve_world(const Args& a, float* slot, int lane, float* __restrict_
     return true;
 }
 
-#if defined(__CUDACC__)
-// ---- the scheduled solve: four warps per tile -------------------------------------
-// Layouts with a contact schedule (sched_layout) store contact k of a world
-// at position p = kSchedWays * round + way.  Warp w solves position
-// kSchedWays * r + w of every world in round r and the block meets after each
-// round, so the contacts of a round, which share no dynamic body, run at once
-// and every body still takes its contact updates in index order.  The items
-// are read from the workspace in place (each warp reads one coalesced line
-// per word; the next rounds' items are prefetched into L2 with bulk
-// prefetches), so the four warps need no shared-memory stages.  Joints run on
-// warp 0 through its pipeline as in solve_world; per-body integration is
-// spread over the warps by body.
-__device__ __forceinline__ void prefetch_l2(const float* p, uint32_t bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
-}
-
-// Rounds of the contact schedule prefetched ahead of the one being solved.
-constexpr int kSchedAhead = 2;
-
-// All 128 threads of the block; lane = world, warp = way.  Returns false when
-// warp 0's joint pipeline failed (the same verdict on every thread).  Follows
-// 09_step.inl:158-181 like solve_world; `interleave` is the
-// B3_INTERLEAVE_CONTACTS mode.
-__device__ bool solve_world_sched(const Args& a, float* slot, int lane, int warp, float* __restrict__ bc,
-        float* __restrict__ bp, const float* __restrict__ bk, Pipe& P, bool interleave) {
-    const float* rec = slot + a.SP.rec + lane;
-    const int nb = ldi(rec, RNB);
-    const int nj = ldi(rec, RNJ);
-    const float* kc = slot + a.SP.konst + lane;
-    float* cc = slot + a.SP.cont + lane;
-    float* jc = slot + a.SP.joint + lane;
-    const float* oc = slot + a.SP.occ + lane;
-
-    const int subs = a.substeps;
-    const float dt = a.dt;
-    const float h = dt / (float)subs;
-    const float inv_dt = 1.0f / dt;
-    const float inv_h = (float)subs * inv_dt;
-    const B3Soft cs = lds(rec, RCS), ss = lds(rec, RSS);
-    const float contact_speed = COL(rec, RSPEED);
-    const float max_lin = COL(rec, RMAXLIN);
-    const float max_ang = B3_MAX_ROTATION * inv_dt;
-    const float max_lin2 = max_lin * max_lin, max_ang2 = max_ang * max_ang;
-    const float restitution_threshold = COL(rec, RRT);
-    // every warp reads the same 32 records: the same tile-wide bounds
-    const int R = warp_max(ldi(rec, RROUNDS));
-    const int wj = warp_max(nj);
-    constexpr uint32_t kItemBytes = (uint32_t)(kCI * kLanes * sizeof(float));
-    const float* cbase = cc - lane;
-
-    // fn(item) on this warp's position of every round that holds a contact
-    // of this lane's world; the block meets after each round.
-    auto rounds = [&](auto&& fn) {
-        if (lane == 0)
-            for (int r = 0; r < kSchedAhead && r < R; r++)
-                prefetch_l2(item(cbase, r * kSchedWays + warp, kCI), kItemBytes);
-        uint32_t occw = 0;
-        for (int r = 0; r < R; r++) {
-            if ((r & 7) == 0) occw = b3x_f2u(oc[(size_t)(r >> 3) * kLanes]);
-            const int pos = r * kSchedWays + warp;
-            if (lane == 0 && r + kSchedAhead < R)
-                prefetch_l2(item(cbase, pos + kSchedAhead * kSchedWays, kCI), kItemBytes);
-            if (warp < (int)((occw >> (4 * (r & 7))) & 15u)) fn(item(cc, pos, kCI));
-            __syncthreads();
-        }
-    };
-    // joint passes: warp 0 streams the joints, the other warps wait
-    auto joints = [&](auto&& fn) -> bool {
-        if (wj == 0) return true;
-        bool ok = true;
-        if (warp == 0) ok = stream_items(P, jc, NJF, kJointStream, wj, fn);
-        return __syncthreads_and(ok) != 0;
-    };
-
-    // -- warm start contacts, then joints (09_step.inl:160-163)
-    bool any_rest = false;
-    rounds([&](float* it) {
-        warm_contact(bc, bk, it);
-        any_rest |= COL(it, WREST) != 0.0f;
-    });
-    any_rest = __syncthreads_or(any_rest) != 0;
-    if (!joints([&](int q, const float* src) {
-            if (q < nj && ldi(src, JOK)) warm_joint(bc, bp, bk, src);
-        }))
-        return false;
-
-    // one contact sweep; the item is both the source and the destination of
-    // the solve (solve_contact reads each word before it writes it)
-    auto contact_pass = [&](auto pass) {
-        constexpr int kPass = decltype(pass)::value;
-        rounds([&](float* it) { solve_contact<kPass>(bc, bp, bk, it, it, inv_h, contact_speed, cs, ss); });
-    };
-    using Fresh = std::integral_constant<int, kBiasFresh>;
-    using Cached = std::integral_constant<int, kBiasCached>;
-    using Relax = std::integral_constant<int, kRelax>;
-    using RelaxCached = std::integral_constant<int, kRelaxCached>;
-    auto joint_pass = [&](int use_bias) {
-        return joints([&](int q, const float* src) {
-            if (q < nj && ldi(src, JOK)) solve_joint(bc, bp, bk, src, item(jc, q, NJF), h, inv_h, use_bias);
-        });
-    };
-    for (int s = 0; s < subs; s++) {
-        // integrate velocities (09_step.inl:5-18, 41-53), bodies over the warps
-        for (int k = warp; k < nb; k += kSchedWays) {
-            if (ldi(bk, BK(k, BTYPE)) != B3_DYNAMIC) continue;
-            const float* kk = item(kc, k, NKF);
-            st3(bc, BI(k, BV), b3_madd(ld3(kk, KDV), COL(kk, KLD), ld3(bc, BI(k, BV))));
-            st3(bc, BI(k, BW), b3_madd(ld3(kk, KDW), COL(kk, KAD), ld3(bc, BI(k, BW))));
-        }
-        __syncthreads();
-        // bias phase (09_step.inl:170-172; interleaved: 07_packed.inl:61-65)
-        if (!interleave) {
-            if (s == 0) contact_pass(Fresh{});
-            else contact_pass(Cached{});
-            for (int it = 0; it < a.joint_iters; it++)
-                if (!joint_pass(1)) return false;
-        } else {
-            for (int it = 0; it < a.joint_iters; it++) {
-                if (it == 0 && s == 0) contact_pass(Fresh{});
-                else contact_pass(Cached{});
-                if (!joint_pass(1)) return false;
-            }
-        }
-        // integrate positions (09_step.inl:55-107), bodies over the warps
-        for (int k = warp; k < nb; k += kSchedWays) {
-            if (ldi(bk, BK(k, BTYPE)) == B3_STATIC) continue;
-            uint32_t flags = b3x_f2u(COL(bk, BK(k, BFLAGS)));
-            B3Vec3 v = ld3(bc, BI(k, BV)), av = ld3(bc, BI(k, BW));
-            if (flags & B3_LOCK_LIN_X) v.x = 0.0f;
-            if (flags & B3_LOCK_LIN_Y) v.y = 0.0f;
-            if (flags & B3_LOCK_LIN_Z) v.z = 0.0f;
-            if (flags & B3_LOCK_ANG_X) av.x = 0.0f;
-            if (flags & B3_LOCK_ANG_Y) av.y = 0.0f;
-            if (flags & B3_LOCK_ANG_Z) av.z = 0.0f;
-            float v2 = b3_len2(v);
-            if (v2 > max_lin2 && v2 > 0.0f) v = b3_mul(v, max_lin / sqrtf(v2));
-            float w2 = b3_len2(av);
-            if (w2 > max_ang2 && w2 > 0.0f) av = b3_mul(av, max_ang / sqrtf(w2));
-            st3(bc, BI(k, BV), v);
-            st3(bc, BI(k, BW), av);
-            st3(bp, BP(k, BDP), b3_madd(ld3(bp, BP(k, BDP)), h, v));
-            stq(bp, BP(k, BDQ), q_integrate(ldq(bp, BP(k, BDQ)), b3_mul(av, h)));
-        }
-        __syncthreads();
-        // relax phase (09_step.inl:173-177), the same way
-        if (!interleave) {
-            contact_pass(Relax{});
-            for (int it = 0; it < a.relax_iters; it++)
-                if (!joint_pass(0)) return false;
-        } else {
-            for (int it = 0; it < a.relax_iters; it++) {
-                if (it == 0) contact_pass(Relax{});
-                else contact_pass(RelaxCached{});
-                if (!joint_pass(0)) return false;
-            }
-        }
-        // restitution (08_contacts.inl:439-480)
-        if (any_rest && !(a.flags & kStepSkipRestitution))
-            rounds([&](float* it) { restitute_contact(bc, bk, it, it, restitution_threshold); });
-    }
-    return true;
-}
-#endif
-
 }  // namespace b3x

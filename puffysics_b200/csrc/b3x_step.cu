@@ -120,55 +120,10 @@ __device__ bool solve_tile(const Args& a, unsigned char* smem_raw) {
     return ok;
 }
 
-// The scheduled solve (layouts with a contact schedule): all four warps,
-// the body columns placed as in solve_tile.  Returns the same verdict on
-// every thread.
-template <int kBody>
-__device__ bool solve_tile_sched(const Args& a, unsigned char* smem_raw) {
-    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
-    float* slot = slot_of(a, blockIdx.x);
-    Pipe P;
-    P.buf = reinterpret_cast<float*>(smem_raw);
-    P.bar = reinterpret_cast<uint64_t*>(smem_raw + kStageBytes);
-    if (warp == 0) pipe_init(P);
-    float* gv = slot + a.SP.body;
-    float* gp = slot + a.SP.bodyp;
-    const float* gk = slot + a.SP.bodyk;
-    float* sv = reinterpret_cast<float*>(smem_raw + kStageBytes + kBarBytes);
-    float* sp = sv + (size_t)a.L.B * NBF * kLanes;
-    float* sk = sp + (size_t)a.L.B * NBP * kLanes;
-    const int nb = warp_max(ldi(slot + a.SP.rec + lane, RNB));
-    if (kBody >= kBodyVel)
-        for (int idx = t; idx < nb * NBF * kLanes; idx += kCta) sv[idx] = gv[idx];
-    if (kBody >= kBodyState)
-        for (int idx = t; idx < nb * NBP * kLanes; idx += kCta) sp[idx] = gp[idx];
-    if (kBody == kBodyAll)
-        for (int idx = t; idx < nb * NBC * kLanes; idx += kCta) sk[idx] = gk[idx];
-    __syncthreads();
-    float* bc = (kBody >= kBodyVel ? sv : gv) + lane;
-    float* bp = (kBody >= kBodyState ? sp : gp) + lane;
-    const float* bk = (kBody == kBodyAll ? sk : gk) + lane;
-    const bool ok = solve_world_sched(a, slot, lane, warp, bc, bp, bk, P, (a.flags & kStepInterleaveContacts) != 0);
-    __syncthreads();
-    if (ok && kBody >= kBodyVel)
-        for (int idx = t; idx < nb * NBF * kLanes; idx += kCta) gv[idx] = sv[idx];
-    if (ok && kBody >= kBodyState)
-        for (int idx = t; idx < nb * NBP * kLanes; idx += kCta) gp[idx] = sp[idx];
-    if (warp == 0) {
-        __syncwarp();
-        if (lane == 0) {
-            for (int s = 0; s < kStages; s++)
-                asm volatile("mbarrier.inval.shared::cta.b64 [%0];" ::"r"(smem_addr(&P.bar[s])) : "memory");
-            if (!ok) atomicExch(&g_fault, 1);
-        }
-    }
-    return ok;
-}
-
-// One block per tile: collide (all warps), solve (warp 0; all warps with a
-// contact schedule, kSched), write-back (all warps).  kRes: the worlds are
-// the resident world columns (a.res) instead of the caller's AoS array.
-template <int kBody, bool kInterleave = false, bool kRes = false, bool kSched = false>
+// One block per tile: collide (all warps), solve (warp 0), write-back (all
+// warps).  kRes: the worlds are the resident world columns (a.res) instead
+// of the caller's AoS array.
+template <int kBody, bool kInterleave = false, bool kRes = false>
 __global__ void __launch_bounds__(kCta, 4) step_kernel(Args a) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     __shared__ int solved;
@@ -179,10 +134,7 @@ __global__ void __launch_bounds__(kCta, 4) step_kernel(Args a) {
     // the generic proxy: each thread orders its accesses before the barrier
     asm volatile("fence.proxy.async;" ::: "memory");
     __syncthreads();
-    if constexpr (kSched) {
-        const bool ok = solve_tile_sched<kBody>(a, smem_raw);
-        if (threadIdx.x == 0) solved = ok;
-    } else if (threadIdx.x < kLanes) {
+    if (threadIdx.x < kLanes) {
         const bool ok = solve_tile<kBody, kInterleave>(a, smem_raw);
         if (threadIdx.x == 0) solved = ok;
     }
@@ -535,8 +487,7 @@ static cudaError_t make_plan(int dev, unsigned long long sig, const Layout& L, P
             break;
         }
     p.smem_bytes = upto[p.body];
-    const size_t collide_bytes = sizeof(CollideShared) + sched_state_bytes(L);
-    if (p.smem_bytes < collide_bytes) p.smem_bytes = collide_bytes;
+    if (p.smem_bytes < sizeof(CollideShared)) p.smem_bytes = sizeof(CollideShared);
     if (p.smem_bytes < sizeof(OutShared)) p.smem_bytes = sizeof(OutShared);
     if (p.smem_bytes > (size_t)cap) return cudaErrorInvalidValue;
     for (auto fn : {step_kernel<kBodyNone>, step_kernel<kBodyVel>, step_kernel<kBodyState>, step_kernel<kBodyAll>,
@@ -545,11 +496,7 @@ static cudaError_t make_plan(int dev, unsigned long long sig, const Layout& L, P
                     step_kernel<kBodyNone, false, true>, step_kernel<kBodyVel, false, true>,
                     step_kernel<kBodyState, false, true>, step_kernel<kBodyAll, false, true>,
                     step_kernel<kBodyNone, true, true>, step_kernel<kBodyVel, true, true>,
-                    step_kernel<kBodyState, true, true>, step_kernel<kBodyAll, true, true>,
-                    step_kernel<kBodyNone, false, false, true>, step_kernel<kBodyVel, false, false, true>,
-                    step_kernel<kBodyState, false, false, true>, step_kernel<kBodyAll, false, false, true>,
-                    step_kernel<kBodyNone, false, true, true>, step_kernel<kBodyVel, false, true, true>,
-                    step_kernel<kBodyState, false, true, true>, step_kernel<kBodyAll, false, true, true>}) {
+                    step_kernel<kBodyState, true, true>, step_kernel<kBodyAll, true, true>}) {
         e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, cap);
         if (e != cudaSuccess) return e;
     }
@@ -616,12 +563,12 @@ static Args step_args(const Worlds& w, float dt, int substeps, const unsigned ch
     return a;
 }
 
-template <bool kI, bool kR, bool kS = false>
+template <bool kI, bool kR>
 static void launch_tiles(const Plan& p, int nt, cudaStream_t stream, const Args& a) {
-    if (p.body == kBodyAll) step_kernel<kBodyAll, kI, kR, kS><<<nt, kCta, p.smem_bytes, stream>>>(a);
-    else if (p.body == kBodyState) step_kernel<kBodyState, kI, kR, kS><<<nt, kCta, p.smem_bytes, stream>>>(a);
-    else if (p.body == kBodyVel) step_kernel<kBodyVel, kI, kR, kS><<<nt, kCta, p.smem_bytes, stream>>>(a);
-    else step_kernel<kBodyNone, kI, kR, kS><<<nt, kCta, p.smem_bytes, stream>>>(a);
+    if (p.body == kBodyAll) step_kernel<kBodyAll, kI, kR><<<nt, kCta, p.smem_bytes, stream>>>(a);
+    else if (p.body == kBodyState) step_kernel<kBodyState, kI, kR><<<nt, kCta, p.smem_bytes, stream>>>(a);
+    else if (p.body == kBodyVel) step_kernel<kBodyVel, kI, kR><<<nt, kCta, p.smem_bytes, stream>>>(a);
+    else step_kernel<kBodyNone, kI, kR><<<nt, kCta, p.smem_bytes, stream>>>(a);
 }
 
 // The step over chunks of `chunk` tiles, one step_kernel launch per chunk.
@@ -634,10 +581,7 @@ static cudaError_t launch_step(const Worlds& w, float dt, int substeps, const un
     for (int t0 = 0; t0 < ntiles; t0 += chunk) {
         const int nt = ntiles - t0 < chunk ? ntiles - t0 : chunk;
         a.tile0 = t0;
-        // (the scheduled solve takes the interleaved mode from a.flags)
-        if (p.SP.sched) res ? launch_tiles<false, true, true>(p, nt, stream, a)
-                            : launch_tiles<false, false, true>(p, nt, stream, a);
-        else if (il) res ? launch_tiles<true, true>(p, nt, stream, a) : launch_tiles<true, false>(p, nt, stream, a);
+        if (il) res ? launch_tiles<true, true>(p, nt, stream, a) : launch_tiles<true, false>(p, nt, stream, a);
         else res ? launch_tiles<false, true>(p, nt, stream, a) : launch_tiles<false, false>(p, nt, stream, a);
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return e;
