@@ -375,31 +375,33 @@ def reference_gpu_env_run(steps, warmup):
                       "environment in place, nvcc -O3 sm_100a", "l2": "flushed between timed steps"}
 
 
-def thread_path_run(cfg, n, steps, warmup, stream, budget_s=60.0, window=0):
+def thread_path_run(cfg, n, steps, warmup, stream, budget_s=60.0, window=0, adapter=False):
     """Time this library's per-thread device b3_step (include/puffysics.cuh,
-    one thread per world, libb3thread_<cfg>.so) over the stretch of the scene
-    the reference GPU kernel is timed on: freshly built worlds, the scene's
-    actions from step 1, the same warm-up, timed steps (or window) and L2
-    rule; CUDA events on `stream` around each step."""
+    one thread per world, libb3thread_<cfg>.so; with `adapter`, the same
+    header built with nvcc's default contraction as an adapter builds it,
+    libb3thread_<cfg>_adapter.so) over the stretch of the scene the reference
+    GPU kernel is timed on: freshly built worlds, the scene's actions from
+    step 1 (one launch, like the reference arm's action kernel), the same
+    warm-up, timed steps (or window) and L2 rule; CUDA events on `stream`
+    around each step."""
     import torch
     from puffysics_b200 import engine, synth
+    name = cfg.name + ("_adapter" if adapter else "")
     try:
-        engine.thread_lib(cfg.name)
+        engine.thread_lib(name)
     except RuntimeError:
         return None
     dev = torch.device("cuda", torch.cuda.current_device())
     w = torch.from_numpy(synth.SceneLib(cfg).build(n, SEED)).to(dev)
     seeded = w.clone() if window else None
-    kind, aidx, nv = cfg.action
-    vals = torch.zeros((n, max(nv, 1)), dtype=torch.float32, device=dev)
+    nv = cfg.action[2]
     step_no = [0]
 
     def one():
         step_no[0] += 1
         if nv:
-            assert synth.actions_gpu(vals, n, cfg.scene, SEED, 0, step_no[0], stream) == nv
-            assert engine.batch_apply_gpu(w, kind, aidx, vals, None, stream, cfg.caps) == 0
-        assert engine.thread_step_gpu(cfg.name, w, cfg.dt, cfg.substeps, stream=stream) == 0
+            assert engine.thread_scene_apply_gpu(name, w, cfg.scene, SEED, 0, step_no[0], stream) == 0
+        assert engine.thread_step_gpu(name, w, cfg.dt, cfg.substeps, stream=stream) == 0
 
     def restart():
         w.copy_(seeded)
@@ -417,7 +419,9 @@ def thread_path_run(cfg, n, steps, warmup, stream, budget_s=60.0, window=0):
     return {"value": n * k / (ms / 1e3), "unit": UNIT, "ms_per_step": ms / k, "worlds": n, "steps": k,
             "l2": "flushed between timed steps" if flush is not None else "world array larger than twice L2",
             "timed_steps": ("steps 1-%d from the seeded state" % window) if window else "after the warm-up",
-            "kernel": "per-thread device b3_step of include/puffysics.cuh (one thread per world)"}
+            "kernel": "per-thread device b3_step of include/puffysics.cuh (one thread per world), "
+                      + ("built with nvcc's default contraction, as an adapter compiles the header"
+                         if adapter else "the parity build (-fmad=false: bit-exact with the CPU reference)")}
 
 
 class ClockSampler:
@@ -811,6 +815,8 @@ def main():
         if world == 1 and not args.no_per_thread_path:
             line["per_thread_path"] = thread_path_run(res["cfg"], per_gpu, res["K"], args.warmup, stream,
                                                       window=res["window"])
+            line["per_thread_path_adapter_build"] = thread_path_run(res["cfg"], per_gpu, res["K"], args.warmup,
+                                                                    stream, window=res["window"], adapter=True)
             if res["cfg"].name == "hover":
                 line["fused_env"] = fused_env_run(res["K"], args.warmup, stream)
         if world == 1 and not args.no_cpu_baseline:
@@ -830,6 +836,9 @@ def main():
                 if not args.no_per_thread_path:
                     sub["per_thread_path"] = thread_path_run(r["cfg"], r["per_gpu"], r["K"], args.warmup, stream,
                                                              window=r["window"])
+                    sub["per_thread_path_adapter_build"] = thread_path_run(r["cfg"], r["per_gpu"], r["K"],
+                                                                           args.warmup, stream, window=r["window"],
+                                                                           adapter=True)
                 if not args.no_cpu_baseline:
                     sub["cpu_baseline"] = cpu_reference_run(r["cfg"], None, 2, budget_s=args.cpu_seconds,
                                                             window=r["window"])

@@ -36,7 +36,8 @@ HOVER_HEADERS = THREAD_HEADERS + [os.path.join(ROOT, "include", "b3x_staged.cuh"
 THREAD_HEADERS = THREAD_HEADERS + [os.path.join(PKG, "scenes", "b3_test_forces.h")]
 # what the per-thread libraries include
 THREAD_DEPS = THREAD_HEADERS + [os.path.join(ROOT, "include", "puffysics_b200.h"),
-                                os.path.join(PKG, "csrc", "b3x_math.cuh"), os.path.join(PKG, "csrc", "b3x_narrow.cuh")]
+                                os.path.join(PKG, "csrc", "b3x_math.cuh"), os.path.join(PKG, "csrc", "b3x_narrow.cuh"),
+                                os.path.join(PKG, "scenes", "b3_scenes.h")]
 # capacity configurations the host scene builders are compiled for:
 # name -> (bodies, shapes, contacts, joints)
 SCENE_CONFIGS = {"hover": (2, 2, 4, 1), "stack": (9, 9, 32, 1), "chain": (12, 12, 32, 10),
@@ -52,6 +53,10 @@ THREAD_CONFIGS = {"hover": (2, 2, 4, 1, 8), "stack": (9, 9, 32, 1, 8), "chain": 
                   "bounce": (9, 9, 32, 1, 8), "capsule": (17, 17, 64, 1, 8), "stackil": (9, 9, 32, 1, 8),
                   "chainil": (12, 12, 32, 10, 8), "chainart": (12, 12, 32, 10, 8),
                   "bouncenr": (9, 9, 32, 1, 8), "bounceilnr": (9, 9, 32, 1, 8), "hoveruf": (2, 2, 4, 1, 8)}
+# the same header step built the way an adapter compiles it (nvcc's default
+# floating-point contraction instead of the parity flags), for timing beside
+# the reference kernel, which is built that way too: libb3thread_<name>_adapter.so
+ADAPTER_THREAD_CONFIGS = ["hover", "stack", "chain", "pile"]
 # the reference's mode macros of the per-thread configurations
 THREAD_MODES = {"stackil": ["-DB3_INTERLEAVE_CONTACTS"], "chainil": ["-DB3_INTERLEAVE_CONTACTS"],
                 "bouncenr": ["-DB3_SKIP_RESTITUTION"],
@@ -78,13 +83,20 @@ def thread_lib(name):
 
 
 def thread_cmd(name):
-    b, s, c, j, it = THREAD_CONFIGS[name]
+    adapter = name.endswith("_adapter")
+    cfg = name[:-len("_adapter")] if adapter else name
+    b, s, c, j, it = THREAD_CONFIGS[cfg]
     caps = ["-DB3_MAX_BODIES=%d" % b, "-DB3_MAX_SHAPES=%d" % s, "-DB3_MAX_CONTACTS=%d" % c,
-            "-DB3_MAX_JOINTS=%d" % j, "-DB3_JOINT_ITERS=%d" % it] + THREAD_MODES.get(name, [])
-    return ([NVCC] + ARCH + ["-lineinfo", "-O3", "-std=c++17"] + PARITY
+            "-DB3_MAX_JOINTS=%d" % j, "-DB3_JOINT_ITERS=%d" % it] + THREAD_MODES.get(cfg, [])
+    return ([NVCC] + ARCH + ["-lineinfo", "-O3", "-std=c++17"] + ([] if adapter else PARITY)
             + ["-Xcompiler", "-fPIC,-fvisibility=hidden", "-shared", "-cudart", "static",
-               "-I" + os.path.join(ROOT, "include"), "-I" + os.path.join(PKG, "csrc")]
+               "-I" + os.path.join(ROOT, "include"), "-I" + os.path.join(PKG, "csrc"),
+               "-I" + os.path.join(PKG, "scenes")]
             + caps + [THREAD_SRC, "-o", thread_lib(name)])
+
+
+def thread_lib_names():
+    return list(THREAD_CONFIGS) + [n + "_adapter" for n in ADAPTER_THREAD_CONFIGS]
 
 
 def hover_cmd():
@@ -97,7 +109,7 @@ def build_thread_libs(force=False):
     """The per-thread step launchers, one per capacity configuration, and the
     hover environment library, compiled concurrently."""
     deps = [THREAD_SRC, __file__] + THREAD_DEPS
-    todo = [n for n in THREAD_CONFIGS if force or _newer(thread_lib(n), deps)]
+    todo = [n for n in thread_lib_names() if force or _newer(thread_lib(n), deps)]
     cmds = {n: thread_cmd(n) for n in todo}
     if force or _newer(HOVER_LIB, [HOVER_SRC, __file__] + THREAD_DEPS + HOVER_HEADERS):
         cmds["hover environment"] = hover_cmd()
@@ -127,7 +139,7 @@ def up_to_date():
     deps = SOURCES + HEADERS + [__file__]
     thread_deps = [THREAD_SRC, __file__] + THREAD_DEPS
     return (not _newer(LIB, deps) and not any(_newer(scenes_lib(n), [SCENES_SRC] + HEADERS) for n in SCENE_CONFIGS)
-            and not any(_newer(thread_lib(n), thread_deps) for n in THREAD_CONFIGS)
+            and not any(_newer(thread_lib(n), thread_deps) for n in thread_lib_names())
             and not _newer(HOVER_LIB, [HOVER_SRC, __file__] + THREAD_DEPS + HOVER_HEADERS))
 
 

@@ -13,6 +13,7 @@
 #include <cuda_runtime.h>
 
 #include "puffysics.cuh"
+#include "b3_scenes.h"
 
 #define B3T_API extern "C" __attribute__((visibility("default")))
 
@@ -23,6 +24,21 @@ constexpr int kThreads = 32;   // one warp per block, as the reference launches
 __global__ void B3X_THREAD_BOUNDS thread_batch_kernel(B3Batch batch, float dt, int substeps, const unsigned char* active) {
     size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i < (size_t)batch.count && (!active || active[i])) b3_step(b3_batch_world(batch, (int)i), dt, substeps);
+}
+
+// The benchmark scene's actions of one step, generated and applied per
+// world with the header's b3_apply_* (one launch, as the reference arm's
+// action kernel does).
+__global__ void thread_scene_apply_kernel(B3Batch batch, int scene, unsigned long long seed, unsigned long long first,
+        unsigned long long step) {
+    size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (size_t)batch.count) return;
+    int kind, index, nv;
+    b3s_action_layout(scene, &kind, &index, &nv);
+    if (nv <= 0) return;
+    float v[16];
+    b3s_actions(scene, seed, first + (unsigned long long)i, step, v);
+    b3s_apply(b3_batch_world(batch, (int)i), kind, index, nv, v);
 }
 
 }  // namespace
@@ -55,6 +71,19 @@ B3T_API int b3x_thread_shim_step_gpu(B3Batch batch, float dt, int substeps, cons
     return (int)b3_batch_step_gpu(batch, dt, substeps, active, (cudaStream_t)stream);
 }
 #endif
+
+// Benchmark input: the scene's actions of `step` applied to every world of
+// the batch in one launch (no launch for scenes without actions).
+B3T_API int b3x_thread_scene_apply_gpu(B3Batch batch, int scene, unsigned long long seed, unsigned long long first,
+        unsigned long long step, void* stream) {
+    if (!b3_batch_valid(batch)) return (int)cudaErrorInvalidValue;
+    int kind, index, nv;
+    b3s_action_layout(scene, &kind, &index, &nv);
+    if (batch.count == 0 || nv <= 0) return (int)cudaSuccess;
+    unsigned blocks = ((unsigned)batch.count + kThreads - 1) / kThreads;
+    thread_scene_apply_kernel<<<blocks, kThreads, 0, (cudaStream_t)stream>>>(batch, scene, seed, first, step);
+    return (int)cudaGetLastError();
+}
 
 // b3_step_kernel (reference 09_step.inl:325-333) over contiguous worlds.
 B3T_API int b3x_thread_step_worlds_gpu(B3World* worlds, int n, float dt, int substeps, void* stream) {

@@ -249,6 +249,9 @@ def thread_lib(name):
         L.b3x_thread_step_worlds_gpu.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_int,
                                                  ctypes.c_void_p]
         L.b3x_thread_step_worlds_gpu.restype = ctypes.c_int
+        L.b3x_thread_scene_apply_gpu.argtypes = [B3Batch, ctypes.c_int, ctypes.c_ulonglong, ctypes.c_ulonglong,
+                                                 ctypes.c_ulonglong, ctypes.c_void_p]
+        L.b3x_thread_scene_apply_gpu.restype = ctypes.c_int
         if hasattr(L, "b3x_thread_shim_step_gpu"):
             L.b3x_thread_shim_step_gpu.argtypes = [B3Batch, ctypes.c_float, ctypes.c_int, ctypes.c_void_p,
                                                    ctypes.c_void_p]
@@ -262,6 +265,14 @@ def thread_step_gpu(name, worlds, dt, substeps, active=None, stream=None, stride
     a batch, b3_batch_step_gpu semantics).  Returns a cudaError_t code."""
     b = make_batch(worlds, stride, offset, count)
     return thread_lib(name).b3x_thread_step_gpu(b, dt, substeps, _ptr(active), _stream(stream))
+
+
+def thread_scene_apply_gpu(name, worlds, scene, seed, first, step, stream=None):
+    """The benchmark scene's actions of `step` applied to every world, one
+    launch with the header's b3_apply_* (benchmark input of the per-thread
+    path).  Returns a cudaError_t code."""
+    b = make_batch(worlds, None, 0, None)
+    return thread_lib(name).b3x_thread_scene_apply_gpu(b, scene, seed, first, step, _stream(stream))
 
 
 def thread_step_worlds_gpu(name, worlds, dt, substeps, stream=None):
