@@ -999,9 +999,11 @@ B3X_API int b3x_scene_reset_gpu(unsigned char* out, int n, unsigned long long se
 /* Nonzero if a step on the current device was abandoned because one of its
  * bounded waits for a bulk copy into shared memory gave up (not expected).
  * The 32 worlds of the tile whose wait gave up are then left as they were
- * before the call (nothing of that tile is written back); the other tiles
- * are stepped.  clear != 0 resets it.  Synchronises the device; -1 on
- * error. */
+ * before the call (nothing of that tile is written back), except on resident
+ * world columns (b3x_engine_step without B3X_STEP_STATE_ONLY), whose contact
+ * rows may already hold the step's new contacts with their previous
+ * impulses; the other tiles are stepped.  clear != 0 resets it.  Synchronises
+ * the device; -1 on error. */
 B3X_API int b3x_fault_flags(int clear);
 
 /* Capacity configuration helpers (host). */

@@ -1281,6 +1281,95 @@ B3X_HD void o_joint_state(const Args& a, int tile, float* slot, OutShared& sh, i
     }
 }
 
+// ---- contact rows of the resident columns ------------------------------------------
+// A contact's words [0, kCW) are the workspace item's (the same
+// [item][word][lane] order: one line per word), copied straight across (point
+// words up to the point count); the words the workspace does not keep are
+// derived in place.  All but the solver's impulses are final once the
+// collide phase has built the contact, so warps 1-3 write them while warp 0
+// solves the tile (o_contacts_early, 96 threads), and the write-back then
+// stores the impulses (o_contact_impulses).
+
+// The contact words the solve writes: per point its normal and accumulated
+// impulses, then twist, friction and rolling impulses (08_contacts.inl:315-413).
+B3X_HDI bool solver_word(int c) {
+    if (c >= WP && c < WCA) {
+        const int f = (c - WP) % NQW;
+        return f == QNI || f == QTOT;
+    }
+    return c == WTWI || c == WFI || c == WFI + 1 || (c >= WRI && c < WRI + 3);
+}
+
+// Run by the 96 threads of warps 1-3 (e = threadIdx.x - 32) during the
+// solve: the other contact words of every contact, then the derived words.
+// Reads only what the solve leaves unchanged (the contacts' other words, the
+// body constants, the record), writes only the columns' contact rows.
+B3X_HD void o_contacts_early(const Args& a, int tile, float* slot, int e) {
+    constexpr int kThreads = kCta - kLanes, kWarps = kThreads / kLanes;
+    constexpr int kRun = (kCW + kWarps - 1) / kWarps;
+    const size_t cw = a.L.contact_off / 4;
+    const int l = e & 31, w0 = e >> 5;
+    const int n = ldi(slot + a.SP.rec + l, RN);
+    for (int k = 0; k < n; k++) {
+        const float* co = item(slot + a.SP.cont, k, kCI) + l;
+        const int hi = WP + clampi(ldi(co, WCNT), 0, B3_MAX_MANIFOLD) * NQW;
+        float* dst = res_word(a, tile, cw + (size_t)k * NCW, l);
+        float v[kRun];
+#pragma unroll
+        for (int i = 0; i < kRun; i++) {
+            const int c = w0 + i * kWarps;
+            v[i] = c < kCW && !solver_word(c) ? COL(co, c) : 0.0f;
+        }
+#pragma unroll
+        for (int i = 0; i < kRun; i++) {
+            const int c = w0 + i * kWarps;
+            if (c < kCW && (c < hi || c >= WCA) && !solver_word(c)) store_world(dst + (size_t)c * kLanes, v[i]);
+        }
+    }
+    // the derived words, read back from the rows the threads above wrote
+#if defined(__CUDA_ARCH__)
+    asm volatile("bar.sync 1, %0;" ::"n"(kThreads) : "memory");
+#endif
+    for (int k = w0; k < n; k += kWarps)
+        o_contact_fill(a, slot, l, ColRow{res_word(a, tile, cw + (size_t)k * NCW, l)});
+}
+
+// After the solve: each contact's impulses (point words up to its count).
+B3X_HD void o_contact_impulses(const Args& a, int tile, const float* slot, OutShared& sh, int t) {
+    const size_t cw = a.L.contact_off / 4;
+    const int l = t & 31;
+    for (int k = t >> 5; k < sh.n[l]; k += kCtaWarps) {
+        const float* co = item(slot + a.SP.cont, k, kCI) + l;
+        const int cnt = clampi(ldi(co, WCNT), 0, B3_MAX_MANIFOLD);
+        float* dst = res_word(a, tile, cw + (size_t)k * NCW, l);
+        float v[2 * B3_MAX_MANIFOLD + 6];
+#pragma unroll
+        for (int p = 0; p < B3_MAX_MANIFOLD; p++) {
+            v[2 * p] = COL(co, PW(p, QNI));
+            v[2 * p + 1] = COL(co, PW(p, QTOT));
+        }
+        const int q = 2 * B3_MAX_MANIFOLD;
+        v[q] = COL(co, WTWI);
+        v[q + 1] = COL(co, WFI);
+        v[q + 2] = COL(co, WFI + 1);
+        v[q + 3] = COL(co, WRI);
+        v[q + 4] = COL(co, WRI + 1);
+        v[q + 5] = COL(co, WRI + 2);
+#pragma unroll
+        for (int p = 0; p < B3_MAX_MANIFOLD; p++) {
+            if (p >= cnt) continue;
+            store_world(dst + (size_t)PW(p, QNI) * kLanes, v[2 * p]);
+            store_world(dst + (size_t)PW(p, QTOT) * kLanes, v[2 * p + 1]);
+        }
+        store_world(dst + (size_t)WTWI * kLanes, v[q]);
+        store_world(dst + (size_t)WFI * kLanes, v[q + 1]);
+        store_world(dst + (size_t)(WFI + 1) * kLanes, v[q + 2]);
+        store_world(dst + (size_t)WRI * kLanes, v[q + 3]);
+        store_world(dst + (size_t)(WRI + 1) * kLanes, v[q + 4]);
+        store_world(dst + (size_t)(WRI + 2) * kLanes, v[q + 5]);
+    }
+}
+
 // Items per write-back round: as many as the staging area holds, balanced.
 B3X_HDI int out_items(int count, int row_floats) {
     int k = kStageFloats / (kLanes * row_floats);
@@ -1348,42 +1437,10 @@ B3X_HD void out_tile(X& x, const Args& a, int bt, OutShared& sh) {
         x.each([&](int t) { o_joint_state(a, tile, slot, sh, t); });
     }
     if constexpr (kRes) {
-        if (!state_only) {
-            // resident columns: a contact's words [0, kCW) are the workspace
-            // item's (same [item][word][lane] order: one line per word),
-            // copied straight across (point words up to the point count);
-            // then the words the workspace does not keep are derived in place
-            const size_t cw = a.L.contact_off / 4;
-            x.each([&](int t) {
-                // thread t: world lane t % 32, words t / 32 + 4i of each of
-                // its contacts; a run of words is loaded before it is stored
-                // (the workspace and the columns are distinct memory)
-                constexpr int kRun = (kCW + kCtaWarps - 1) / kCtaWarps;
-                const int l = t & 31, w0 = t >> 5;
-                for (int k = 0; k < sh.n[l]; k++) {
-                    const float* co = item(slot + a.SP.cont, k, kCI) + l;
-                    const int hi = WP + clampi(ldi(co, WCNT), 0, B3_MAX_MANIFOLD) * NQW;
-                    float* dst = res_word(a, tile, cw + (size_t)k * NCW, l);
-                    float v[kRun];
-#pragma unroll
-                    for (int i = 0; i < kRun; i++) {
-                        const int c = w0 + i * kCtaWarps;
-                        v[i] = c < kCW ? COL(co, c) : 0.0f;
-                    }
-#pragma unroll
-                    for (int i = 0; i < kRun; i++) {
-                        const int c = w0 + i * kCtaWarps;
-                        if (c < kCW && (c < hi || c >= WCA)) store_world(dst + (size_t)c * kLanes, v[i]);
-                    }
-                }
-            });
-            x.each([&](int t) {
-                for (int j = t; j < sh.maxn * kLanes; j += kCta) {
-                    const int k = j >> 5, l = j & 31;
-                    if (k < sh.n[l]) o_contact_fill(a, slot, l, ColRow{res_word(a, tile, cw + (size_t)k * NCW, l)});
-                }
-            });
-        }
+        // resident columns: every other contact word went to the columns
+        // while the tile was solved (o_contacts_early); the solver's impulses
+        // follow now
+        if (!state_only) x.each([&](int t) { o_contact_impulses(a, tile, slot, sh, t); });
     } else {
         const int K = out_items(sh.maxn, NCW);
         for (int k0 = 0; k0 < sh.maxn; k0 += K) {
