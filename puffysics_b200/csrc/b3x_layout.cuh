@@ -114,7 +114,7 @@ constexpr int kStreamWords = kContactStream > kJointStream ? kContactStream : kJ
 
 // Candidate pairs are tested in windows of kPairWindow consecutive pair
 // indices (lexicographic (i, j) order, the reference's loop order).
-constexpr int kPairWindow = 64;
+constexpr int kPairWindow = 128;
 // A manifold of the narrowphase, parked between the narrowphase and the
 // contact build of a window (region mani, one item per window candidate):
 // point count, normal, then per point p_a, p_b, separation, feature id.

@@ -27,6 +27,7 @@ namespace b3x {
 
 constexpr int kCta = 128;            // threads of a collide / write-back block
 constexpr int kCtaWarps = kCta / 32;
+static_assert(kPairWindow <= kCta && kPairWindow % 32 == 0, "a window's pairs are set up one per thread");
 constexpr int kRow = NYW + 1;        // staged struct row (odd: conflict-free columns)
 // Collide staging area: rows of caller structs gathered for a group of worlds.
 constexpr int kStageFloats = 12 * 1024;
@@ -77,10 +78,15 @@ B3X_HDI float* res_word(const Args& a, int tile, size_t w, int l) {
     return a.res + ((size_t)tile * a.resW + w) * kLanes + l;
 }
 
-// Index of the n-th set bit of a window mask (two words).
+// Index of the n-th set bit of a window mask (kPairWindow / 32 words).
 B3X_HDI int nth_bit64(const uint32_t* m, int n) {
-    int c0 = popc32(m[0]);
-    return n < c0 ? nth_bit32(m[0], n) : 32 + nth_bit32(m[1], n - c0);
+#pragma unroll
+    for (int w = 0; w < kPairWindow / 32 - 1; w++) {
+        const int c = popc32(m[w]);
+        if (n < c) return 32 * w + nth_bit32(m[w], n);
+        n -= c;
+    }
+    return 32 * (kPairWindow / 32 - 1) + nth_bit32(m[kPairWindow / 32 - 1], n);
 }
 
 // ================================ collide ==========================================
