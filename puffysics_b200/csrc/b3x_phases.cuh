@@ -1217,28 +1217,18 @@ B3X_HD void o_joints(const Args& a, float* slot, OutShared& sh, int q0, int K, i
     }
 }
 
-// Joints [q0, q0 + K) of every world; invalid joints (body index out of
-// range) are left as they were.
-template <bool kRes>
+// Joints [q0, q0 + K) of every world (the caller's AoS worlds); invalid
+// joints (body index out of range) are left as they were.
 B3X_HD void o_joint_write(const Args& a, int tile, float* slot, OutShared& sh, int q0, int K, int t) {
     const int w = t >> 5, i = t & 31;
-    if constexpr (kRes) {
-        for (int idx = t; idx < K * NVW * kLanes; idx += kCta) {
-            const int l = idx & 31, r = idx >> 5, kk = r / NVW, c = r - kk * NVW;
-            if (q0 + kk >= sh.nj[l] || !ldi(item(slot + a.SP.joint, q0 + kk, NJF) + l, JOK)) continue;
-            store_world(res_word(a, tile, a.L.joint_off / 4 + (size_t)(q0 + kk) * NVW + c, l),
-                        out_row(sh, l, kk, K, NVW)[c]);
-        }
-    } else {
-        for (int l = w; l < kLanes; l += kCtaWarps) {
-            const int n = (sh.nj[l] < q0 + K ? sh.nj[l] : q0 + K) - q0;
-            if (n <= 0) continue;
-            float* dst = world_words_w(a, tile * kLanes + l) + (a.L.joint_off + (size_t)B3X_JOINT_BYTES * q0) / 4;
-            for (int kk = 0; kk < n; kk++) {
-                if (!ldi(item(slot + a.SP.joint, q0 + kk, NJF) + l, JOK)) continue;
-                const float* row = out_row(sh, l, kk, K, NVW);
-                for (int c = i; c < NVW; c += 32) store_world(dst + kk * NVW + c, row[c]);
-            }
+    for (int l = w; l < kLanes; l += kCtaWarps) {
+        const int n = (sh.nj[l] < q0 + K ? sh.nj[l] : q0 + K) - q0;
+        if (n <= 0) continue;
+        float* dst = world_words_w(a, tile * kLanes + l) + (a.L.joint_off + (size_t)B3X_JOINT_BYTES * q0) / 4;
+        for (int kk = 0; kk < n; kk++) {
+            if (!ldi(item(slot + a.SP.joint, q0 + kk, NJF) + l, JOK)) continue;
+            const float* row = out_row(sh, l, kk, K, NVW);
+            for (int c = i; c < NVW; c += 32) store_world(dst + kk * NVW + c, row[c]);
         }
     }
 }
@@ -1287,14 +1277,16 @@ B3X_HD void o_joint_state(const Args& a, int tile, float* slot, OutShared& sh, i
     }
 }
 
-// ---- contact rows of the resident columns ------------------------------------------
+// ---- contact and joint rows of the resident columns --------------------------------
 // A contact's words [0, kCW) are the workspace item's (the same
 // [item][word][lane] order: one line per word), copied straight across (point
 // words up to the point count); the words the workspace does not keep are
 // derived in place.  All but the solver's impulses are final once the
 // collide phase has built the contact, so warps 1-3 write them while warp 0
-// solves the tile (o_contacts_early, 96 threads), and the write-back then
-// stores the impulses (o_contact_impulses).
+// solves the tile (o_rows_early, 96 threads), and the write-back then
+// stores the impulses (o_contact_impulses).  Prepared joint rows go the same
+// way: all words but the impulses and hinge axes the solve finalizes during
+// the solve, those after it (o_joint_impulses).
 
 // The contact words the solve writes: per point its normal and accumulated
 // impulses, then twist, friction and rolling impulses (08_contacts.inl:315-413).
@@ -1306,11 +1298,23 @@ B3X_HDI bool solver_word(int c) {
     return c == WTWI || c == WFI || c == WFI + 1 || (c >= WRI && c < WRI + 3);
 }
 
+// The words of a prepared B3Joint row that the solve finalizes (put in by
+// o_joint_patch): the linear impulse, then the angular impulse of a weld or
+// the hinge impulses and perpendicular axes of a revolute joint.
+B3X_HDI bool joint_solver_word(int v, bool weld) {
+    if (v >= VLI && v < VLI + 3) return true;
+    if (weld) return v >= VAI && v < VAI + 3;
+    return v == VPI || v == VPI + 1 || v == VSI || v == VMI || v == VLOI || v == VUPI || (v >= VPX && v < VPX + 3)
+        || (v >= VPY && v < VPY + 3);
+}
+
 // Run by the 96 threads of warps 1-3 (e = threadIdx.x - 32) during the
-// solve: the other contact words of every contact, then the derived words.
-// Reads only what the solve leaves unchanged (the contacts' other words, the
-// body constants, the record), writes only the columns' contact rows.
-B3X_HD void o_contacts_early(const Args& a, int tile, float* slot, int e) {
+// solve: the other contact words of every contact, the derived words, then
+// the joint rows but for the words the solve finalizes.  Reads only what the
+// solve leaves unchanged (the contacts' other words, the prepared joint rows,
+// the body constants, the record), writes only the columns' contact and
+// joint rows.
+B3X_HD void o_rows_early(const Args& a, int tile, float* slot, int e) {
     constexpr int kThreads = kCta - kLanes, kWarps = kThreads / kLanes;
     constexpr int kRun = (kCW + kWarps - 1) / kWarps;
     const size_t cw = a.L.contact_off / 4;
@@ -1338,6 +1342,44 @@ B3X_HD void o_contacts_early(const Args& a, int tile, float* slot, int e) {
 #endif
     for (int k = w0; k < n; k += kWarps)
         o_contact_fill(a, slot, l, ColRow{res_word(a, tile, cw + (size_t)k * NCW, l)});
+    // the prepared joint rows (collide phase), but for the words the solve
+    // finalizes; invalid joints are left as they were
+    const size_t jw = a.L.joint_off / 4;
+    const int nj = ldi(slot + a.SP.rec + l, RNJ);
+    for (int q = 0; q < nj; q++) {
+        const float* jo = item(slot + a.SP.joint, q, NJF) + l;
+        if (!ldi(jo, JOK)) continue;
+        const bool weld = ldi(jo, JTYPE) == B3_JOINT_WELD;
+        const float* ji = item(slot + a.SP.jimg, q, NVW) + l;
+        float* dst = res_word(a, tile, jw + (size_t)q * NVW, l);
+        for (int c = w0; c < NVW; c += kWarps)
+            if (!joint_solver_word(c, weld)) store_world(dst + (size_t)c * kLanes, COL(ji, c));
+    }
+}
+
+// After the solve: each valid joint's finalized words (o_joint_patch's).
+B3X_HD void o_joint_impulses(const Args& a, int tile, float* slot, OutShared& sh, int t) {
+    for (int j = t; j < sh.maxnj * kLanes; j += kCta) {
+        const int q = j >> 5, l = j & 31;
+        if (q >= sh.nj[l]) continue;
+        const float* jo = item(slot + a.SP.joint, q, NJF) + l;
+        if (!ldi(jo, JOK)) continue;
+        const size_t base = a.L.joint_off / 4 + (size_t)q * NVW;
+        auto put = [&](int v, int c) { store_world(res_word(a, tile, base + v, l), COL(jo, c)); };
+        for (int c = 0; c < 3; c++) put(VLI + c, JLI + c);
+        if (ldi(jo, JTYPE) == B3_JOINT_WELD) {
+            for (int c = 0; c < 3; c++) put(VAI + c, JAI + c);
+        } else {
+            put(VPI, JPI);
+            put(VPI + 1, JPI + 1);
+            put(VSI, JSI);
+            put(VMI, JMI);
+            put(VLOI, JLOI);
+            put(VUPI, JUPI);
+            for (int c = 0; c < 3; c++) put(VPX + c, JPX + c);
+            for (int c = 0; c < 3; c++) put(VPY + c, JPY + c);
+        }
+    }
 }
 
 // After the solve: each contact's impulses (point words up to its count).
@@ -1444,7 +1486,7 @@ B3X_HD void out_tile(X& x, const Args& a, int bt, OutShared& sh) {
     }
     if constexpr (kRes) {
         // resident columns: every other contact word went to the columns
-        // while the tile was solved (o_contacts_early); the solver's impulses
+        // while the tile was solved (o_rows_early); the solver's impulses
         // follow now
         if (!state_only) x.each([&](int t) { o_contact_impulses(a, tile, slot, sh, t); });
     } else {
@@ -1459,12 +1501,17 @@ B3X_HD void out_tile(X& x, const Args& a, int bt, OutShared& sh) {
         }
     }
     if (!state_only) {
-        const int K = out_items(sh.maxnj, NVW);
-        for (int q0 = 0; q0 < sh.maxnj; q0 += K) {
-            const int Kr = sh.maxnj - q0 < K ? sh.maxnj - q0 : K;
-            x.each([&](int t) { o_stage(item(slot + a.SP.jimg, q0, NVW), sh, Kr, NVW, NVW, t); });
-            x.each([&](int t) { o_joints(a, slot, sh, q0, Kr, t); });
-            x.each([&](int t) { o_joint_write<kRes>(a, tile, slot, sh, q0, Kr, t); });
+        if constexpr (kRes) {
+            // the joint rows went to the columns during the solve too
+            x.each([&](int t) { o_joint_impulses(a, tile, slot, sh, t); });
+        } else {
+            const int K = out_items(sh.maxnj, NVW);
+            for (int q0 = 0; q0 < sh.maxnj; q0 += K) {
+                const int Kr = sh.maxnj - q0 < K ? sh.maxnj - q0 : K;
+                x.each([&](int t) { o_stage(item(slot + a.SP.jimg, q0, NVW), sh, Kr, NVW, NVW, t); });
+                x.each([&](int t) { o_joints(a, slot, sh, q0, Kr, t); });
+                x.each([&](int t) { o_joint_write(a, tile, slot, sh, q0, Kr, t); });
+            }
         }
     }
     x.each([&](int t) { if (t < kLanes) o_header<kRes>(a, tile, slot, sh, t); });

@@ -138,8 +138,8 @@ __global__ void __launch_bounds__(kCta, 4) step_kernel(Args a) {
         const bool ok = solve_tile<kBody, kInterleave>(a, smem_raw);
         if (threadIdx.x == 0) solved = ok;
     } else if constexpr (kRes) {
-        // the other warps write the contact words the solve does not change
-        if (!(a.flags & kStepStateOnly)) o_contacts_early(a, a.tile0 + blockIdx.x, slot_of(a, blockIdx.x),
+        // the other warps write the contact and joint words the solve does not change
+        if (!(a.flags & kStepStateOnly)) o_rows_early(a, a.tile0 + blockIdx.x, slot_of(a, blockIdx.x),
                                                           threadIdx.x - kLanes);
     }
     __syncthreads();
