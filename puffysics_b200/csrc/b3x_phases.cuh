@@ -210,12 +210,6 @@ struct ColRow {
     float* p;
     B3X_HDI float& operator[](int f) const { return p[(size_t)f * kLanes]; }
 };
-// The warm-start words of a previous-step contact row in the resident
-// columns, in OLD field order.
-struct OldColRow {
-    const float* p;
-    B3X_HDI float operator[](int f) const { return p[(size_t)old_word(f) * kLanes]; }
-};
 
 template <bool kRes>
 B3X_HD void c_gather_old(const Args& a, int tile, CollideShared& sh, int l0, int G, int M, int dst, int t) {
