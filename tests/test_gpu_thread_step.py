@@ -138,3 +138,35 @@ def test_thread_step_argument_checks(built):
     assert engine.thread_step_gpu("stack", dev, 1 / 60, 4, count=0) == 0
     torch.cuda.synchronize()
     assert torch.equal(dev, ref)
+
+
+@pytest.mark.parametrize("name", ["hover", "stack", "chain"])
+def test_thread_scene_apply_equals_library_apply(name, built):
+    """The per-thread library's one-launch scene actions (the per-thread
+    bench leg's input) write the same bytes as the library's action
+    generator followed by b3x_batch_apply_gpu, and as the reference's apply
+    on the CPU; no launch and no change for a scene without actions."""
+    import torch
+    cfg = CONFIGS[name]
+    kind, idx, nv = cfg.action
+    n = 97
+    o = orc.Oracle(name, "port")
+    host = o.build(n, cfg.scene, 9)
+    a = torch.from_numpy(host.copy()).cuda()
+    b = a.clone()
+    vals = torch.zeros((n, max(nv, 1)), dtype=torch.float32, device="cuda")
+    for step in (1, 2):
+        assert engine.thread_scene_apply_gpu(name, a, cfg.scene, 9, 0, step) == 0
+        assert synth.actions_gpu(vals, n, cfg.scene, 9, 0, step) == nv
+        assert engine.batch_apply_gpu(b, kind, idx, vals, caps=cfg.caps) == 0
+        o.apply(host, cfg.scene, 9, 0, step)
+    torch.cuda.synchronize()
+    assert np.array_equal(a.cpu().numpy(), b.cpu().numpy())
+    assert np.array_equal(a.cpu().numpy(), host)
+    pile = CONFIGS["pile"]
+    assert pile.action[2] == 0
+    w = torch.from_numpy(orc.Oracle("pile", "port").build(33, pile.scene, 9)).cuda()
+    before = w.cpu().numpy()
+    assert engine.thread_scene_apply_gpu("pile", w, pile.scene, 9, 0, 1) == 0
+    torch.cuda.synchronize()
+    assert np.array_equal(w.cpu().numpy(), before)
